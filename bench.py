@@ -1,0 +1,408 @@
+#!/usr/bin/env python
+"""Benchmark of the ECC-INT4 KV-cache hot path on B200.
+
+Default workload (one "step"): one decode step of the single-layer decode
+benchmark -- batch 8, 32 query heads over 8 KV heads (GQA 4), head dim 128,
+65536-token compressed context that grows by one token per step:
+compress the step's new K and V token into the block pools, then fused decode
+attention of the step's queries over the whole context.  Inputs are seeded
+synthetic N(0,1) fp16 (no dataset is involved on this path).  The pools
+(2 x 8 x 8 x 65536 x 128 B = 1.07 GB) are far larger than the 126 MB L2, so
+no L2 flush is needed between steps.
+
+Also measured in the same run: compress throughput on the compress benchmark
+(8 KV heads x 131072 tokens, K and V, heavy-tailed fp16).
+
+N > 1 GPUs (torchrun): sequence-chunk sharding, weak scaling -- every rank
+holds its own 65536-token chunk of a context N x 65536 tokens long, computes
+split partials, all-gathers them over NCCL and merges them (LSE combine).
+
+``--impl reference`` times the reference algorithm's CPU implementation (the
+oracle port in oracle/, all host threads) on a bounded sample of the same
+workload and prints the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for p in (os.path.join(ROOT, "ecc-kv-cache_b200"), os.path.join(ROOT, "tests", "golden")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+METRIC = "ECC-INT4 decode-attn HBM GB/s (% peak); decode tok/s @64k ctx; compress tok/s"
+B, HQ, HKV, D, CTX = 8, 32, 8, 128, 65536
+BLOCK = 128
+COMPRESS_TOKENS = 131072
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        return float(pk["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu = gpu_id
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import custom_ecc_cuda as ops
+    import workloads
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        pg = dist.group.WORLD
+    K, W = args.steps, args.warmup
+    cap = CTX + W + K + 2 * (K + W) + 8
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+
+    # --- block pools filled by the compress kernel from seeded N(0,1) ---
+    kpool = torch.empty((B, HKV, cap, BLOCK), dtype=torch.uint8, device=dev)
+    vpool = torch.empty_like(kpool)
+    chunk = 8192
+    for t0 in range(0, CTX, chunk):
+        for pool in (kpool, vpool):
+            x = torch.randn((B, HKV, chunk, D), generator=gen, device=dev).half()
+            ops.compress_into(x, pool, pos=t0, rotate=True)
+    torch.cuda.synchronize()
+
+    n_steps = W + K
+    new_k = torch.randn((n_steps, B, HKV, 1, D), generator=gen, device=dev).half()
+    new_v = torch.randn((n_steps, B, HKV, 1, D), generator=gen, device=dev).half()
+    qs = torch.stack([workloads.make_queries(i, B, HQ, device=dev) for i in range(n_steps)])
+    out = torch.empty((B, HQ, 1, D), dtype=torch.float16, device=dev)
+    splits = ops.default_splits(B, HKV, CTX)
+    nspl = splits
+    stream = torch.cuda.current_stream(dev)
+
+    if world > 1:
+        import torch.distributed as dist
+        gm = torch.empty((world, B, HQ, nspl), dtype=torch.float32, device=dev)
+        gl = torch.empty_like(gm)
+        go = torch.empty((world, B, HQ, nspl, D), dtype=torch.float32, device=dev)
+
+    def step(i, seq_len, events=None):
+        # append the new token (sharded run: the last rank owns the newest chunk)
+        if world == 1 or rank == world - 1:
+            ops.compress_into(new_k[i], kpool, pos=seq_len - 1, rotate=True)
+            ops.compress_into(new_v[i], vpool, pos=seq_len - 1, rotate=True)
+        if events is not None:
+            events[0].record(stream)
+        if world == 1:
+            ops.decode_attention(qs[i], kpool, vpool, seq_len=seq_len, rotate_q=True, unrotate_out=True,
+                                 num_splits=splits, out=out)
+            if events is not None:
+                events[1].record(stream)
+        else:
+            pm, pl, po = ops.decode_partials(qs[i], kpool, vpool, seq_len=seq_len, num_splits=nspl, rotate_q=True)
+            if events is not None:
+                events[1].record(stream)
+            dist.all_gather_into_tensor(gm, pm, group=pg)
+            dist.all_gather_into_tensor(gl, pl, group=pg)
+            dist.all_gather_into_tensor(go, po, group=pg)
+            ops.lse_merge(gm.permute(1, 2, 0, 3).reshape(B, HQ, world * nspl).contiguous(),
+                          gl.permute(1, 2, 0, 3).reshape(B, HQ, world * nspl).contiguous(),
+                          go.permute(1, 2, 0, 3, 4).reshape(B, HQ, world * nspl, D).contiguous(),
+                          unrotate_out=True, out=out)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    seq = CTX
+    for i in range(W):
+        seq += 1
+        step(i, seq)
+    barrier()
+
+    # ---- timed region: K device-resident steps ----
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    seq0 = seq
+    try:
+        gpu_id = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        gpu_id = str(local)
+    with ClockSampler(gpu_id) as clk:
+        barrier()
+        start.record(stream)
+        for i in range(K):
+            seq += 1
+            step(W + i, seq, ev[i])
+        stop.record(stream)
+        barrier()
+    total_ms = start.elapsed_time(stop)
+    dec_ms = [a.elapsed_time(b) for a, b in ev]
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = t.item()
+
+    mean_ctx = seq0 + (K + 1) / 2.0
+    bytes_per_step = B * HKV * mean_ctx * 2 * BLOCK          # K + V blocks read, per rank
+    value = bytes_per_step * world * K / (total_ms / 1e3) / 1e9
+    tok_s = B * K / (total_ms / 1e3)
+    dec_avg_ms = sum(dec_ms) / len(dec_ms)
+    achieved = bytes_per_step / (dec_avg_ms / 1e3) / 1e9
+    peak, peak_kind = peaks()
+    clocks = clk.summary()
+
+    # ---- e2e: host buffers in, result out, every step (reference-facing API) ----
+    e2e = None
+    if world == 1:
+        hq = torch.empty((K, B, HQ, 1, D), dtype=torch.float16).pin_memory()
+        hk = torch.empty((K, B, HKV, 1, D), dtype=torch.float16).pin_memory()
+        hv = torch.empty_like(hk).pin_memory()
+        hq.copy_(qs[W:].cpu())
+        hk.copy_(new_k[W:].cpu())
+        hv.copy_(new_v[W:].cpu())
+        hout = torch.empty((K, B, HQ, 1, D), dtype=torch.float16).pin_memory()
+        dq = torch.empty((B, HQ, 1, D), dtype=torch.float16, device=dev)
+        dk = torch.empty((B, HKV, 1, D), dtype=torch.float16, device=dev)
+        dv = torch.empty_like(dk)
+        seq_e = seq
+        barrier()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record(stream)
+        for i in range(K):
+            seq_e += 1
+            dq.copy_(hq[i], non_blocking=True)
+            dk.copy_(hk[i], non_blocking=True)
+            dv.copy_(hv[i], non_blocking=True)
+            ops.compress_into(dk, kpool, pos=seq_e - 1, rotate=True)
+            ops.compress_into(dv, vpool, pos=seq_e - 1, rotate=True)
+            ops.decode_attention(dq, kpool, vpool, seq_len=seq_e, rotate_q=True, unrotate_out=True,
+                                 num_splits=splits, out=out)
+            hout[i].copy_(out, non_blocking=True)
+        e2.record(stream)
+        barrier()
+        e2e_ms = s2.elapsed_time(e2)
+        mean_ctx_e = seq + (K + 1) / 2.0
+        e2e = {"value": B * HKV * mean_ctx_e * 2 * BLOCK * K / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
+               "tok_s": B * K / (e2e_ms / 1e3), "ms_per_step": e2e_ms / K,
+               "h2d_bytes_per_step": (dq.numel() + dk.numel() + dv.numel()) * 2,
+               "d2h_bytes_per_step": out.numel() * 2}
+
+    # ---- compress throughput (8 KV heads x 131072 tokens, K and V) ----
+    comp = None
+    if world == 1 and not args.skip_compress:
+        del kpool, vpool
+        torch.cuda.empty_cache()
+        ck, cv = workloads.make_c2(seed=0, L=COMPRESS_TOKENS, device=dev)
+        cpool_k = torch.empty((1, HKV, COMPRESS_TOKENS, BLOCK), dtype=torch.uint8, device=dev)
+        cpool_v = torch.empty_like(cpool_k)
+        for _ in range(3):
+            ops.compress_into(ck, cpool_k, rotate=True)
+            ops.compress_into(cv, cpool_v, rotate=True)
+        reps = max(5, min(50, K))
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        barrier()
+        for a, b in evs:
+            a.record(stream)
+            ops.compress_into(ck, cpool_k, rotate=True)
+            ops.compress_into(cv, cpool_v, rotate=True)
+            b.record(stream)
+        barrier()
+        cms = [a.elapsed_time(b) for a, b in evs]
+        c_avg = sum(cms) / len(cms)
+        n_vec = 2 * HKV * COMPRESS_TOKENS
+        cbytes = n_vec * (2 * D + BLOCK)
+        c_gbs = cbytes / (c_avg / 1e3) / 1e9
+        comp = {"workload": "compress 8 KV heads x 131072 tokens, K and V, fp16 N(0,1) + Student-t(3) on 3% of "
+                            "channels -> 128-B blocks",
+                "tok_s": HKV * COMPRESS_TOKENS / (c_avg / 1e3), "vectors_per_s": n_vec / (c_avg / 1e3),
+                "ms_per_pass": c_avg, "gbs": c_gbs,
+                "roofline": {"bound": "hbm", "achieved": c_gbs, "peak": peak, "unit": "GB/s",
+                             "frac": c_gbs / peak, "traffic": None,
+                             "note": f"384 B per vector (256 B fp16 in + 128 B block out); peak {peak_kind}"}}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        cpu = cpu_baseline(args.cpu_tokens)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp32", "data": "synthetic",
+            "config": {"workload": f"decode step: B{B} Hq{HQ}/Hkv{HKV} D{D}, {CTX}-token compressed context "
+                                   f"per rank growing 1 token/step, append + fused decode",
+                       "batch": B, "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "context_per_rank": CTX,
+                       "parallelism": "seq-chunk" if world > 1 else "single", "num_splits": splits,
+                       "l2": "inputs 1.07 GB/rank > L2 (no flush needed)"},
+            "decode_tok_s": tok_s, "pct_peak": value / world / peak,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": args.traffic,
+                         "note": f"decode (split partials + merge) per launch: 256 B per (token, kv head), "
+                                 f"{B * HKV} (b, kv head) rows x mean {mean_ctx:.0f} tokens; peak {peak_kind}"},
+            "gpu_launches": K * (4 if (world == 1 or rank == world - 1) else 2),
+            "clocks": clocks, "e2e": e2e, "compress": comp, "cpu_baseline": cpu,
+        }
+        if comp:
+            line["compress_tok_s"] = comp["tok_s"]
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline / reference arm: the oracle port of the reference's CPU path
+# ---------------------------------------------------------------------------
+def _cpu_sample(tokens: int, seed: int = 0):
+    import numpy as np
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import ecc_oracle
+    g = torch.Generator().manual_seed(seed)
+    k = torch.randn(1, HKV, tokens, D, generator=g).half().numpy()
+    v = torch.randn(1, HKV, tokens, D, generator=g).half().numpy()
+    kb = ecc_oracle.compress(k.reshape(-1, D), rotate=True).reshape(1, HKV, tokens, BLOCK)
+    vb = ecc_oracle.compress(v.reshape(-1, D), rotate=True).reshape(1, HKV, tokens, BLOCK)
+    q = torch.randn(1, HQ, 1, D, generator=g).half().numpy()
+    return ecc_oracle, np, q, kb, vb
+
+
+def cpu_baseline(tokens: int):
+    """Oracle decode (cpu_reference_decode restated in C, GQA) on one batch
+    row x 8 KV heads x `tokens` tokens, all host threads."""
+    orc, np, q, kb, vb = _cpu_sample(tokens)
+    threads = len(os.sched_getaffinity(0))
+    orc.decode(q, kb[:, :, :64], vb[:, :, :64], hkv=HKV, seq_len=64, threads=threads)
+    t0 = time.perf_counter()
+    orc.decode(q, kb, vb, hkv=HKV, seq_len=tokens, rotate_q=True, unrotate_out=True, threads=threads)
+    dt = time.perf_counter() - t0
+    gbs = HKV * tokens * 2 * BLOCK / dt / 1e9
+    return {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"oracle decode (C port of cpu_reference_decode) of 1 batch row x {HQ} q heads / {HKV} kv "
+                      f"heads x {tokens} tokens ({dt:.2f} s)"}
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    orc, np, q, kb, vb = _cpu_sample(args.cpu_tokens)
+    threads = len(os.sched_getaffinity(0))
+    times = []
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        orc.decode(q, kb, vb, hkv=HKV, seq_len=args.cpu_tokens, rotate_q=True, unrotate_out=True, threads=threads)
+        dt = time.perf_counter() - t0
+        if i >= args.warmup:
+            times.append(dt)
+    total = sum(times)
+    gbs = HKV * args.cpu_tokens * 2 * BLOCK * len(times) / total / 1e9
+    line = {"impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / len(times),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+            "config": {"workload": f"decode step sample: 1 batch row x Hq{HQ}/Hkv{HKV} D{D} x {args.cpu_tokens} "
+                                   f"tokens of the {CTX}-token decode workload", "parallelism": "host threads"},
+            "decode_tok_s": 1.0 / (total / len(times)) * (args.cpu_tokens / CTX),
+            "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": f"oracle decode (C port of cpu_reference_decode) per step: 1 row x "
+                                       f"{args.cpu_tokens} tokens"},
+            "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-tokens", type=int, default=8192)
+    ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--skip-compress", action="store_true")
+    ap.add_argument("--traffic", type=float, default=None,
+                    help="ncu dram bytes per decode launch (from profiles/), reported in the roofline")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,621 @@
+// compress.cu -- WHT + Lloyd-Max INT4 + sign syndrome -> 128-byte blocks, the
+// standalone WHT op, block metadata readback, dequantisation and SoA packing.
+//
+// The compress kernel is bit-exact with the reference's CPU pipeline
+// custom_kv/ops_cpu.py:198 compress_cpu by construction:
+//   * WHT stages stride 1,2,...,64 in fp32 (ops_cpu.py:47-56), then the IEEE
+//     quotient by fp32(sqrt(128)) (ops_cpu.py:59) computed as
+//     q0 = x*r, rem = fma(-q0, c, x), q = fma(rem, r, q0) with r = RN(1/c):
+//     one remainder-corrected Newton step (Markstein, "IA-64 and elementary
+//     functions", 2000, ch. 8).  An exhaustive check over all fp32 x with
+//     2^-100 <= |x| < 2^100 shows it equals x/c (every nonzero WHT value of
+//     fp16 inputs lies in that range); x = -0 gives +0, and no output depends
+//     on the sign of a zero rotated element.
+//   * fp32 sums (mean, alpha) in the order torch's CPU sum kernel uses for a
+//     contiguous 128-float vector: acc[(j/8)%4][j%8] seeded with +0, blocks of
+//     32 added in order, t = ((acc0+acc1)+acc2)+acc3, then t0+...+t7.
+//   * std: fp64 sum of (double(x) - double(mean))^2 / 127, sqrt, rounded to
+//     fp32 (torch's std_var_all_cpu).  The fast path sums with FMA and a tree;
+//     when the fp64 result lies within 1e-12 (relative) of an fp32 rounding
+//     midpoint the vector is re-summed in element order with separate
+//     multiply and add, exactly like the CPU.
+//   * quantiser: argmin_k |(x-zero)/scale - C[k]| (ops_cpu.py:96-100) is taken
+//     from a cell table of the approximate quotient u = (x-zero)*RN(1/scale);
+//     whenever u lies within 4e-6 of a decision threshold the element is
+//     recomputed with the IEEE quotient and the full first-index argmin.
+//   * k_tilde = C[q]*scale + zero with two roundings, eps = x - k_tilde,
+//     bit = eps >= 0 (ops_cpu.py:104, :126).
+//
+// Thread layout: 4 lanes per vector, 8 vectors per warp.  Lane g of a vector
+// holds elements e = 32c + 8g + i (c, i in 0..3, 0..7): WHT strides 1,2,4 and
+// 32,64 stay in registers, strides 8,16 are lane exchanges, and each lane owns
+// torch's accumulator a = g for all four blocks c.
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+
+#include "ecc_common.cuh"
+
+namespace ecc {
+
+constexpr unsigned kFull = 0xffffffffu;
+constexpr int kCells = 192;       // u cells of width 1/8: cell = rint(8u + 96)
+constexpr int kReplicas = 8;      // one table copy per (lane % 8): conflict-free LDS.128
+constexpr float kBand = 4e-6f;    // exact-recompute band around each threshold
+constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: fma(u, 8, kMagic + 96) rounds 8u+96 to an integer
+constexpr int kCompressWarps = 8;
+constexpr int kVecPerWarp = 8;
+constexpr int kVecPerTile = kCompressWarps * kVecPerWarp;
+
+// Unsigned 32-bit division by a runtime constant d >= 1 (round-up method:
+// s = ceil(log2 d), m = floor(2^32 (2^s - d) / d) + 1, q = (umulhi(n,m) + n) >> s),
+// valid for every n < 2^32.
+struct FastDiv {
+    uint32_t d, m, s;
+};
+static inline FastDiv make_fastdiv(uint32_t d) {
+    FastDiv f;
+    f.d = d;
+    f.s = 0;
+    while ((1ull << f.s) < d) ++f.s;
+    f.m = (uint32_t)((((1ull << 32) * ((1ull << f.s) - d)) / d) + 1);
+    return f;
+}
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, FastDiv f) {
+    return (uint32_t)(((uint64_t)__umulhi(n, f.m) + n) >> f.s);
+}
+
+struct __align__(16) QEntry {
+    float thr;   // decision threshold inside this cell, +inf if none
+    float c_lo;  // centroid below the threshold
+    float c_hi;  // centroid above the threshold
+    int q_lo;    // code below the threshold
+};
+
+__device__ __forceinline__ int cell_of(float u) {
+    const float t = __fmaf_rn(u, 8.0f, kMagic + 96.0f);
+    return __float_as_int(t) - __float_as_int(kMagic);
+}
+
+// Thresholds m_j = (C[j-1] + C[j]) / 2, j = 1..15.  They are >= 2 cells apart
+// and >= 0.09 cells from every cell boundary, so a value within kBand of a
+// threshold always falls in that threshold's own cell.
+__device__ void build_qtable(QEntry *tab) {
+    for (int cell = threadIdx.x; cell < kCells; cell += blockDim.x) {
+        int below = 0, own = -1;
+#pragma unroll
+        for (int j = 1; j < 16; ++j) {
+            const float m = __fmul_rn(__fadd_rn(lm(j - 1), lm(j)), 0.5f);
+            const int cm = cell_of(m);
+            if (cm < cell) ++below;
+            if (cm == cell) own = j;
+        }
+        QEntry e;
+        if (own > 0) {
+            e.thr = __fmul_rn(__fadd_rn(lm(own - 1), lm(own)), 0.5f);
+            e.q_lo = own - 1;
+        } else {
+            e.thr = __int_as_float(0x7f800000);
+            e.q_lo = below;
+        }
+        e.c_lo = lm(e.q_lo);
+        e.c_hi = lm(e.q_lo < 15 ? e.q_lo + 1 : 15);
+#pragma unroll
+        for (int r = 0; r < kReplicas; ++r) tab[cell * kReplicas + r] = e;
+    }
+}
+
+// torch-order fp32 sum over the 128 elements of the vector held by the 4
+// lanes starting at `base` (see the file comment); every lane gets the sum.
+__device__ __forceinline__ float tsum_group(const float (&v)[4][8], int base) {
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        float acc = __fadd_rn(0.0f, v[0][i]);
+        acc = __fadd_rn(acc, v[1][i]);
+        acc = __fadd_rn(acc, v[2][i]);
+        acc = __fadd_rn(acc, v[3][i]);
+        const float a0 = __shfl_sync(kFull, acc, base + 0);
+        const float a1 = __shfl_sync(kFull, acc, base + 1);
+        const float a2 = __shfl_sync(kFull, acc, base + 2);
+        const float a3 = __shfl_sync(kFull, acc, base + 3);
+        const float t = __fadd_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3);
+        s = (i == 0) ? t : __fadd_rn(s, t);
+    }
+    return s;
+}
+
+// Normalised WHT of the vector held by a 4-lane group (layout above).
+__device__ __forceinline__ void wht_group(float (&v)[4][8], int g) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {  // stride 1
+            const float a = v[c][i], b = v[c][i + 1];
+            v[c][i] = __fadd_rn(a, b);
+            v[c][i + 1] = __fsub_rn(a, b);
+        }
+#pragma unroll
+        for (int i0 = 0; i0 < 8; i0 += 4) {  // stride 2
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const float a = v[c][i0 + j], b = v[c][i0 + j + 2];
+                v[c][i0 + j] = __fadd_rn(a, b);
+                v[c][i0 + j + 2] = __fsub_rn(a, b);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {  // stride 4
+            const float a = v[c][j], b = v[c][j + 4];
+            v[c][j] = __fadd_rn(a, b);
+            v[c][j + 4] = __fsub_rn(a, b);
+        }
+    }
+#pragma unroll
+    for (int s = 1; s <= 2; s <<= 1) {  // strides 8, 16: partner lane g ^ s
+        // lower index: mine + partner; upper index: partner - mine.  An FMA
+        // with multiplier +-1 rounds exactly like the add/sub.
+        const float sgn = (g & s) ? -1.0f : 1.0f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float p = __shfl_xor_sync(kFull, v[c][i], s);
+                v[c][i] = __fmaf_rn(sgn, v[c][i], p);
+            }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {  // stride 32 (c ^ 1) then 64 (c ^ 2)
+        float a = v[0][i], b = v[1][i];
+        v[0][i] = __fadd_rn(a, b);
+        v[1][i] = __fsub_rn(a, b);
+        a = v[2][i];
+        b = v[3][i];
+        v[2][i] = __fadd_rn(a, b);
+        v[3][i] = __fsub_rn(a, b);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        float a = v[0][i], b = v[2][i];
+        v[0][i] = __fadd_rn(a, b);
+        v[2][i] = __fsub_rn(a, b);
+        a = v[1][i];
+        b = v[3][i];
+        v[1][i] = __fadd_rn(a, b);
+        v[3][i] = __fsub_rn(a, b);
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float x = v[c][i];
+            const float q0 = __fmul_rn(x, kInvSqrt128);
+            const float rem = __fmaf_rn(-q0, kSqrt128, x);
+            v[c][i] = __fmaf_rn(rem, kInvSqrt128, q0);
+        }
+}
+
+__device__ __forceinline__ float2 h2_to_f2(uint32_t w) {
+    __half2 h = *reinterpret_cast<__half2 *>(&w);
+    return __half22float2(h);
+}
+
+// Exact first-index argmin of ops_cpu.py:99-100 for one element.
+__device__ __noinline__ int exact_code(float d, float scale) {
+    const float xn = __fdiv_rn(d, scale);
+    int best = 0;
+    float bd = fabsf(__fsub_rn(xn, lm(0)));
+#pragma unroll
+    for (int k = 1; k < 16; ++k) {
+        const float dk = fabsf(__fsub_rn(xn, lm(k)));
+        if (dk < bd) {
+            bd = dk;
+            best = k;
+        }
+    }
+    return best;
+}
+
+template <bool kRotate>
+__global__ void __launch_bounds__(kCompressWarps * 32)
+compress_kernel(const __half *__restrict__ x, int64_t xs_b, int64_t xs_h, int64_t xs_l,
+                uint8_t *__restrict__ blocks, int64_t bs_b, int64_t bs_h, FastDiv div_h, FastDiv div_l,
+                uint32_t n_vec) {
+    __shared__ QEntry tab[kCells * kReplicas];
+    __shared__ __align__(16) uint32_t stage[kCompressWarps][kVecPerWarp][20];
+    build_qtable(tab);
+    __syncthreads();
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane & 3, vsub = lane >> 2, base = lane & ~3;
+    uint32_t *st = stage[warp][vsub];
+    const uint32_t n_tiles = (n_vec + kVecPerTile - 1) / kVecPerTile;
+
+    for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+        const uint32_t vi = tile * kVecPerTile + warp * kVecPerWarp + vsub;
+        const bool valid = vi < n_vec;
+        const uint32_t row = fdiv(valid ? vi : 0u, div_l);
+        const int64_t l = (valid ? vi : 0u) - row * div_l.d;
+        const uint32_t bq = fdiv(row, div_h);
+        const int64_t b = bq, h = row - bq * div_h.d;
+
+        float v[4][8];
+        {
+            const __half *src = x + b * xs_b + h * xs_h + l * xs_l + 8 * g;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint4 raw = make_uint4(0, 0, 0, 0);
+                if (valid) raw = __ldcs(reinterpret_cast<const uint4 *>(src + 32 * c));
+                float2 f;
+                f = h2_to_f2(raw.x); v[c][0] = f.x; v[c][1] = f.y;
+                f = h2_to_f2(raw.y); v[c][2] = f.x; v[c][3] = f.y;
+                f = h2_to_f2(raw.z); v[c][4] = f.x; v[c][5] = f.y;
+                f = h2_to_f2(raw.w); v[c][6] = f.x; v[c][7] = f.y;
+            }
+        }
+        if (kRotate) wht_group(v, g);
+
+        // mean (zero point), ops_cpu.py:72
+        const float zero = __fmul_rn(tsum_group(v, base), 0.0078125f);
+
+        // unbiased std, ops_cpu.py:73
+        const double md = (double)zero;
+        double acc = 0.0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const double dx = (double)v[c][i] - md;
+                acc = fma(dx, dx, acc);
+            }
+        acc += __shfl_xor_sync(kFull, acc, 1);
+        acc += __shfl_xor_sync(kFull, acc, 2);
+        double sd = __dsqrt_rn(__ddiv_rn(acc, 127.0));
+        float s32 = __double2float_rn(sd);
+        {
+            const double lo = (double)s32;
+            const double nb = (double)(lo <= sd ? nextafterf(s32, INFINITY) : nextafterf(s32, 0.0f));
+            const double mid = 0.5 * (lo + nb);
+            const bool amb = fabs(sd - mid) <= 1e-12 * sd;
+            if (__any_sync(kFull, amb)) {  // rare: re-sum in element order
+                double ex = 0.0;
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+#pragma unroll 1
+                    for (int gg = 0; gg < 4; ++gg)
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const float xv = __shfl_sync(kFull, v[c][i], base + gg);
+                            const double dx = __dsub_rn((double)xv, md);
+                            ex = __dadd_rn(ex, __dmul_rn(dx, dx));
+                        }
+                if (amb) {
+                    sd = __dsqrt_rn(__ddiv_rn(ex, 127.0));
+                    s32 = __double2float_rn(sd);
+                }
+            }
+        }
+        const float scale = __double2float_rn(__dadd_rn((double)s32, 1e-8));
+        const float rs = __frcp_rn(scale);
+
+        // quantise, residual, syndrome
+        uint32_t codes[4] = {0u, 0u, 0u, 0u};
+        uint32_t bits = 0u;
+        const QEntry *mytab = tab + (lane & (kReplicas - 1));
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float xv = v[c][i];
+                const float d = __fsub_rn(xv, zero);
+                const float u = __fmul_rn(d, rs);
+                const unsigned cell = min((unsigned)cell_of(u), (unsigned)(kCells - 1));
+                const QEntry e = mytab[cell * kReplicas];
+                const bool hi = u > e.thr;
+                float cq = hi ? e.c_hi : e.c_lo;
+                int q = e.q_lo + (hi ? 1 : 0);
+                if (fabsf(__fsub_rn(u, e.thr)) < kBand) {
+                    q = exact_code(d, scale);
+                    cq = lm(0);
+#pragma unroll
+                    for (int k = 1; k < 16; ++k) cq = (q == k) ? lm(k) : cq;
+                }
+                const float kt = __fadd_rn(__fmul_rn(cq, scale), zero);
+                const float eps = __fsub_rn(xv, kt);
+                bits |= (eps >= 0.0f ? 1u : 0u) << (8 * c + i);
+                codes[c] |= (uint32_t)q << (4 * i);
+                v[c][i] = fabsf(eps);
+            }
+        const float alpha = __fmul_rn(tsum_group(v, base), 0.0078125f);
+
+        // stage: code word 4c+g and syndrome byte 4c+g of this vector
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            st[4 * c + g] = codes[c];
+            reinterpret_cast<uint8_t *>(st + 16)[4 * c + g] = (uint8_t)(bits >> (8 * c));
+        }
+        __syncwarp();
+        if (valid) {
+            uint8_t *dst = blocks + (b * bs_b + h * bs_h + l) * kBlockBytes;
+            const uint4 w0 = *reinterpret_cast<const uint4 *>(st + 4 * g);
+            uint4 w1;
+            if (g == 0) {
+                w1 = *reinterpret_cast<const uint4 *>(st + 16);
+            } else if (g == 1) {
+                const uint32_t hs = __half_as_ushort(__float2half_rn(scale));
+                const uint32_t hz = __half_as_ushort(__float2half_rn(zero));
+                const uint32_t ha = __half_as_ushort(__float2half_rn(alpha));
+                w1 = make_uint4(hs | (hz << 16), ha, 0u, 0u);
+            } else {
+                w1 = make_uint4(0u, 0u, 0u, 0u);
+            }
+            __stcs(reinterpret_cast<uint4 *>(dst + 16 * g), w0);
+            __stcs(reinterpret_cast<uint4 *>(dst + 64 + 16 * g), w1);
+        }
+        __syncwarp();
+    }
+}
+
+// ---- generic WHT (any power of two d <= 1024), one CTA per row ------------
+template <typename T>
+__device__ __forceinline__ float to_f(T v);
+template <>
+__device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+template <typename T>
+__device__ __forceinline__ T from_f(float v);
+template <>
+__device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
+
+template <typename T>
+__global__ void hadamard_generic_kernel(T *__restrict__ x, int d, float norm) {
+    extern __shared__ float sh[];
+    T *row = x + (int64_t)blockIdx.x * d;
+    for (int j = threadIdx.x; j < d; j += blockDim.x) sh[j] = to_f<T>(row[j]);
+    __syncthreads();
+    for (int s = 1; s < d; s <<= 1) {
+        for (int p = threadIdx.x; p < d / 2; p += blockDim.x) {
+            const int lo = (p / s) * 2 * s + (p % s);
+            const float a = sh[lo], b = sh[lo + s];
+            sh[lo] = __fadd_rn(a, b);
+            sh[lo + s] = __fsub_rn(a, b);
+        }
+        __syncthreads();
+    }
+    for (int j = threadIdx.x; j < d; j += blockDim.x) row[j] = from_f<T>(__fdiv_rn(sh[j], norm));
+}
+
+// D = 128 fast path: 4 lanes per row, same arithmetic as the compress prologue.
+template <typename T>
+__global__ void __launch_bounds__(256) hadamard128_kernel(T *__restrict__ x, int64_t n) {
+    const int lane = threadIdx.x & 31;
+    const int g = lane & 3;
+    const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 2;
+    const bool valid = r < n;
+    T *row = x + r * kD;
+    float v[4][8];
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[c][i] = valid ? to_f<T>(row[32 * c + 8 * g + i]) : 0.0f;
+    wht_group(v, g);
+    if (valid) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) row[32 * c + 8 * g + i] = from_f<T>(v[c][i]);
+    }
+}
+
+// ---- dequantise: blocks -> fp16 reconstruction ---------------------------
+__global__ void dequant_kernel(const uint8_t *__restrict__ blocks, __half *__restrict__ out, int64_t n) {
+    const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (r >= n) return;
+    const uint8_t *blk = blocks + r * kBlockBytes;
+    const uint32_t code16 = *reinterpret_cast<const uint16_t *>(blk + 2 * lane);
+    const uint32_t syn = (blk[kSynOff + lane / 2] >> (4 * (lane & 1))) & 0xfu;
+    const float sc = __half2float(*reinterpret_cast<const __half *>(blk + kScaleOff));
+    const float zr = __half2float(*reinterpret_cast<const __half *>(blk + kZeroOff));
+    const float al = __half2float(*reinterpret_cast<const __half *>(blk + kAlphaOff));
+    __half o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int q = (code16 >> (4 * j)) & 0xf;
+        float c = lm(0);
+#pragma unroll
+        for (int k = 1; k < 16; ++k) c = (q == k) ? lm(k) : c;
+        const float kt = __fadd_rn(__fmul_rn(c, sc), zr);
+        const float s = ((syn >> j) & 1u) ? al : -al;
+        o[j] = __float2half_rn(__fadd_rn(kt, s));
+    }
+    *reinterpret_cast<uint2 *>(out + r * kD + 4 * lane) = *reinterpret_cast<uint2 *>(o);
+}
+
+// ---- SoA trio -> blocks ---------------------------------------------------
+__global__ void pack_soa_kernel(const uint8_t *__restrict__ int4, int64_t i4s, const uint8_t *__restrict__ syn,
+                                int64_t sys, const uint8_t *__restrict__ meta, int64_t ms,
+                                uint8_t *__restrict__ blocks, int64_t n) {
+    const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (r >= n) return;
+    uint8_t *dst = blocks + r * kBlockBytes;
+    // lanes 0..15 copy 4 code bytes each, 16..19 syndrome, 20..21 meta, rest zero
+    uint32_t w = 0;
+    const int off = 4 * lane;
+    if (lane < 16) {
+        const uint8_t *s = int4 + r * i4s + off;
+        w = s[0] | (s[1] << 8) | (s[2] << 16) | ((uint32_t)s[3] << 24);
+    } else if (lane < 20) {
+        const uint8_t *s = syn + r * sys + (off - 64);
+        w = s[0] | (s[1] << 8) | (s[2] << 16) | ((uint32_t)s[3] << 24);
+    } else if (lane == 20) {
+        const uint8_t *s = meta + r * ms;
+        w = s[0] | (s[1] << 8) | (s[2] << 16) | ((uint32_t)s[3] << 24);
+    } else if (lane == 21) {
+        const uint8_t *s = meta + r * ms + 4;
+        w = s[0] | (s[1] << 8);
+    }
+    reinterpret_cast<uint32_t *>(dst)[lane] = w;
+}
+
+// ---- host side ------------------------------------------------------------
+struct DevInfo {
+    int sms = 0;
+    int compress_ctas_per_sm[2] = {0, 0};
+};
+
+static DevInfo g_dev[64];
+static std::mutex g_dev_mu;
+
+static int dev_info(DevInfo **out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ECC_ERR_DEVICE;
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    DevInfo &di = g_dev[dev];
+    if (di.sms == 0) {
+        int sms = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return ECC_ERR_DEVICE;
+        int a = 0, b = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&a, compress_kernel<false>, kCompressWarps * 32, 0);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, compress_kernel<true>, kCompressWarps * 32, 0);
+        di.compress_ctas_per_sm[0] = std::max(a, 1);
+        di.compress_ctas_per_sm[1] = std::max(b, 1);
+        di.sms = sms;
+    }
+    *out = &di;
+    return ECC_OK;
+}
+
+int launch_status() {
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? ECC_OK : ECC_ERR_LAUNCH;
+}
+
+int sm_count() {
+    DevInfo *di = nullptr;
+    const int rc = dev_info(&di);
+    return rc == ECC_OK ? di->sms : 148;
+}
+
+}  // namespace ecc
+
+using namespace ecc;
+
+static inline bool aligned(const void *p, size_t a) { return ((uintptr_t)p % a) == 0; }
+
+extern "C" int ecc_compress_strided(const void *x_f16, int64_t xs_b, int64_t xs_h, int64_t xs_l, void *blocks,
+                                    int64_t bs_b, int64_t bs_h, int B, int H, int64_t L, int rotate,
+                                    ecc_stream_t stream) {
+    if (B < 0 || H < 0 || L < 0) return ECC_ERR_SHAPE;
+    const int64_t n = (int64_t)B * H * L;
+    if (n == 0) return ECC_OK;
+    if (n >= (int64_t)0xffffff00ll) return ECC_ERR_SHAPE;  // 32-bit vector index
+    if (!x_f16 || !blocks) return ECC_ERR_NULL;
+    if (!aligned(x_f16, 16) || !aligned(blocks, 128)) return ECC_ERR_ALIGN;
+    if ((xs_b % 8) || (xs_h % 8) || (xs_l % 8)) return ECC_ERR_ALIGN;
+    DevInfo *di = nullptr;
+    int rc = dev_info(&di);
+    if (rc != ECC_OK) return rc;
+    const int64_t tiles = (n + kVecPerTile - 1) / kVecPerTile;
+    const int64_t grid = std::min<int64_t>(tiles, (int64_t)di->sms * di->compress_ctas_per_sm[rotate ? 1 : 0]);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (rotate)
+        compress_kernel<true><<<(unsigned)grid, kCompressWarps * 32, 0, s>>>(
+            reinterpret_cast<const __half *>(x_f16), xs_b, xs_h, xs_l, reinterpret_cast<uint8_t *>(blocks),
+            bs_b, bs_h, make_fastdiv((uint32_t)H), make_fastdiv((uint32_t)L), (uint32_t)n);
+    else
+        compress_kernel<false><<<(unsigned)grid, kCompressWarps * 32, 0, s>>>(
+            reinterpret_cast<const __half *>(x_f16), xs_b, xs_h, xs_l, reinterpret_cast<uint8_t *>(blocks),
+            bs_b, bs_h, make_fastdiv((uint32_t)H), make_fastdiv((uint32_t)L), (uint32_t)n);
+    return launch_status();
+}
+
+extern "C" int ecc_compress(const void *x_f16, void *blocks, int64_t n, int rotate, ecc_stream_t stream) {
+    if (n < 0) return ECC_ERR_SHAPE;
+    return ecc_compress_strided(x_f16, 0, 0, kD, blocks, 0, 0, 1, 1, n, rotate, stream);
+}
+
+template <typename T>
+static int hadamard_impl(void *x, int64_t n, int d, ecc_stream_t stream) {
+    if (n < 0 || d < 1 || d > 1024 || (d & (d - 1))) return ECC_ERR_SHAPE;
+    if (n == 0) return ECC_OK;
+    if (!x) return ECC_ERR_NULL;
+    if (!aligned(x, sizeof(T))) return ECC_ERR_ALIGN;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (d == kD) {
+        const int64_t threads = n * 4;
+        hadamard128_kernel<T><<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(reinterpret_cast<T *>(x), n);
+    } else {
+        if (n > 0x7fffffff) return ECC_ERR_SHAPE;
+        const float norm = (float)std::sqrt((double)d);
+        const int threads = std::min(std::max(d / 2, 32), 512);
+        hadamard_generic_kernel<T><<<(unsigned)n, threads, d * sizeof(float), s>>>(reinterpret_cast<T *>(x), d, norm);
+    }
+    return launch_status();
+}
+
+extern "C" int ecc_hadamard_f16(void *x, int64_t n, int d, ecc_stream_t stream) {
+    return hadamard_impl<__half>(x, n, d, stream);
+}
+
+extern "C" int ecc_hadamard_f32(void *x, int64_t n, int d, ecc_stream_t stream) {
+    return hadamard_impl<float>(x, n, d, stream);
+}
+
+extern "C" int ecc_get_block_metadata(const void *blocks, int64_t n_blocks, int64_t block_idx, float *host_out3,
+                                      ecc_stream_t stream) {
+    if (!blocks || !host_out3) return ECC_ERR_NULL;
+    if (block_idx < 0 || block_idx >= n_blocks) return ECC_ERR_SHAPE;
+    __half h[3];
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const uint8_t *src = reinterpret_cast<const uint8_t *>(blocks) + block_idx * kBlockBytes + kScaleOff;
+    if (cudaMemcpyAsync(h, src, sizeof(h), cudaMemcpyDeviceToHost, s) != cudaSuccess) return ECC_ERR_CUDA;
+    if (cudaStreamSynchronize(s) != cudaSuccess) return ECC_ERR_CUDA;
+    for (int i = 0; i < 3; ++i) host_out3[i] = __half2float(h[i]);
+    return ECC_OK;
+}
+
+extern "C" int ecc_dequantize(const void *blocks, void *out_f16, int64_t n, ecc_stream_t stream) {
+    if (n < 0) return ECC_ERR_SHAPE;
+    if (n == 0) return ECC_OK;
+    if (!blocks || !out_f16) return ECC_ERR_NULL;
+    if (!aligned(blocks, 16) || !aligned(out_f16, 8)) return ECC_ERR_ALIGN;
+    const int64_t threads = n * 32;
+    dequant_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        reinterpret_cast<const uint8_t *>(blocks), reinterpret_cast<__half *>(out_f16), n);
+    return launch_status();
+}
+
+extern "C" int ecc_pack_soa(const void *int4, int64_t int4_row_bytes, const void *syn, int64_t syn_row_bytes,
+                            const void *meta, int64_t meta_row_bytes, void *blocks, int64_t n, ecc_stream_t stream) {
+    if (n < 0) return ECC_ERR_SHAPE;
+    if (n == 0) return ECC_OK;
+    if (!int4 || !syn || !meta || !blocks) return ECC_ERR_NULL;
+    if (!aligned(blocks, 128)) return ECC_ERR_ALIGN;
+    const int64_t threads = n * 32;
+    pack_soa_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        reinterpret_cast<const uint8_t *>(int4), int4_row_bytes, reinterpret_cast<const uint8_t *>(syn),
+        syn_row_bytes, reinterpret_cast<const uint8_t *>(meta), meta_row_bytes, reinterpret_cast<uint8_t *>(blocks), n);
+    return launch_status();
+}
+
+extern "C" const char *ecc_strerror(int code) {
+    switch (code) {
+        case ECC_OK: return "ok";
+        case ECC_ERR_NULL: return "null pointer";
+        case ECC_ERR_SHAPE: return "size out of range";
+        case ECC_ERR_ALIGN: return "misaligned pointer or stride";
+        case ECC_ERR_GQA: return "query heads not a multiple of kv heads";
+        case ECC_ERR_WORKSPACE: return "workspace missing or too small";
+        case ECC_ERR_LAUNCH: return "kernel launch failed";
+        case ECC_ERR_CUDA: return "CUDA runtime call failed";
+        case ECC_ERR_DEVICE: return "no usable CUDA device";
+        default: return "unknown error";
+    }
+}
+
+extern "C" int ecc_version(void) { return 100; }

@@ -1,0 +1,327 @@
+// decode.cu -- fused ECC-INT4 decode attention over 128-byte blocks
+// (replaces the Triton _ecc_decode_kernel of custom_kv/fused_decode.py:30 and
+// the dequantise-then-SDPA step of custom_kv/patch.py:100) and the
+// log-sum-exp merge of split partials.
+//
+// Math per (batch b, query head h, token t), kv head = h / (Hq/Hkv):
+//   k_rec = C[q_t]*scale_t + zero_t + alpha_t * s_t         (fused_decode.py:229-241)
+//   score = sm_scale * <q_rot, k_rec>                         (:242)
+//   out   = sum_t softmax(score)_t * v_rec_t                  (:260-262)
+// evaluated as split-sequence (flash-decoding) partials: each CTA owns one
+// (b, kv head, split) and keeps its GQA query group resident; the merge
+// combines (m, l, o) of the splits.
+#include <algorithm>
+#include <cmath>
+
+#include "ecc_common.cuh"
+
+namespace ecc {
+
+int launch_status();
+int sm_count();
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr int kV1Warps = 4;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// In-place normalised WHT of sh[0..127] by 128 threads (ascending stride,
+// remainder-corrected quotient by fp32(sqrt(128)), as in compress.cu).
+__device__ __forceinline__ void smem_wht128(float *sh, int d) {
+    __syncthreads();
+    for (int s = 1; s < kD; s <<= 1) {
+        if ((d & s) == 0) {
+            const float a = sh[d], b = sh[d + s];
+            sh[d] = __fadd_rn(a, b);
+            sh[d + s] = __fsub_rn(a, b);
+        }
+        __syncthreads();
+    }
+    const float x = sh[d];
+    const float q0 = __fmul_rn(x, kInvSqrt128);
+    const float rem = __fmaf_rn(-q0, kSqrt128, x);
+    sh[d] = __fmaf_rn(rem, kInvSqrt128, q0);
+    __syncthreads();
+}
+
+// Dequantise the 4 elements 4*lane .. 4*lane+3 of a block:
+// (C[q]*scale + zero) + alpha*s in fp32.
+__device__ __forceinline__ void dequant4(const uint8_t *blk, int lane, float (&r)[4]) {
+    const uint32_t code16 = __ldg(reinterpret_cast<const uint16_t *>(blk + 2 * lane));
+    const uint32_t syn = (__ldg(blk + kSynOff + lane / 2) >> (4 * (lane & 1))) & 0xfu;
+    const uint2 meta = __ldg(reinterpret_cast<const uint2 *>(blk + kScaleOff));
+    const float sc = __half2float(__ushort_as_half((unsigned short)(meta.x & 0xffffu)));
+    const float zr = __half2float(__ushort_as_half((unsigned short)(meta.x >> 16)));
+    const float al = __half2float(__ushort_as_half((unsigned short)(meta.y & 0xffffu)));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int q = (code16 >> (4 * j)) & 0xf;
+        float c = lm(0);
+#pragma unroll
+        for (int k = 1; k < 16; ++k) c = (q == k) ? lm(k) : c;
+        const float kt = __fadd_rn(__fmul_rn(c, sc), zr);
+        r[j] = __fadd_rn(kt, ((syn >> j) & 1u) ? al : -al);
+    }
+}
+
+// Reference-path kernel: CUDA cores, lane = 4 dims, each warp streams every
+// fourth token of the split with an online softmax, warps merged at the end.
+template <int G>
+__global__ void __launch_bounds__(kV1Warps * 32)
+decode_v1_kernel(const __half *__restrict__ q, const uint8_t *__restrict__ kb, const uint8_t *__restrict__ vb,
+                 int64_t bs_b, int64_t bs_h, float *__restrict__ pm, float *__restrict__ pl,
+                 float *__restrict__ po, int Hq, int group, int n_hchunks, int64_t seq_len, int64_t chunk,
+                 int nsplit, float scale_log2, int flags) {
+    const int split = blockIdx.x;
+    const int kvh = blockIdx.y / n_hchunks, hc = blockIdx.y - kvh * n_hchunks;
+    const int b = blockIdx.z;
+    const int h0 = kvh * group + hc * G;
+    const int nh = min(G, group - hc * G);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+
+    __shared__ float sq[G][kD];
+    __shared__ float s_m[kV1Warps][G], s_l[kV1Warps][G];
+    __shared__ float s_o[kV1Warps][G][kD];
+
+    for (int idx = threadIdx.x; idx < G * kD; idx += blockDim.x) {
+        const int h = idx / kD, d = idx - h * kD;
+        sq[h][d] = (h < nh) ? __half2float(q[((int64_t)b * Hq + h0 + h) * kD + d]) : 0.0f;
+    }
+    static_assert(kV1Warps * 32 == kD, "one thread per dimension for the query WHT");
+    if (flags & ECC_DECODE_ROTATE_Q) {  // q_rot = fp16(WHT(q)), like patch.py:106
+        for (int h = 0; h < G; ++h) {
+            smem_wht128(sq[h], threadIdx.x);
+            sq[h][threadIdx.x] = __half2float(__float2half_rn(sq[h][threadIdx.x]));
+        }
+    }
+    __syncthreads();
+
+    float qr[G][4];
+#pragma unroll
+    for (int h = 0; h < G; ++h)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) qr[h][j] = sq[h][4 * lane + j];
+
+    float m[G], l[G], o[G][4];
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+        m[h] = -INFINITY;
+        l[h] = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[h][j] = 0.0f;
+    }
+
+    const int64_t t0 = (int64_t)split * chunk;
+    const int64_t t1 = min(seq_len, t0 + chunk);
+    const int64_t row_off = (int64_t)b * bs_b + (int64_t)kvh * bs_h;
+    for (int64_t t = t0 + warp; t < t1; t += kV1Warps) {
+        float kr[4], vr[4];
+        dequant4(kb + (row_off + t) * kBlockBytes, lane, kr);
+        dequant4(vb + (row_off + t) * kBlockBytes, lane, vr);
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+            float dot = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) dot = fmaf(qr[h][j], kr[j], dot);
+            const float s2 = warp_sum(dot) * scale_log2;
+            const float mn = fmaxf(m[h], s2);
+            const float corr = exp2f(m[h] - mn);
+            const float p = exp2f(s2 - mn);
+            l[h] = fmaf(l[h], corr, p);
+            m[h] = mn;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) o[h][j] = fmaf(o[h][j], corr, p * vr[j]);
+        }
+    }
+
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+        if (lane == 0) {
+            s_m[warp][h] = m[h];
+            s_l[warp][h] = l[h];
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) s_o[warp][h][4 * lane + j] = o[h][j];
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < nh * kD; idx += blockDim.x) {
+        const int h = idx / kD, d = idx - h * kD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kV1Warps; ++w) M = fmaxf(M, s_m[w][h]);
+        float L = 0.0f, O = 0.0f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < kV1Warps; ++w) {
+                const float e = exp2f(s_m[w][h] - M);
+                L = fmaf(s_l[w][h], e, L);
+                O = fmaf(s_o[w][h][d], e, O);
+            }
+        }
+        const int64_t prow = (int64_t)b * Hq + h0 + h;
+        const int64_t pi = prow * nsplit + split;
+        po[pi * kD + d] = O;
+        if (d == 0) {
+            pm[pi] = (M == -INFINITY) ? -INFINITY : M * kLn2;  // natural-log units
+            pl[pi] = L;
+        }
+    }
+}
+
+// Merge n partials per row; 128 threads = 128 dims.
+__global__ void __launch_bounds__(kD)
+lse_merge_kernel(const float *__restrict__ pm, const float *__restrict__ pl, const float *__restrict__ po,
+                 int n, __half *__restrict__ out, int flags) {
+    __shared__ float sh[kD];
+    const int64_t row = blockIdx.x;
+    const int d = threadIdx.x;
+    const float *m = pm + row * n;
+    const float *l = pl + row * n;
+    float M = -INFINITY;
+    for (int i = 0; i < n; ++i)
+        if (l[i] > 0.0f) M = fmaxf(M, m[i]);
+    float L = 0.0f, O = 0.0f;
+    if (M != -INFINITY) {
+        for (int i = 0; i < n; ++i) {
+            if (!(l[i] > 0.0f)) continue;
+            const float e = __expf(m[i] - M);
+            L = fmaf(l[i], e, L);
+            O = fmaf(po[(row * n + i) * kD + d], e, O);
+        }
+    }
+    float val = (L > 0.0f) ? O / L : 0.0f;
+    if (flags & ECC_DECODE_UNROTATE_OUT) {
+        sh[d] = val;
+        smem_wht128(sh, d);
+        val = sh[d];
+    }
+    out[row * kD + d] = __float2half_rn(val);
+}
+
+}  // namespace ecc
+
+using namespace ecc;
+
+static inline bool aligned(const void *p, size_t a) { return ((uintptr_t)p % a) == 0; }
+
+static inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+extern "C" int ecc_decode_default_splits(int B, int Hkv, int64_t seq_len) {
+    if (B <= 0 || Hkv <= 0 || seq_len <= 0) return 1;
+    const int64_t target = (int64_t)sm_count() * 8;  // CTAs to cover the SMs several times
+    int64_t ns = cdiv(target, (int64_t)B * Hkv);
+    ns = std::min<int64_t>(ns, cdiv(seq_len, 256));  // at least 256 tokens per split
+    return (int)std::max<int64_t>(1, std::min<int64_t>(ns, 4096));
+}
+
+static int effective_splits(int B, int Hkv, int64_t seq_len, int num_splits, int64_t *chunk_out) {
+    int ns = num_splits > 0 ? num_splits : ecc_decode_default_splits(B, Hkv, seq_len);
+    int64_t chunk = cdiv(std::max<int64_t>(seq_len, 1), ns);
+    chunk = cdiv(chunk, 64) * 64;  // whole 64-token tiles per split
+    ns = (int)std::max<int64_t>(1, cdiv(std::max<int64_t>(seq_len, 1), chunk));
+    if (chunk_out) *chunk_out = chunk;
+    return ns;
+}
+
+extern "C" size_t ecc_decode_workspace_size(int B, int Hq, int Hkv, int64_t seq_len, int num_splits) {
+    if (B <= 0 || Hq <= 0 || Hkv <= 0) return 0;
+    const int ns = effective_splits(B, Hkv, seq_len, num_splits, nullptr);
+    const size_t parts = (size_t)B * Hq * ns;
+    return parts * sizeof(float) * (2 + kD) + 256;
+}
+
+static int check_decode_args(const void *q, const void *kb, const void *vb, int B, int Hq, int Hkv,
+                             int64_t seq_len) {
+    if (!q || !kb || !vb) return ECC_ERR_NULL;
+    if (B <= 0 || Hq <= 0 || Hkv <= 0 || seq_len < 0) return ECC_ERR_SHAPE;
+    if (Hq % Hkv) return ECC_ERR_GQA;
+    if (!aligned(q, 16) || !aligned(kb, 16) || !aligned(vb, 16)) return ECC_ERR_ALIGN;
+    return ECC_OK;
+}
+
+template <int G>
+static void launch_v1(const void *q, const void *kb, const void *vb, int64_t bs_b, int64_t bs_h, float *pm,
+                      float *pl, float *po, int B, int Hq, int Hkv, int64_t seq_len, int64_t chunk, int ns,
+                      float scale_log2, int flags, cudaStream_t s) {
+    const int group = Hq / Hkv;
+    const int n_hchunks = (group + G - 1) / G;
+    dim3 grid(ns, Hkv * n_hchunks, B);
+    decode_v1_kernel<G><<<grid, kV1Warps * 32, 0, s>>>(
+        reinterpret_cast<const __half *>(q), reinterpret_cast<const uint8_t *>(kb),
+        reinterpret_cast<const uint8_t *>(vb), bs_b, bs_h, pm, pl, po, Hq, group, n_hchunks, seq_len, chunk, ns,
+        scale_log2, flags);
+}
+
+static int run_partials(const void *q, const void *kb, const void *vb, int64_t bs_b, int64_t bs_h, float *pm,
+                        float *pl, float *po, int B, int Hq, int Hkv, int64_t seq_len, int64_t chunk, int ns,
+                        float sm_scale, int flags, cudaStream_t s) {
+    if (!(sm_scale > 0.0f)) sm_scale = 1.0f / std::sqrt((float)kD);
+    const float scale_log2 = sm_scale * kLog2e;
+    const int group = Hq / Hkv;
+    if (group == 1)
+        launch_v1<1>(q, kb, vb, bs_b, bs_h, pm, pl, po, B, Hq, Hkv, seq_len, chunk, ns, scale_log2, flags, s);
+    else if (group == 2)
+        launch_v1<2>(q, kb, vb, bs_b, bs_h, pm, pl, po, B, Hq, Hkv, seq_len, chunk, ns, scale_log2, flags, s);
+    else if (group <= 4)
+        launch_v1<4>(q, kb, vb, bs_b, bs_h, pm, pl, po, B, Hq, Hkv, seq_len, chunk, ns, scale_log2, flags, s);
+    else
+        launch_v1<8>(q, kb, vb, bs_b, bs_h, pm, pl, po, B, Hq, Hkv, seq_len, chunk, ns, scale_log2, flags, s);
+    return launch_status();
+}
+
+extern "C" int ecc_decode_partials(const void *q_f16, const void *k_blocks, const void *v_blocks, int64_t bs_b,
+                                   int64_t bs_h, float *part_m, float *part_l, float *part_o, int B, int Hq,
+                                   int Hkv, int64_t seq_len, float sm_scale, int flags, int num_splits,
+                                   ecc_stream_t stream) {
+    int rc = check_decode_args(q_f16, k_blocks, v_blocks, B, Hq, Hkv, seq_len);
+    if (rc != ECC_OK) return rc;
+    if (!part_m || !part_l || !part_o) return ECC_ERR_NULL;
+    if (num_splits <= 0) return ECC_ERR_SHAPE;  // the caller sizes the partial arrays
+    int64_t chunk = 0;
+    const int ns = effective_splits(B, Hkv, seq_len, num_splits, &chunk);
+    if (ns != num_splits) {
+        // a split would be empty of whole tiles; keep the caller's count and
+        // let trailing splits come out empty (l = 0)
+        chunk = cdiv(cdiv(std::max<int64_t>(seq_len, 1), num_splits), 64) * 64;
+    }
+    return run_partials(q_f16, k_blocks, v_blocks, bs_b, bs_h, part_m, part_l, part_o, B, Hq, Hkv, seq_len, chunk,
+                        num_splits, sm_scale, flags & ECC_DECODE_ROTATE_Q, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ecc_lse_merge(const float *part_m, const float *part_l, const float *part_o, int64_t rows, int n,
+                             void *out_f16, int flags, ecc_stream_t stream) {
+    if (rows < 0 || n <= 0) return ECC_ERR_SHAPE;
+    if (rows == 0) return ECC_OK;
+    if (!part_m || !part_l || !part_o || !out_f16) return ECC_ERR_NULL;
+    if (rows > 0x7fffffff) return ECC_ERR_SHAPE;
+    lse_merge_kernel<<<(unsigned)rows, kD, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        part_m, part_l, part_o, n, reinterpret_cast<__half *>(out_f16), flags);
+    return launch_status();
+}
+
+extern "C" int ecc_decode(const void *q_f16, const void *k_blocks, const void *v_blocks, int64_t bs_b, int64_t bs_h,
+                          void *out_f16, void *workspace, size_t workspace_bytes, int B, int Hq, int Hkv,
+                          int64_t seq_len, float sm_scale, int flags, int num_splits, ecc_stream_t stream) {
+    int rc = check_decode_args(q_f16, k_blocks, v_blocks, B, Hq, Hkv, seq_len);
+    if (rc != ECC_OK) return rc;
+    if (!out_f16) return ECC_ERR_NULL;
+    const size_t need = ecc_decode_workspace_size(B, Hq, Hkv, seq_len, num_splits);
+    if (!workspace || workspace_bytes < need) return ECC_ERR_WORKSPACE;
+    int64_t chunk = 0;
+    const int ns = effective_splits(B, Hkv, seq_len, num_splits, &chunk);
+    const size_t parts = (size_t)B * Hq * ns;
+    uintptr_t base = (reinterpret_cast<uintptr_t>(workspace) + 255) & ~(uintptr_t)255;
+    float *po = reinterpret_cast<float *>(base);
+    float *pm = po + parts * kD;
+    float *pl = pm + parts;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    rc = run_partials(q_f16, k_blocks, v_blocks, bs_b, bs_h, pm, pl, po, B, Hq, Hkv, seq_len, chunk, ns, sm_scale,
+                      flags & ECC_DECODE_ROTATE_Q, s);
+    if (rc != ECC_OK) return rc;
+    return ecc_lse_merge(pm, pl, po, (int64_t)B * Hq, ns, out_f16, flags & ECC_DECODE_UNROTATE_OUT, stream);
+}

@@ -1,0 +1,391 @@
+"""custom_ecc_cuda -- the reference's CUDA op module (csrc/ecc_ops.cpp:119-138)
+re-implemented over the C ABI of libeccb200.so (sm_100a).
+
+Same op names, argument meaning and error behaviour as the reference's
+pybind module:
+
+* ``hadamard_rotate(x)``                 csrc/ecc_ops.cpp:32
+* ``compress_and_store(x_rot, cache_raw)`` csrc/ecc_ops.cpp:68
+* ``get_block_metadata(cache_raw, idx)``  csrc/ecc_ops.cpp:98
+
+plus the ops the rest of this package is built on (fused rotate+compress into a
+strided block pool, fused decode attention, split partials and their merge,
+dequantisation, SoA packing).  Every op runs the CUDA library; there is no CPU
+path, and CPU tensors raise ``RuntimeError`` like the reference's
+``TORCH_CHECK(x.is_cuda())``.  Launches go to torch's current stream.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+import threading
+
+import torch
+
+__all__ = [
+    "hadamard_rotate", "compress_and_store", "get_block_metadata", "rotate_and_compress",
+    "compress_into", "decode_attention", "decode_partials", "lse_merge", "dequantize", "pack_soa",
+    "decode_workspace_size", "default_splits", "library_path", "EccError",
+]
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_NAME = "libeccb200.so"
+library_path = os.path.join(_HERE, _LIB_NAME)
+
+ROTATE_Q = 1
+UNROTATE_OUT = 2
+D = 128
+BLOCK_BYTES = 128
+
+
+class EccError(RuntimeError):
+    """A negative status from libeccb200.so."""
+
+
+def _load():
+    if not os.path.exists(library_path):
+        raise ImportError(
+            f"custom_ecc_cuda: {library_path} is missing; build it with "
+            f"`make -C {os.path.join(os.path.dirname(_HERE), 'csrc')}` (sm_100a)")
+    lib = ctypes.CDLL(library_path)
+    p, i64, i32, f32, sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
+    sig = {
+        "ecc_strerror": ([i32], ctypes.c_char_p),
+        "ecc_version": ([], i32),
+        "ecc_hadamard_f16": ([p, i64, i32, p], i32),
+        "ecc_hadamard_f32": ([p, i64, i32, p], i32),
+        "ecc_compress": ([p, p, i64, i32, p], i32),
+        "ecc_compress_strided": ([p, i64, i64, i64, p, i64, i64, i32, i32, i64, i32, p], i32),
+        "ecc_get_block_metadata": ([p, i64, i64, p, p], i32),
+        "ecc_dequantize": ([p, p, i64, p], i32),
+        "ecc_pack_soa": ([p, i64, p, i64, p, i64, p, i64, p], i32),
+        "ecc_decode": ([p, p, p, i64, i64, p, p, sz, i32, i32, i32, i64, f32, i32, i32, p], i32),
+        "ecc_decode_workspace_size": ([i32, i32, i32, i64, i32], sz),
+        "ecc_decode_default_splits": ([i32, i32, i64], i32),
+        "ecc_decode_partials": ([p, p, p, i64, i64, p, p, p, i32, i32, i32, i64, f32, i32, i32, p], i32),
+        "ecc_lse_merge": ([p, p, p, i64, i32, p, i32, p], i32),
+    }
+    for name, (args, res) in sig.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = res
+    return lib
+
+
+_lib = _load()
+_ws_lock = threading.Lock()
+_ws_cache: dict = {}
+
+
+def _check(rc: int, what: str):
+    if rc != 0:
+        msg = _lib.ecc_strerror(rc).decode()
+        raise EccError(f"{what}: {msg} (code {rc})")
+
+
+def _stream(t: torch.Tensor):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _ptr(t: torch.Tensor):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _require_cuda(t: torch.Tensor, name: str):
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor")
+
+
+def _require_input(t: torch.Tensor, name: str):
+    _require_cuda(t, name)
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+
+
+# ---------------------------------------------------------------------------
+# reference op surface (csrc/ecc_ops.cpp)
+# ---------------------------------------------------------------------------
+def hadamard_rotate(x: torch.Tensor) -> torch.Tensor:
+    """In-place normalised WHT of each row of ``x`` [N, D] (fp16/fp32, D a
+    power of two <= 1024); returns ``x``.  Arithmetic of
+    custom_kv/ops_cpu.py:29 hadamard_rotate_cpu (fp32 butterfly, stride
+    1..D/2, division by fp32(sqrt(D))), rounded to fp16 for fp16 input."""
+    _require_input(x, "x")
+    if x.dim() != 2:
+        raise RuntimeError("Expected 2D tensor [N, D]")
+    n, d = x.shape
+    if d <= 0 or (d & (d - 1)) != 0:
+        raise RuntimeError("D must be a power of 2")
+    if d > 1024:
+        raise RuntimeError("D must be <= 1024 (shared memory limit)")
+    with torch.cuda.device(x.device):
+        if x.dtype == torch.float16:
+            rc = _lib.ecc_hadamard_f16(_ptr(x), n, d, _stream(x))
+        elif x.dtype == torch.float32:
+            rc = _lib.ecc_hadamard_f32(_ptr(x), n, d, _stream(x))
+        else:
+            raise RuntimeError("hadamard_rotate only supports float16 and float32")
+    _check(rc, "hadamard_rotate")
+    return x
+
+
+def compress_and_store(x_rot: torch.Tensor, cache_raw: torch.Tensor) -> None:
+    """Compress already-rotated fp16 vectors ``x_rot`` [N, 128] into the
+    128-byte block pool ``cache_raw`` [N', 128] uint8 (N' >= N), row i into
+    block i.  Bit-exact with the reference's CPU compress of the same input."""
+    _require_input(x_rot, "x_rot")
+    _require_input(cache_raw, "cache_raw")
+    if x_rot.dtype != torch.float16:
+        raise RuntimeError("x_rot must be float16")
+    if cache_raw.dtype != torch.uint8:
+        raise RuntimeError("cache_raw must be uint8")
+    if x_rot.dim() != 2 or x_rot.shape[1] != D:
+        raise RuntimeError("Only D=128 supported (hardcoded kernel)")
+    if cache_raw.dim() != 2 or cache_raw.shape[1] != BLOCK_BYTES:
+        raise RuntimeError("Cache must be [N, 128] bytes")
+    if cache_raw.shape[0] < x_rot.shape[0]:
+        raise RuntimeError("cache_raw has fewer blocks than x_rot has rows")
+    if x_rot.device != cache_raw.device:
+        raise RuntimeError("x_rot and cache_raw must be on the same device")
+    with torch.cuda.device(x_rot.device):
+        rc = _lib.ecc_compress(_ptr(x_rot), _ptr(cache_raw), x_rot.shape[0], 0, _stream(x_rot))
+    _check(rc, "compress_and_store")
+
+
+def get_block_metadata(cache_raw: torch.Tensor, block_idx: int) -> torch.Tensor:
+    """(scale, zero_point, alpha) of block ``block_idx`` as a CPU float32[3]
+    tensor.  Synchronous, like the reference's debug accessor."""
+    _require_input(cache_raw, "cache_raw")
+    n_blocks = cache_raw.numel() // BLOCK_BYTES
+    out = torch.empty(3, dtype=torch.float32)
+    with torch.cuda.device(cache_raw.device):
+        rc = _lib.ecc_get_block_metadata(_ptr(cache_raw), n_blocks, int(block_idx),
+                                         ctypes.c_void_p(out.data_ptr()), _stream(cache_raw))
+    _check(rc, "get_block_metadata")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# pool ops used by custom_kv
+# ---------------------------------------------------------------------------
+def _pool_strides(pool: torch.Tensor, name: str):
+    """A block pool is a uint8 tensor [..., B, H, L, 128] whose last two dims
+    are contiguous blocks; returns (bs_b, bs_h) in blocks."""
+    _require_cuda(pool, name)
+    if pool.dtype != torch.uint8 or pool.dim() < 4 or pool.shape[-1] != BLOCK_BYTES:
+        raise RuntimeError(f"{name} must be a uint8 block pool [B, H, L, 128]")
+    if pool.stride(-1) != 1 or pool.stride(-2) != BLOCK_BYTES:
+        raise RuntimeError(f"{name}: blocks along L must be contiguous 128-byte rows")
+    sb, sh = pool.stride(-4), pool.stride(-3)
+    if sb % BLOCK_BYTES or sh % BLOCK_BYTES:
+        raise RuntimeError(f"{name}: batch/head strides must be whole blocks")
+    return sb // BLOCK_BYTES, sh // BLOCK_BYTES
+
+
+def compress_into(x: torch.Tensor, pool: torch.Tensor, pos: int = 0, rotate: bool = True) -> None:
+    """Compress ``x`` [B, H, L, 128] fp16 (any strides with a contiguous last
+    dim) into ``pool`` [B, H, Lcap, 128] at token positions pos .. pos+L-1.
+    ``rotate`` applies the WHT first (custom_kv/ops_cpu.py:198)."""
+    _require_cuda(x, "x")
+    if x.dtype != torch.float16:
+        raise RuntimeError("x must be float16")
+    if x.dim() != 4 or x.shape[-1] != D:
+        raise RuntimeError("Only D=128 supported (hardcoded kernel)")
+    if x.stride(-1) != 1:
+        raise RuntimeError("x must have a contiguous last dimension")
+    bs_b, bs_h = _pool_strides(pool, "pool")
+    B, H, L, _ = x.shape
+    if pool.shape[-4] != B or pool.shape[-3] != H:
+        raise RuntimeError("pool batch/head dims do not match x")
+    if pos < 0 or pos + L > pool.shape[-2]:
+        raise RuntimeError(f"positions {pos}..{pos + L} exceed the pool capacity {pool.shape[-2]}")
+    if x.device != pool.device:
+        raise RuntimeError("x and pool must be on the same device")
+    dst = pool[..., pos:, :] if pos else pool
+    with torch.cuda.device(x.device):
+        rc = _lib.ecc_compress_strided(_ptr(x), x.stride(0), x.stride(1), x.stride(2), _ptr(dst), bs_b, bs_h,
+                                       B, H, L, int(bool(rotate)), _stream(x))
+    _check(rc, "compress_into")
+
+
+def rotate_and_compress(x: torch.Tensor, blocks: torch.Tensor | None = None) -> torch.Tensor:
+    """WHT + compress of contiguous rows ``x`` [N, 128] fp16 -> blocks [N, 128] u8."""
+    _require_input(x, "x")
+    if x.dtype != torch.float16 or x.dim() != 2 or x.shape[1] != D:
+        raise RuntimeError("x must be float16 [N, 128]")
+    if blocks is None:
+        blocks = torch.empty((x.shape[0], BLOCK_BYTES), dtype=torch.uint8, device=x.device)
+    _require_input(blocks, "blocks")
+    with torch.cuda.device(x.device):
+        rc = _lib.ecc_compress(_ptr(x), _ptr(blocks), x.shape[0], 1, _stream(x))
+    _check(rc, "rotate_and_compress")
+    return blocks
+
+
+def dequantize(blocks: torch.Tensor) -> torch.Tensor:
+    """[..., 128] u8 contiguous blocks -> [..., 128] fp16 reconstructions
+    (C[q]*scale + zero) + alpha*s (custom_kv/fused_decode.py:229-241)."""
+    _require_input(blocks, "blocks")
+    n = blocks.numel() // BLOCK_BYTES
+    out = torch.empty(blocks.shape[:-1] + (D,), dtype=torch.float16, device=blocks.device)
+    with torch.cuda.device(blocks.device):
+        rc = _lib.ecc_dequantize(_ptr(blocks), _ptr(out), n, _stream(blocks))
+    _check(rc, "dequantize")
+    return out
+
+
+def pack_soa(int4: torch.Tensor, syn: torch.Tensor, meta: torch.Tensor) -> torch.Tensor:
+    """Reference SoA trio (int4 [..., 64] u8, syn [..., 16] u8, meta [..., 3]
+    fp16, custom_kv/cache.py:79-84) -> contiguous blocks [..., 128] u8."""
+    for t, nme in ((int4, "int4"), (syn, "syn"), (meta, "meta")):
+        _require_cuda(t, nme)
+    lead = int4.shape[:-1]
+    if int4.shape[-1] != 64 or syn.shape[-1] != 16 or meta.shape[-1] != 3 or syn.shape[:-1] != lead \
+            or meta.shape[:-1] != lead:
+        raise RuntimeError("expected int4 [..., 64], syn [..., 16], meta [..., 3]")
+    if int4.dtype != torch.uint8 or syn.dtype != torch.uint8 or meta.dtype != torch.float16:
+        raise RuntimeError("expected uint8 int4/syn and float16 meta")
+    i4 = int4.reshape(-1, 64)
+    sy = syn.reshape(-1, 16)
+    me = meta.reshape(-1, 3)
+    for t, w in ((i4, 1), (sy, 1), (me, 1)):
+        if t.stride(-1) != w:
+            raise RuntimeError("SoA tensors need a contiguous last dim")
+    n = i4.shape[0]
+    out = torch.empty(lead + (BLOCK_BYTES,), dtype=torch.uint8, device=int4.device)
+    with torch.cuda.device(int4.device):
+        rc = _lib.ecc_pack_soa(_ptr(i4), i4.stride(0), _ptr(sy), sy.stride(0), _ptr(me), me.stride(0) * 2,
+                               _ptr(out), n, _stream(int4))
+    _check(rc, "pack_soa")
+    return out
+
+
+def default_splits(B: int, hkv: int, seq_len: int) -> int:
+    return int(_lib.ecc_decode_default_splits(B, hkv, seq_len))
+
+
+def decode_workspace_size(B: int, hq: int, hkv: int, seq_len: int, num_splits: int = 0) -> int:
+    return int(_lib.ecc_decode_workspace_size(B, hq, hkv, seq_len, num_splits))
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """A grow-only per-device workspace reused across calls (stream-ordered:
+    calls on one stream never overlap)."""
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+    with _ws_lock:
+        ws = _ws_cache.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            _ws_cache[key] = ws
+    return ws
+
+
+def _query(q: torch.Tensor):
+    _require_cuda(q, "query")
+    if q.dtype != torch.float16:
+        raise RuntimeError("query must be float16")
+    if q.dim() == 4:
+        if q.shape[2] != 1:
+            raise RuntimeError("decode attention takes one query token ([B, H, 1, D])")
+        q3 = q[:, :, 0, :]
+    elif q.dim() == 3:
+        q3 = q
+    else:
+        raise RuntimeError("query must be [B, H, 1, D] or [B, H, D]")
+    if q3.shape[-1] != D:
+        raise RuntimeError(f"Only D=128 supported, got {q3.shape[-1]}")
+    return q3.contiguous()
+
+
+def decode_attention(query: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, seq_len: int,
+                     sm_scale: float | None = None, rotate_q: bool = False, unrotate_out: bool = False,
+                     num_splits: int = 0, out: torch.Tensor | None = None,
+                     workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """One decode step of GQA attention over block pools [B, Hkv, Lcap, 128].
+
+    query [B, Hq, 1, 128] (or [B, Hq, 128]) fp16 -> [B, Hq, 1, 128] fp16.
+    Query head h reads kv head h // (Hq // Hkv).  ``sm_scale`` defaults to
+    1/sqrt(128) (custom_kv/fused_decode.py:57)."""
+    q3 = _query(query)
+    kbs = _pool_strides(k_pool, "k_pool")
+    vbs = _pool_strides(v_pool, "v_pool")
+    if kbs != vbs or k_pool.shape != v_pool.shape:
+        raise RuntimeError("k_pool and v_pool must have the same shape and strides")
+    B, hq, _ = q3.shape
+    hkv = k_pool.shape[-3]
+    if k_pool.shape[-4] != B:
+        raise RuntimeError("pool batch does not match the query")
+    if hq % hkv:
+        raise RuntimeError(f"query heads ({hq}) must be a multiple of kv heads ({hkv})")
+    if seq_len < 0 or seq_len > k_pool.shape[-2]:
+        raise RuntimeError(f"seq_len {seq_len} exceeds the pool capacity {k_pool.shape[-2]}")
+    if out is None:
+        out = torch.empty((B, hq, 1, D), dtype=torch.float16, device=q3.device)
+    elif not out.is_contiguous() or out.dtype != torch.float16 or out.numel() != B * hq * D:
+        raise RuntimeError("out must be a contiguous float16 tensor of B*Hq*128 elements")
+    flags = (ROTATE_Q if rotate_q else 0) | (UNROTATE_OUT if unrotate_out else 0)
+    scale = float(sm_scale) if sm_scale is not None else 0.0
+    need = decode_workspace_size(B, hq, hkv, seq_len, num_splits)
+    with torch.cuda.device(q3.device):
+        ws = workspace if workspace is not None else _workspace(q3.device, need)
+        if ws.numel() < need:
+            raise RuntimeError(f"workspace too small: {ws.numel()} < {need} bytes")
+        rc = _lib.ecc_decode(_ptr(q3), _ptr(k_pool), _ptr(v_pool), kbs[0], kbs[1], _ptr(out), _ptr(ws),
+                             ws.numel(), B, hq, hkv, int(seq_len), scale, flags, int(num_splits), _stream(q3))
+    _check(rc, "decode_attention")
+    return out
+
+
+def decode_partials(query: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, seq_len: int,
+                    num_splits: int, sm_scale: float | None = None, rotate_q: bool = False):
+    """Split partials (m, l, o) of one decode step over token positions
+    [0, seq_len) of the pools: m, l [B, Hq, num_splits] fp32 (m in natural-log
+    units), o [B, Hq, num_splits, 128] fp32 unnormalised."""
+    q3 = _query(query)
+    kbs = _pool_strides(k_pool, "k_pool")
+    vbs = _pool_strides(v_pool, "v_pool")
+    if kbs != vbs:
+        raise RuntimeError("k_pool and v_pool must have the same strides")
+    B, hq, _ = q3.shape
+    hkv = k_pool.shape[-3]
+    if num_splits <= 0:
+        raise RuntimeError("num_splits must be positive")
+    dev = q3.device
+    pm = torch.empty((B, hq, num_splits), dtype=torch.float32, device=dev)
+    pl = torch.empty_like(pm)
+    po = torch.empty((B, hq, num_splits, D), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        rc = _lib.ecc_decode_partials(_ptr(q3), _ptr(k_pool), _ptr(v_pool), kbs[0], kbs[1], _ptr(pm), _ptr(pl),
+                                      _ptr(po), B, hq, hkv, int(seq_len),
+                                      float(sm_scale) if sm_scale is not None else 0.0,
+                                      ROTATE_Q if rotate_q else 0, int(num_splits), _stream(q3))
+    _check(rc, "decode_partials")
+    return pm, pl, po
+
+
+def lse_merge(pm: torch.Tensor, pl: torch.Tensor, po: torch.Tensor, unrotate_out: bool = False,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """Merge partials along their split axis: pm/pl [..., n], po [..., n, 128]
+    -> [..., 128] fp16 (optionally WHT-unrotated)."""
+    for t, nme in ((pm, "pm"), (pl, "pl"), (po, "po")):
+        _require_input(t, nme)
+        if t.dtype != torch.float32:
+            raise RuntimeError(f"{nme} must be float32")
+    n = pm.shape[-1]
+    rows = pm.numel() // max(n, 1)
+    if pl.shape != pm.shape or po.shape != pm.shape + (D,):
+        raise RuntimeError("partial shapes disagree")
+    if out is None:
+        out = torch.empty(pm.shape[:-1] + (D,), dtype=torch.float16, device=pm.device)
+    with torch.cuda.device(pm.device):
+        rc = _lib.ecc_lse_merge(_ptr(pm), _ptr(pl), _ptr(po), rows, n, _ptr(out),
+                                UNROTATE_OUT if unrotate_out else 0, _stream(pm))
+    _check(rc, "lse_merge")
+    return out
+
+
+def version() -> int:
+    return int(_lib.ecc_version())

@@ -1,0 +1,140 @@
+/*
+ * ecc_kv_b200.h -- C ABI of libeccb200.so, the B200 (sm_100a) implementation
+ * of the ECC-INT4 KV-cache hot path: compress (WHT + Lloyd-Max INT4 + sign
+ * syndrome -> 128-byte ECC_KV_Block) and fused decode attention.
+ *
+ * Plain pointers and sizes only.  Every function is asynchronous on the given
+ * stream (NULL = legacy default stream) unless stated otherwise, returns
+ * ECC_OK (0) or a negative ECC_ERR_* code, and never aborts; ecc_strerror()
+ * names a code.  Pointers are device pointers unless stated otherwise.
+ *
+ * Block format (one token of one KV head, csrc/ecc_ops.h:22-32 of the
+ * reference): bytes 0..63 INT4 codes, byte i = q[2i] | q[2i+1] << 4;
+ * bytes 64..79 sign syndrome, bit j in byte j/8 at position j%8 (1 = the
+ * quantisation residual is >= 0); fp16 scale @80, zero @82, alpha @84;
+ * bytes 86..127 zero.
+ */
+#ifndef ECC_KV_B200_H
+#define ECC_KV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *ecc_stream_t; /* same type as cudaStream_t */
+
+enum {
+    ECC_OK = 0,
+    ECC_ERR_NULL = -1,        /* a required pointer is NULL */
+    ECC_ERR_SHAPE = -2,       /* a size is out of range (D != 128, n < 0, ...) */
+    ECC_ERR_ALIGN = -3,       /* a pointer or stride is not suitably aligned */
+    ECC_ERR_GQA = -4,         /* Hq is not a multiple of Hkv */
+    ECC_ERR_WORKSPACE = -5,   /* workspace missing or smaller than required */
+    ECC_ERR_LAUNCH = -6,      /* the CUDA launch failed (cudaGetLastError) */
+    ECC_ERR_CUDA = -7,        /* another CUDA runtime call failed */
+    ECC_ERR_DEVICE = -8       /* no usable sm_100 device */
+};
+
+#define ECC_DECODE_ROTATE_Q 1    /* rotate the query (WHT) inside the kernel */
+#define ECC_DECODE_UNROTATE_OUT 2 /* apply the WHT to the output (values stored rotated) */
+
+/* Name of an error code (static string). */
+const char *ecc_strerror(int code);
+
+/* Library version, e.g. 100 for 0.1.0. */
+int ecc_version(void);
+
+/* ---- WHT ------------------------------------------------------------------
+ * In-place normalised Walsh-Hadamard transform of n rows of length d (power
+ * of two, 1 <= d <= 1024), contiguous [n, d], fp16 or fp32.  Butterfly with
+ * stride 1,2,...,d/2 then an IEEE division by fp32(sqrt(d)) -- the same
+ * arithmetic as custom_kv/ops_cpu.py:29 hadamard_rotate_cpu.
+ * Replaces launch_hadamard_f16 / launch_hadamard_f32 (csrc/hadamard.cu:107,
+ * :119) behind custom_ecc_cuda.hadamard_rotate (csrc/ecc_ops.cpp:32). */
+int ecc_hadamard_f16(void *x, int64_t n, int d, ecc_stream_t stream);
+int ecc_hadamard_f32(void *x, int64_t n, int d, ecc_stream_t stream);
+
+/* ---- compress -------------------------------------------------------------
+ * n contiguous fp16 vectors [n, 128] -> n blocks [n, 128] bytes.  rotate = 1
+ * applies the WHT first (custom_kv/ops_cpu.py:198 compress_cpu); rotate = 0
+ * takes an already rotated input.  Bit-exact with compress_cpu.
+ * Replaces launch_compress_ecc (csrc/compress_ecc.cu:183) behind
+ * custom_ecc_cuda.compress_and_store (csrc/ecc_ops.cpp:68) with rotate = 0.
+ * x must be 16-byte aligned, blocks 128-byte aligned. */
+int ecc_compress(const void *x_f16, void *blocks, int64_t n, int rotate, ecc_stream_t stream);
+
+/* Strided compress of x[b][h][l][0..127] (element strides xs_b, xs_h, xs_l,
+ * last dim contiguous, each multiple of 8) into the block pool at
+ * block index b*bs_b + h*bs_h + l (token stride one block).  This is the
+ * cache write of ErrorCorrectedCache.update (custom_kv/cache.py:103-126). */
+int ecc_compress_strided(const void *x_f16, int64_t xs_b, int64_t xs_h, int64_t xs_l,
+                         void *blocks, int64_t bs_b, int64_t bs_h,
+                         int B, int H, int64_t L, int rotate, ecc_stream_t stream);
+
+/* Copy the fp16 (scale, zero, alpha) of block block_idx to host memory as
+ * fp32.  Synchronous on `stream`.  Replaces custom_ecc_cuda.get_block_metadata
+ * (csrc/ecc_ops.cpp:98). */
+int ecc_get_block_metadata(const void *blocks, int64_t n_blocks, int64_t block_idx,
+                           float *host_out3, ecc_stream_t stream);
+
+/* Reconstruct blocks to fp16 vectors: out = (C[q]*scale + zero) + alpha*s
+ * (custom_kv/fused_decode.py:229-241), n contiguous blocks -> [n, 128]. */
+int ecc_dequantize(const void *blocks, void *out_f16, int64_t n, ecc_stream_t stream);
+
+/* Pack the reference's SoA trio (custom_kv/cache.py:79-84: int4 [N,64] u8,
+ * syn [N,16] u8, meta [N,3] fp16, each with its own row stride in bytes)
+ * into contiguous 128-byte blocks. */
+int ecc_pack_soa(const void *int4, int64_t int4_row_bytes, const void *syn, int64_t syn_row_bytes,
+                 const void *meta, int64_t meta_row_bytes, void *blocks, int64_t n, ecc_stream_t stream);
+
+/* ---- decode attention -----------------------------------------------------
+ * One decode step of GQA attention over compressed K and V pools.
+ *   q:        [B, Hq, 128] fp16, contiguous (rotated query unless flags has
+ *             ECC_DECODE_ROTATE_Q).
+ *   k_blocks, v_blocks: pools; block (b, kv_head, t) at block index
+ *             b*bs_b + kv_head*bs_h + t, t in [0, seq_len).  128-byte aligned.
+ *   out:      [B, Hq, 128] fp16, contiguous.
+ *   sm_scale: softmax scale; <= 0 selects 1/sqrt(128).
+ *   num_splits: sequence partitions per (b, kv_head); <= 0 chooses one.
+ *   workspace: device scratch of at least ecc_decode_workspace_size() bytes
+ *             for the split partials (may be NULL when that size is 0).
+ * Query head h reads kv head h / (Hq / Hkv) (HF repeat_kv convention).
+ * Replaces the Triton fused_ecc_decode_attention
+ * (custom_kv/fused_decode.py:153) and the dequantise-then-SDPA decode step of
+ * custom_kv/patch.py:100 _ecc_decode_step. */
+int ecc_decode(const void *q_f16, const void *k_blocks, const void *v_blocks, int64_t bs_b,
+               int64_t bs_h, void *out_f16, void *workspace, size_t workspace_bytes, int B, int Hq,
+               int Hkv, int64_t seq_len, float sm_scale, int flags, int num_splits,
+               ecc_stream_t stream);
+
+/* Workspace bytes ecc_decode needs for these sizes (0 if it needs none);
+ * num_splits as passed to ecc_decode. */
+size_t ecc_decode_workspace_size(int B, int Hq, int Hkv, int64_t seq_len, int num_splits);
+
+/* The split count ecc_decode uses when num_splits <= 0. */
+int ecc_decode_default_splits(int B, int Hkv, int64_t seq_len);
+
+/* Per-split partials of one decode step without the merge, for combining
+ * partials across devices (sequence-chunk sharding): writes m, l
+ * [B, Hq, num_splits] fp32 and o [B, Hq, num_splits, 128] fp32 (o is the
+ * unnormalised sum of e^(s - m) v, in the stored value basis).  Token
+ * positions [0, seq_len) of the pools are this device's chunk. */
+int ecc_decode_partials(const void *q_f16, const void *k_blocks, const void *v_blocks,
+                        int64_t bs_b, int64_t bs_h, float *part_m, float *part_l, float *part_o,
+                        int B, int Hq, int Hkv, int64_t seq_len, float sm_scale, int flags,
+                        int num_splits, ecc_stream_t stream);
+
+/* Log-sum-exp merge of n partials per row (rows = B*Hq): m, l [rows, n],
+ * o [rows, n, 128] as written by ecc_decode_partials (rows may gather
+ * partials of several devices).  out [rows, 128] fp16; flags may hold
+ * ECC_DECODE_UNROTATE_OUT. */
+int ecc_lse_merge(const float *part_m, const float *part_l, const float *part_o, int64_t rows, int n,
+                  void *out_f16, int flags, ecc_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ECC_KV_B200_H */

@@ -1,0 +1,166 @@
+"""Compress path on the GPU through the C ABI, bit-exact against the oracle and
+the reference's golden vectors."""
+import hashlib
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import workloads
+
+pytestmark = pytest.mark.gpu
+GROUPS = ["c1", "heavy", "offset", "edge"]
+
+
+@pytest.fixture(scope="module")
+def ops(cuda_device):
+    import custom_ecc_cuda
+    return custom_ecc_cuda
+
+
+def _f16(a: np.ndarray, dev) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(torch.float16).to(dev)
+
+
+@pytest.mark.parametrize("group", GROUPS)
+def test_rotate_compress_matches_reference_golden(ops, compress_golden, cuda_device, group):
+    x = _f16(compress_golden[f"{group}_x16"], cuda_device)
+    blocks = ops.rotate_and_compress(x)
+    got = blocks.cpu().numpy()
+    ref = compress_golden[f"{group}_r1_blocks"]
+    bad = np.nonzero((got != ref).any(1))[0]
+    assert bad.size == 0, f"rows {bad[:10]} differ"
+
+
+@pytest.mark.parametrize("group", GROUPS)
+def test_compress_and_store_matches_reference_golden(ops, compress_golden, cuda_device, group):
+    """Pre-rotated input, the reference op's contract (csrc/ecc_ops.cpp:68)."""
+    x = _f16(compress_golden[f"{group}_x16"], cuda_device)
+    cache = torch.full((x.shape[0] + 3, 128), 0xAB, dtype=torch.uint8, device=cuda_device)
+    ops.compress_and_store(x, cache)
+    got = cache.cpu().numpy()
+    assert np.array_equal(got[:x.shape[0]], compress_golden[f"{group}_r0_blocks"])
+    assert np.all(got[x.shape[0]:] == 0xAB)  # rows past N untouched
+
+
+def test_full_c1_digest(ops, cuda_device):
+    with open(os.path.join(os.path.dirname(__file__), "golden", "c1_digest.json")) as f:
+        dig = json.load(f)
+    k16, v16, _ = workloads.make_c1(seed=0)
+    kp = torch.empty((1, 8, 2048, 128), dtype=torch.uint8, device=cuda_device)
+    vp = torch.empty_like(kp)
+    ops.compress_into(k16.to(cuda_device), kp, pos=0, rotate=True)
+    ops.compress_into(v16.to(cuda_device), vp, pos=0, rotate=True)
+    assert hashlib.sha256(kp.cpu().numpy().tobytes()).hexdigest() == dig["k_sha256"]
+    assert hashlib.sha256(vp.cpu().numpy().tobytes()).hexdigest() == dig["v_sha256"]
+
+
+@pytest.mark.parametrize("rotate", [True, False])
+def test_large_heavy_tail_equals_oracle(ops, oracle, cuda_device, rotate):
+    """2 heads x 131072 tokens of the compress-throughput workload, every block."""
+    x16 = workloads.make_heavy(seed=77, n=262144)
+    got = ops.rotate_and_compress(x16.to(cuda_device)) if rotate else None
+    if not rotate:
+        got = torch.empty((x16.shape[0], 128), dtype=torch.uint8, device=cuda_device)
+        ops.compress_and_store(x16.to(cuda_device), got)
+    ref = oracle.compress(x16.numpy(), rotate=rotate)
+    got = got.cpu().numpy()
+    bad = np.nonzero((got != ref).any(1))[0]
+    ties = oracle.count_ties(x16.numpy()[bad], rotate=rotate, tol=1e-6) if bad.size else 0
+    assert bad.size == 0, f"{bad.size} blocks differ ({ties} tie elements among them)"
+
+
+def test_strided_input_into_pool_positions(ops, oracle, cuda_device):
+    """HF key_states are a transposed view [B, H, L, D]; write at pos > 0."""
+    B, H, L, cap, pos = 2, 3, 37, 64, 11
+    g = torch.Generator().manual_seed(5)
+    base = torch.randn(B, L, H, 128, generator=g).half()
+    x = base.to(cuda_device).transpose(1, 2)  # [B, H, L, D], non-contiguous
+    pool = torch.zeros((B, H, cap, 128), dtype=torch.uint8, device=cuda_device)
+    ops.compress_into(x, pool, pos=pos, rotate=True)
+    ref = oracle.compress(base.transpose(1, 2).contiguous().reshape(-1, 128).numpy(), rotate=True)
+    got = pool.cpu().numpy()
+    assert np.array_equal(got[:, :, pos:pos + L].reshape(-1, 128), ref)
+    assert not got[:, :, :pos].any() and not got[:, :, pos + L:].any()
+
+
+@pytest.mark.parametrize("n", [1, 7, 63, 64, 65, 1000])
+def test_ragged_counts(ops, oracle, cuda_device, n):
+    x16 = workloads.make_heavy(seed=n, n=n)
+    got = ops.rotate_and_compress(x16.to(cuda_device)).cpu().numpy()
+    assert np.array_equal(got, oracle.compress(x16.numpy(), rotate=True))
+
+
+def test_empty_input(ops, cuda_device):
+    x = torch.empty((0, 128), dtype=torch.float16, device=cuda_device)
+    assert ops.rotate_and_compress(x).shape == (0, 128)
+
+
+@pytest.mark.parametrize("d", [1, 2, 16, 64, 128, 256, 1024])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
+def test_hadamard_rotate(ops, oracle, cuda_device, d, dtype):
+    g = torch.Generator().manual_seed(d)
+    x = (torch.randn(33, d, generator=g) * 3).to(dtype)
+    y = x.to(cuda_device)
+    out = ops.hadamard_rotate(y)
+    assert out.data_ptr() == y.data_ptr()  # in place
+    ref = oracle.wht(x.float().numpy()) if d > 1 else x.float().numpy()
+    if dtype == torch.float32:
+        assert np.array_equal(y.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+    else:
+        assert np.array_equal(y.cpu().numpy().view(np.uint16), ref.astype(np.float16).view(np.uint16))
+
+
+def test_hadamard_errors(ops, cuda_device):
+    with pytest.raises(RuntimeError, match="power of 2"):
+        ops.hadamard_rotate(torch.zeros(2, 100, device=cuda_device))
+    with pytest.raises(RuntimeError, match="1024"):
+        ops.hadamard_rotate(torch.zeros(2, 2048, device=cuda_device))
+    with pytest.raises(RuntimeError, match="float16 and float32"):
+        ops.hadamard_rotate(torch.zeros(2, 128, device=cuda_device, dtype=torch.float64))
+    with pytest.raises(RuntimeError, match="2D"):
+        ops.hadamard_rotate(torch.zeros(2, 2, 128, device=cuda_device))
+    with pytest.raises(RuntimeError, match="contiguous"):
+        ops.hadamard_rotate(torch.zeros(128, 4, device=cuda_device).t())
+
+
+def test_compress_errors(ops, cuda_device):
+    x = torch.zeros(4, 128, dtype=torch.float16, device=cuda_device)
+    with pytest.raises(RuntimeError, match="D=128"):
+        ops.compress_and_store(torch.zeros(4, 64, dtype=torch.float16, device=cuda_device),
+                               torch.zeros(4, 128, dtype=torch.uint8, device=cuda_device))
+    with pytest.raises(RuntimeError, match="\\[N, 128\\]"):
+        ops.compress_and_store(x, torch.zeros(4, 64, dtype=torch.uint8, device=cuda_device))
+    with pytest.raises(RuntimeError):
+        ops.compress_and_store(x.float(), torch.zeros(4, 128, dtype=torch.uint8, device=cuda_device))
+    with pytest.raises(RuntimeError, match="capacity"):
+        ops.compress_into(x.view(1, 1, 4, 128), torch.zeros((1, 1, 6, 128), dtype=torch.uint8, device=cuda_device),
+                          pos=3)
+
+
+def test_get_block_metadata(ops, compress_golden, cuda_device):
+    blocks = torch.from_numpy(compress_golden["heavy_r1_blocks"]).to(cuda_device)
+    for i in (0, 5, 255):
+        md = ops.get_block_metadata(blocks, i)
+        assert md.device.type == "cpu" and md.dtype == torch.float32
+        ref = compress_golden["heavy_r1_blocks"][i, 80:86].view(np.float16).astype(np.float32)
+        assert np.array_equal(md.numpy(), ref)
+    with pytest.raises(RuntimeError):
+        ops.get_block_metadata(blocks, 256)
+
+
+def test_dequantize_matches_reconstruction(ops, oracle, compress_golden, cuda_device):
+    blk = np.concatenate([compress_golden[f"{g}_r1_blocks"] for g in ("c1", "heavy")])
+    got = ops.dequantize(torch.from_numpy(blk).to(cuda_device)).cpu().numpy()
+    ref = oracle.reconstruct(blk).astype(np.float16)
+    assert np.array_equal(got.view(np.uint16), ref.view(np.uint16))
+
+
+def test_pack_soa_roundtrip(ops, oracle, compress_golden, cuda_device):
+    blk = compress_golden["c1_r1_blocks"]
+    int4, syn, meta = oracle.blocks_to_soa(blk)
+    t = lambda a: torch.from_numpy(a).to(cuda_device)
+    packed = ops.pack_soa(t(int4), t(syn), t(meta.view(np.int16)).view(torch.float16)).cpu().numpy()
+    assert np.array_equal(packed, blk)

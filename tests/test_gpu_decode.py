@@ -1,0 +1,164 @@
+"""Fused decode attention on the GPU through the C ABI against the oracle and
+the reference's golden outputs.  Tolerance: 2e-3 max abs error in fp16."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import workloads
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-3
+
+
+@pytest.fixture(scope="module")
+def ops(cuda_device):
+    import custom_ecc_cuda
+    return custom_ecc_cuda
+
+
+def _dev(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _q(a16_bits, dev):
+    return torch.from_numpy(np.ascontiguousarray(a16_bits).view(np.int16)).view(torch.float16).to(dev)
+
+
+def _err(got: torch.Tensor, ref: np.ndarray) -> float:
+    g = got.float().cpu().numpy().reshape(ref.shape)
+    return float(np.abs(g - ref.astype(np.float16).astype(np.float32)).max())
+
+
+@pytest.mark.parametrize("ci", range(4))
+def test_decode_matches_reference_golden(ops, decode_golden, cuda_device, ci):
+    B, hq, hkv, L = [int(v) for v in decode_golden[f"case{ci}_meta"]]
+    kb = _dev(decode_golden[f"case{ci}_kblocks"], cuda_device)
+    vb = _dev(decode_golden[f"case{ci}_vblocks"], cuda_device)
+    q = _q(decode_golden[f"case{ci}_q16"], cuda_device)
+    out = ops.decode_attention(q, kb, vb, seq_len=L)
+    ref = decode_golden[f"case{ci}_out16"].view(np.float16).astype(np.float32).reshape(B, hq, 128)
+    assert _err(out, ref) <= TOL
+
+
+def test_fused_ecc_decode_attention_soa_api(decode_golden, cuda_device):
+    """The reference wrapper's signature with SoA tensors, both as standalone
+    tensors (packed) and as zero-copy views of a pool."""
+    from custom_kv.fused_decode import fused_ecc_decode_attention
+    from custom_kv.cache import soa_views
+    B, hq, hkv, L = [int(v) for v in decode_golden["case1_meta"]]
+    kb = _dev(decode_golden["case1_kblocks"], cuda_device)
+    vb = _dev(decode_golden["case1_vblocks"], cuda_device)
+    q = _q(decode_golden["case1_q16"], cuda_device)
+    ref = decode_golden["case1_out16"].view(np.float16).astype(np.float32).reshape(B, hq, 128)
+    kv, vv = soa_views(kb), soa_views(vb)
+    out_views = fused_ecc_decode_attention(q, *kv, *vv, L)
+    standalone = [t.contiguous() for t in kv + vv]
+    out_packed = fused_ecc_decode_attention(q, *standalone, L)
+    assert _err(out_views, ref) <= TOL and _err(out_packed, ref) <= TOL
+    assert out_views.shape == (B, hq, 1, 128) and out_views.dtype == torch.float16
+
+
+def test_full_c1_decode_against_reference(ops, cuda_device):
+    """Single-layer op test: GPU compress then decode vs the reference's
+    cpu_reference_decode output (GQA via repeat_kv)."""
+    path = os.path.join(os.path.dirname(__file__), "golden", "c1_decode_out16.npy")
+    if not os.path.exists(path):
+        pytest.skip("c1 decode fixture not generated")
+    k16, v16, q16 = workloads.make_c1(seed=0)
+    kp = torch.empty((1, 8, 2048, 128), dtype=torch.uint8, device=cuda_device)
+    vp = torch.empty_like(kp)
+    ops.compress_into(k16.to(cuda_device), kp, pos=0, rotate=True)
+    ops.compress_into(v16.to(cuda_device), vp, pos=0, rotate=True)
+    out = ops.decode_attention(q16.to(cuda_device), kp, vp, seq_len=2048)
+    ref = np.load(path).view(np.float16).astype(np.float32).reshape(1, 32, 128)
+    assert _err(out, ref) <= TOL
+
+
+def _random_pools(oracle, B, hkv, L, cap, seed):
+    k16, v16, _ = workloads.make_c1(seed=seed, B=B, hkv=hkv, hq=hkv, L=L)
+    kb = oracle.compress(k16.reshape(-1, 128).numpy()).reshape(B, hkv, L, 128)
+    vb = oracle.compress(v16.reshape(-1, 128).numpy()).reshape(B, hkv, L, 128)
+    kp = np.zeros((B, hkv, cap, 128), np.uint8)
+    vp = np.zeros_like(kp)
+    kp[:, :, :L], vp[:, :, :L] = kb, vb
+    return kp, vp
+
+
+@pytest.mark.parametrize("B,hq,hkv,L,splits", [
+    (1, 8, 8, 1, 0), (1, 4, 1, 65, 0), (2, 8, 2, 127, 3), (3, 12, 4, 300, 0),   # group 3
+    (1, 32, 8, 2048, 1), (1, 32, 8, 2048, 7), (2, 16, 2, 1000, 0),              # group 8
+    (1, 48, 4, 640, 0),                                                          # group 12
+])
+@pytest.mark.parametrize("flags", [(False, False), (True, True)])
+def test_decode_shapes_vs_oracle(ops, oracle, cuda_device, B, hq, hkv, L, splits, flags):
+    cap = L + 5
+    kp, vp = _random_pools(oracle, B, hkv, L, cap, seed=L + hq)
+    g = torch.Generator().manual_seed(L)
+    q = torch.randn(B, hq, 1, 128, generator=g).half()
+    out = ops.decode_attention(q.to(cuda_device), _dev(kp, cuda_device), _dev(vp, cuda_device), seq_len=L,
+                               rotate_q=flags[0], unrotate_out=flags[1], num_splits=splits)
+    ref = oracle.decode(q.numpy(), kp, vp, hkv=hkv, seq_len=L, rotate_q=flags[0], unrotate_out=flags[1])
+    assert _err(out, ref) <= TOL
+
+
+def test_decode_custom_scale_and_prefix(ops, oracle, cuda_device):
+    """sm_scale is honoured and only the first seq_len tokens are read."""
+    kp, vp = _random_pools(oracle, 1, 2, 200, 256, seed=3)
+    kp[:, :, 150:] = 0xFF  # garbage beyond seq_len
+    vp[:, :, 150:] = 0xFF
+    q = torch.randn(1, 4, 1, 128, generator=torch.Generator().manual_seed(9)).half()
+    out = ops.decode_attention(q.to(cuda_device), _dev(kp, cuda_device), _dev(vp, cuda_device), seq_len=150,
+                               sm_scale=0.05)
+    ref = oracle.decode(q.numpy(), kp, vp, hkv=2, seq_len=150, sm_scale=0.05)
+    assert _err(out, ref) <= TOL
+
+
+def test_partials_and_merge_equal_decode(ops, oracle, cuda_device):
+    """decode_partials + lse_merge (the cross-device combine) equals decode,
+    including partials gathered from two token chunks (sequence sharding)."""
+    kp, vp = _random_pools(oracle, 2, 2, 700, 700, seed=8)
+    q = torch.randn(2, 8, 1, 128, generator=torch.Generator().manual_seed(2)).half().to(cuda_device)
+    K, V = _dev(kp, cuda_device), _dev(vp, cuda_device)
+    full = ops.decode_attention(q, K, V, seq_len=700, rotate_q=True, unrotate_out=True)
+    pm, pl, po = ops.decode_partials(q, K, V, seq_len=700, num_splits=5, rotate_q=True)
+    merged = ops.lse_merge(pm, pl, po, unrotate_out=True)
+    assert (merged.view(-1).float() - full.view(-1).float()).abs().max().item() <= 1e-3
+    # two "devices": tokens [0, 400) and [400, 700)
+    a = ops.decode_partials(q, K[:, :, :400], V[:, :, :400], seq_len=400, num_splits=2, rotate_q=True)
+    b = ops.decode_partials(q, K[:, :, 400:], V[:, :, 400:], seq_len=300, num_splits=3, rotate_q=True)
+    cat = [torch.cat([x, y], dim=2).contiguous() for x, y in zip(a, b)]
+    merged2 = ops.lse_merge(*cat, unrotate_out=True)
+    assert (merged2.view(-1).float() - full.view(-1).float()).abs().max().item() <= 1e-3
+
+
+def test_empty_context_and_empty_splits(ops, cuda_device):
+    kp = torch.zeros((1, 1, 64, 128), dtype=torch.uint8, device=cuda_device)
+    q = torch.randn(1, 2, 1, 128, device=cuda_device).half()
+    out = ops.decode_attention(q, kp, kp, seq_len=0)
+    assert torch.count_nonzero(out) == 0
+    pm, pl, po = ops.decode_partials(q, kp, kp, seq_len=10, num_splits=4)
+    assert (pl[..., 1:] == 0).all()  # 10 tokens fit in the first 64-token split
+
+
+def test_decode_errors(ops, cuda_device):
+    kp = torch.zeros((1, 3, 64, 128), dtype=torch.uint8, device=cuda_device)
+    q = torch.randn(1, 4, 1, 128, device=cuda_device).half()
+    with pytest.raises(RuntimeError, match="multiple"):
+        ops.decode_attention(q, kp, kp, seq_len=8)
+    with pytest.raises(RuntimeError, match="capacity"):
+        ops.decode_attention(q[:, :3], kp, kp, seq_len=65)
+    with pytest.raises(RuntimeError, match="float16"):
+        ops.decode_attention(q.float()[:, :3], kp, kp, seq_len=8)
+
+
+def test_long_context_vs_oracle(ops, oracle, cuda_device):
+    """64k tokens, one batch row, GQA group 4 (the decode benchmark's shape per row)."""
+    L, hkv, hq = 65536, 2, 8
+    kp, vp = _random_pools(oracle, 1, hkv, L, L, seed=64)
+    q = torch.randn(1, hq, 1, 128, generator=torch.Generator().manual_seed(64)).half()
+    out = ops.decode_attention(q.to(cuda_device), _dev(kp, cuda_device), _dev(vp, cuda_device), seq_len=L,
+                               rotate_q=True, unrotate_out=True)
+    ref = oracle.decode(q.numpy(), kp, vp, hkv=hkv, seq_len=L, rotate_q=True, unrotate_out=True)
+    assert _err(out, ref) <= TOL
