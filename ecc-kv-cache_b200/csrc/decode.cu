@@ -19,6 +19,9 @@ namespace ecc {
 
 int launch_status();
 int sm_count();
+int launch_decode_mma(const void *q, const void *kbp, const void *vbp, int64_t bs_b, int64_t bs_h, float *pm,
+                      float *pl, float *po, int B, int Hq, int Hkv, int64_t seq_len, int64_t chunk, int ns,
+                      float scale_log2, int flags, cudaStream_t s);
 
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -263,6 +266,11 @@ static int run_partials(const void *q, const void *kb, const void *vb, int64_t b
     if (!(sm_scale > 0.0f)) sm_scale = 1.0f / std::sqrt((float)kD);
     const float scale_log2 = sm_scale * kLog2e;
     const int group = Hq / Hkv;
+    if (group <= 8 && !(flags & ECC_DECODE_CUDA_CORES)) {
+        const int rc = launch_decode_mma(q, kb, vb, bs_b, bs_h, pm, pl, po, B, Hq, Hkv, seq_len, chunk, ns,
+                                         scale_log2, flags & ECC_DECODE_ROTATE_Q, s);
+        return rc != ECC_OK ? rc : launch_status();
+    }
     if (group == 1)
         launch_v1<1>(q, kb, vb, bs_b, bs_h, pm, pl, po, B, Hq, Hkv, seq_len, chunk, ns, scale_log2, flags, s);
     else if (group == 2)
@@ -290,7 +298,8 @@ extern "C" int ecc_decode_partials(const void *q_f16, const void *k_blocks, cons
         chunk = cdiv(cdiv(std::max<int64_t>(seq_len, 1), num_splits), 64) * 64;
     }
     return run_partials(q_f16, k_blocks, v_blocks, bs_b, bs_h, part_m, part_l, part_o, B, Hq, Hkv, seq_len, chunk,
-                        num_splits, sm_scale, flags & ECC_DECODE_ROTATE_Q, reinterpret_cast<cudaStream_t>(stream));
+                        num_splits, sm_scale, flags & (ECC_DECODE_ROTATE_Q | ECC_DECODE_CUDA_CORES),
+                        reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int ecc_lse_merge(const float *part_m, const float *part_l, const float *part_o, int64_t rows, int n,
@@ -321,7 +330,7 @@ extern "C" int ecc_decode(const void *q_f16, const void *k_blocks, const void *v
     float *pl = pm + parts;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     rc = run_partials(q_f16, k_blocks, v_blocks, bs_b, bs_h, pm, pl, po, B, Hq, Hkv, seq_len, chunk, ns, sm_scale,
-                      flags & ECC_DECODE_ROTATE_Q, s);
+                      flags & (ECC_DECODE_ROTATE_Q | ECC_DECODE_CUDA_CORES), s);
     if (rc != ECC_OK) return rc;
     return ecc_lse_merge(pm, pl, po, (int64_t)B * Hq, ns, out_f16, flags & ECC_DECODE_UNROTATE_OUT, stream);
 }

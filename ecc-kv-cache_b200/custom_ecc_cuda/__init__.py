@@ -35,6 +35,7 @@ library_path = os.path.join(_HERE, _LIB_NAME)
 
 ROTATE_Q = 1
 UNROTATE_OUT = 2
+CUDA_CORES = 4
 D = 128
 BLOCK_BYTES = 128
 
@@ -303,12 +304,14 @@ def _query(q: torch.Tensor):
 def decode_attention(query: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, seq_len: int,
                      sm_scale: float | None = None, rotate_q: bool = False, unrotate_out: bool = False,
                      num_splits: int = 0, out: torch.Tensor | None = None,
-                     workspace: torch.Tensor | None = None) -> torch.Tensor:
+                     workspace: torch.Tensor | None = None, cuda_cores: bool = False) -> torch.Tensor:
     """One decode step of GQA attention over block pools [B, Hkv, Lcap, 128].
 
     query [B, Hq, 1, 128] (or [B, Hq, 128]) fp16 -> [B, Hq, 1, 128] fp16.
     Query head h reads kv head h // (Hq // Hkv).  ``sm_scale`` defaults to
-    1/sqrt(128) (custom_kv/fused_decode.py:57)."""
+    1/sqrt(128) (custom_kv/fused_decode.py:57).  ``cuda_cores`` selects the
+    CUDA-core kernel (always used for more than 8 query heads per kv head)
+    instead of the tensor-core one."""
     q3 = _query(query)
     kbs = _pool_strides(k_pool, "k_pool")
     vbs = _pool_strides(v_pool, "v_pool")
@@ -326,7 +329,7 @@ def decode_attention(query: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Te
         out = torch.empty((B, hq, 1, D), dtype=torch.float16, device=q3.device)
     elif not out.is_contiguous() or out.dtype != torch.float16 or out.numel() != B * hq * D:
         raise RuntimeError("out must be a contiguous float16 tensor of B*Hq*128 elements")
-    flags = (ROTATE_Q if rotate_q else 0) | (UNROTATE_OUT if unrotate_out else 0)
+    flags = (ROTATE_Q if rotate_q else 0) | (UNROTATE_OUT if unrotate_out else 0) | (CUDA_CORES if cuda_cores else 0)
     scale = float(sm_scale) if sm_scale is not None else 0.0
     need = decode_workspace_size(B, hq, hkv, seq_len, num_splits)
     with torch.cuda.device(q3.device):
@@ -340,7 +343,8 @@ def decode_attention(query: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Te
 
 
 def decode_partials(query: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, seq_len: int,
-                    num_splits: int, sm_scale: float | None = None, rotate_q: bool = False):
+                    num_splits: int, sm_scale: float | None = None, rotate_q: bool = False,
+                    cuda_cores: bool = False):
     """Split partials (m, l, o) of one decode step over token positions
     [0, seq_len) of the pools: m, l [B, Hq, num_splits] fp32 (m in natural-log
     units), o [B, Hq, num_splits, 128] fp32 unnormalised."""
@@ -361,7 +365,8 @@ def decode_partials(query: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Ten
         rc = _lib.ecc_decode_partials(_ptr(q3), _ptr(k_pool), _ptr(v_pool), kbs[0], kbs[1], _ptr(pm), _ptr(pl),
                                       _ptr(po), B, hq, hkv, int(seq_len),
                                       float(sm_scale) if sm_scale is not None else 0.0,
-                                      ROTATE_Q if rotate_q else 0, int(num_splits), _stream(q3))
+                                      (ROTATE_Q if rotate_q else 0) | (CUDA_CORES if cuda_cores else 0),
+                                      int(num_splits), _stream(q3))
     _check(rc, "decode_partials")
     return pm, pl, po
 

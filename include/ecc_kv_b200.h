@@ -40,6 +40,8 @@ enum {
 
 #define ECC_DECODE_ROTATE_Q 1    /* rotate the query (WHT) inside the kernel */
 #define ECC_DECODE_UNROTATE_OUT 2 /* apply the WHT to the output (values stored rotated) */
+#define ECC_DECODE_CUDA_CORES 4   /* use the CUDA-core kernel instead of the tensor-core one
+                                     (groups of more than 8 query heads always use it) */
 
 /* Name of an error code (static string). */
 const char *ecc_strerror(int code);
