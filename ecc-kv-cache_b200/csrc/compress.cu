@@ -614,6 +614,7 @@ extern "C" const char *ecc_strerror(int code) {
         case ECC_ERR_LAUNCH: return "kernel launch failed";
         case ECC_ERR_CUDA: return "CUDA runtime call failed";
         case ECC_ERR_DEVICE: return "no usable CUDA device";
+        case ECC_ERR_SCRATCH_LIMIT: return "request exceeds the library's static decode scratch";
         default: return "unknown error";
     }
 }

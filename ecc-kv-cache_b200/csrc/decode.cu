@@ -334,3 +334,57 @@ extern "C" int ecc_decode(const void *q_f16, const void *k_blocks, const void *v
     if (rc != ECC_OK) return rc;
     return ecc_lse_merge(pm, pl, po, (int64_t)B * Hq, ns, out_f16, flags & ECC_DECODE_UNROTATE_OUT, stream);
 }
+
+// ---------------------------------------------------------------------------
+// Decode without any allocation: the split partials live in a fixed device
+// array that belongs to this library (ECC_DECODE_STATIC_SCRATCH_BYTES, held on
+// every GPU that loads the library until the process exits).  For callers
+// that must not call cudaMalloc themselves -- e.g. a host whose device memory
+// is owned by another allocator that has already reserved the budget, or a
+// latency-critical path that cannot afford cudaMalloc's implicit
+// synchronisation.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+static __device__ __align__(256) unsigned char g_decode_scratch[ECC_DECODE_STATIC_SCRATCH_BYTES];
+
+static std::mutex g_scratch_mu;
+static void *g_scratch_addr[64];
+
+// Device address of g_decode_scratch on the current device (the host-side
+// name is only a stand-in for it), looked up once per device.
+static int static_scratch(void **out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ECC_ERR_DEVICE;
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (!g_scratch_addr[dev]) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_decode_scratch) != cudaSuccess || !p) return ECC_ERR_CUDA;
+        g_scratch_addr[dev] = p;
+    }
+    *out = g_scratch_addr[dev];
+    return ECC_OK;
+}
+
+extern "C" int ecc_decode_static(const void *q_f16, const void *k_blocks, const void *v_blocks, int64_t bs_b,
+                                 int64_t bs_h, void *out_f16, int B, int Hq, int Hkv, int64_t seq_len,
+                                 float sm_scale, int flags, int num_splits, ecc_stream_t stream) {
+    int rc = check_decode_args(q_f16, k_blocks, v_blocks, B, Hq, Hkv, seq_len);
+    if (rc != ECC_OK) return rc;
+    if (!out_f16) return ECC_ERR_NULL;
+    const size_t cap = ECC_DECODE_STATIC_SCRATCH_BYTES;
+    int ns_req = num_splits;
+    if (ns_req <= 0) {
+        // default split count, lowered until the partials fit the array
+        const size_t per_split = (size_t)B * Hq * sizeof(float) * (2 + kD);
+        const size_t fit = cap > 256 ? (cap - 256) / per_split : 0;
+        if (fit < 1) return ECC_ERR_SCRATCH_LIMIT;
+        ns_req = std::min<int>(ecc_decode_default_splits(B, Hkv, seq_len), (int)std::min<size_t>(fit, 4096));
+    }
+    if (ecc_decode_workspace_size(B, Hq, Hkv, seq_len, ns_req) > cap) return ECC_ERR_SCRATCH_LIMIT;
+    void *scratch = nullptr;
+    rc = static_scratch(&scratch);
+    if (rc != ECC_OK) return rc;
+    return ecc_decode(q_f16, k_blocks, v_blocks, bs_b, bs_h, out_f16, scratch, cap, B, Hq, Hkv, seq_len, sm_scale,
+                      flags, ns_req, stream);
+}

@@ -35,7 +35,8 @@ enum {
     ECC_ERR_WORKSPACE = -5,   /* workspace missing or smaller than required */
     ECC_ERR_LAUNCH = -6,      /* the CUDA launch failed (cudaGetLastError) */
     ECC_ERR_CUDA = -7,        /* another CUDA runtime call failed */
-    ECC_ERR_DEVICE = -8       /* no usable sm_100 device */
+    ECC_ERR_DEVICE = -8,      /* no usable sm_100 device */
+    ECC_ERR_SCRATCH_LIMIT = -9 /* request larger than ECC_DECODE_STATIC_SCRATCH_BYTES */
 };
 
 #define ECC_DECODE_ROTATE_Q 1    /* rotate the query (WHT) inside the kernel */
@@ -135,6 +136,31 @@ int ecc_decode_partials(const void *q_f16, const void *k_blocks, const void *v_b
  * ECC_DECODE_UNROTATE_OUT. */
 int ecc_lse_merge(const float *part_m, const float *part_l, const float *part_o, int64_t rows, int n,
                   void *out_f16, int flags, ecc_stream_t stream);
+
+/* Bytes of the library-owned device array ecc_decode_static uses for its
+ * split partials (4 MiB on every GPU that loads the library, kept until the
+ * process exits). */
+#define ECC_DECODE_STATIC_SCRATCH_BYTES (4u << 20)
+
+/* ecc_decode without a caller workspace and without any allocation, for
+ * callers that must not allocate device memory themselves (a host whose
+ * device memory is owned by another allocator, a latency-critical path that
+ * cannot take cudaMalloc's implicit synchronisation).  No counterpart in the
+ * reference.  Same arguments and results as ecc_decode minus the workspace;
+ * the split partials go to a fixed library-owned device array of
+ * ECC_DECODE_STATIC_SCRATCH_BYTES:
+ *   - B * Hq * splits * 520 bytes (+256) must fit; with num_splits <= 0 the
+ *     default split count is lowered until it fits, otherwise (or when even
+ *     one split does not fit) the call returns ECC_ERR_SCRATCH_LIMIT;
+ *   - the first call on a device looks up the array's device address; make
+ *     that first call before any stream capture;
+ *   - every call on a device shares the one array: calls that overlap on the
+ *     GPU (other streams, other threads) race and corrupt each other's
+ *     results; serialise them on one stream.  Nothing in the array needs to
+ *     start at zero -- each call writes every partial it reads. */
+int ecc_decode_static(const void *q_f16, const void *k_blocks, const void *v_blocks, int64_t bs_b,
+                      int64_t bs_h, void *out_f16, int B, int Hq, int Hkv, int64_t seq_len,
+                      float sm_scale, int flags, int num_splits, ecc_stream_t stream);
 
 #ifdef __cplusplus
 }
