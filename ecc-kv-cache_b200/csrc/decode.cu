@@ -22,6 +22,10 @@ int sm_count();
 int launch_decode_mma(const void *q, const void *kbp, const void *vbp, int64_t bs_b, int64_t bs_h, float *pm,
                       float *pl, float *po, int B, int Hq, int Hkv, int64_t seq_len, int64_t chunk, int ns,
                       float scale_log2, int flags, cudaStream_t s);
+int launch_decode_tma(const void *q, const void *kb, const void *vb, int64_t bs_b, int64_t bs_h, float *pm,
+                      float *pl, float *po, int B, int Hq, int Hkv, int64_t seq_len, int64_t chunk, int ns,
+                      float scale_log2, int flags, cudaStream_t s);
+int tma_default_splits(int B, int Hkv, int64_t seq_len);
 
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -216,17 +220,24 @@ static inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 extern "C" int ecc_decode_default_splits(int B, int Hkv, int64_t seq_len) {
     if (B <= 0 || Hkv <= 0 || seq_len <= 0) return 1;
-    const int64_t target = (int64_t)sm_count() * 8;  // CTAs to cover the SMs several times
-    int64_t ns = cdiv(target, (int64_t)B * Hkv);
-    ns = std::min<int64_t>(ns, cdiv(seq_len, 256));  // at least 256 tokens per split
-    return (int)std::max<int64_t>(1, std::min<int64_t>(ns, 4096));
+    return tma_default_splits(B, Hkv, seq_len);
 }
 
+// Split count and tokens per split.  Default (num_splits <= 0): the partial
+// slots of the TMA kernel's balanced partition, kept as is so that the
+// partial layout is the one that kernel writes (the register kernel then
+// runs one split per slot, trailing ones possibly empty).  Explicit counts
+// are rounded to whole 64-token tiles per split.
 static int effective_splits(int B, int Hkv, int64_t seq_len, int num_splits, int64_t *chunk_out) {
-    int ns = num_splits > 0 ? num_splits : ecc_decode_default_splits(B, Hkv, seq_len);
-    int64_t chunk = cdiv(std::max<int64_t>(seq_len, 1), ns);
-    chunk = cdiv(chunk, 64) * 64;  // whole 64-token tiles per split
-    ns = (int)std::max<int64_t>(1, cdiv(std::max<int64_t>(seq_len, 1), chunk));
+    const int64_t L = std::max<int64_t>(seq_len, 1);
+    if (num_splits <= 0) {
+        const int ns = ecc_decode_default_splits(B, Hkv, seq_len);
+        if (chunk_out) *chunk_out = cdiv(cdiv(L, ns), 64) * 64;
+        return ns;
+    }
+    int ns = num_splits;
+    int64_t chunk = cdiv(cdiv(L, ns), 64) * 64;  // whole 64-token tiles per split
+    ns = (int)std::max<int64_t>(1, cdiv(L, chunk));
     if (chunk_out) *chunk_out = chunk;
     return ns;
 }
@@ -267,6 +278,11 @@ static int run_partials(const void *q, const void *kb, const void *vb, int64_t b
     const float scale_log2 = sm_scale * kLog2e;
     const int group = Hq / Hkv;
     if (group <= 8 && !(flags & ECC_DECODE_CUDA_CORES)) {
+        if (!(flags & ECC_DECODE_REGISTER_PATH)) {
+            const int rc = launch_decode_tma(q, kb, vb, bs_b, bs_h, pm, pl, po, B, Hq, Hkv, seq_len, chunk, ns,
+                                             scale_log2, flags & ECC_DECODE_ROTATE_Q, s);
+            if (rc <= 0) return rc;  // launched (or failed); > 0: shape not handled, use the register path
+        }
         const int rc = launch_decode_mma(q, kb, vb, bs_b, bs_h, pm, pl, po, B, Hq, Hkv, seq_len, chunk, ns,
                                          scale_log2, flags & ECC_DECODE_ROTATE_Q, s);
         return rc != ECC_OK ? rc : launch_status();
@@ -298,7 +314,7 @@ extern "C" int ecc_decode_partials(const void *q_f16, const void *k_blocks, cons
         chunk = cdiv(cdiv(std::max<int64_t>(seq_len, 1), num_splits), 64) * 64;
     }
     return run_partials(q_f16, k_blocks, v_blocks, bs_b, bs_h, part_m, part_l, part_o, B, Hq, Hkv, seq_len, chunk,
-                        num_splits, sm_scale, flags & (ECC_DECODE_ROTATE_Q | ECC_DECODE_CUDA_CORES),
+                        num_splits, sm_scale, flags & (ECC_DECODE_ROTATE_Q | ECC_DECODE_CUDA_CORES | ECC_DECODE_REGISTER_PATH),
                         reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -330,7 +346,7 @@ extern "C" int ecc_decode(const void *q_f16, const void *k_blocks, const void *v
     float *pl = pm + parts;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     rc = run_partials(q_f16, k_blocks, v_blocks, bs_b, bs_h, pm, pl, po, B, Hq, Hkv, seq_len, chunk, ns, sm_scale,
-                      flags & (ECC_DECODE_ROTATE_Q | ECC_DECODE_CUDA_CORES), s);
+                      flags & (ECC_DECODE_ROTATE_Q | ECC_DECODE_CUDA_CORES | ECC_DECODE_REGISTER_PATH), s);
     if (rc != ECC_OK) return rc;
     return ecc_lse_merge(pm, pl, po, (int64_t)B * Hq, ns, out_f16, flags & ECC_DECODE_UNROTATE_OUT, stream);
 }
@@ -379,7 +395,10 @@ extern "C" int ecc_decode_static(const void *q_f16, const void *k_blocks, const 
         const size_t per_split = (size_t)B * Hq * sizeof(float) * (2 + kD);
         const size_t fit = cap > 256 ? (cap - 256) / per_split : 0;
         if (fit < 1) return ECC_ERR_SCRATCH_LIMIT;
-        ns_req = std::min<int>(ecc_decode_default_splits(B, Hkv, seq_len), (int)std::min<size_t>(fit, 4096));
+        const int dflt = ecc_decode_default_splits(B, Hkv, seq_len);
+        // the default count itself when it fits (it selects the same kernel
+        // and partition as ecc_decode with num_splits = 0)
+        ns_req = (size_t)dflt <= fit ? 0 : (int)std::min<size_t>(fit, 4096);
     }
     if (ecc_decode_workspace_size(B, Hq, Hkv, seq_len, ns_req) > cap) return ECC_ERR_SCRATCH_LIMIT;
     void *scratch = nullptr;

@@ -66,7 +66,7 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
 __device__ __forceinline__ uint2 lut(uint32_t tab, uint32_t word, int byte_idx, uint32_t lane8) {
     const uint32_t off = __byte_perm(word, lane8, 0x5504u | ((uint32_t)byte_idx << 4));
     uint2 r;
-    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "r"(tab + off));
+    asm("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "r"(tab + off));
     return r;
 }
 

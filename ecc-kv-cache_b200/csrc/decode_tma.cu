@@ -1,0 +1,621 @@
+// decode_tma.cu -- TMA-fed tensor-core decode attention over 128-byte blocks
+// (sm_100a), GQA groups of up to 8 query heads per kv head.
+//
+// Work split: the tiles (16 tokens of one (b, kv head) row) of all rows are
+// laid end to end and cut into equal contiguous ranges, one per warp of the
+// grid (persistent CTAs, one per SM, kWarps warps each).  A warp therefore
+// sees at most a few row segments; for each it builds the query fragments in
+// its own registers (loaded straight from global memory, WHT-rotated across
+// the four lanes that hold one head) and writes one split partial (m, l, o)
+// at the end.  Partial slot of a segment = warp - first warp of the row, so
+// every row's partials are contiguous; the last warp of a row marks the
+// row's unused slots empty.  No CTA-wide barrier is needed after set-up.
+//
+// Each warp streams its tiles through its own kStages-stage shared-memory
+// ring: one lane issues four cp.async.bulk.tensor boxes per tile (K codes
+// 16x64 B, K syndrome+meta 16x32 B, V codes, V syndrome+meta) on an mbarrier
+// and later waits on it, then __syncwarp hands the data to the warp.  The
+// tensor maps cover [0, seq_len) tokens, so rows past the sequence end come
+// back as zeros; such tokens are masked to -inf.  The consumer math is the one
+// of decode_mma.cu (three m16n8k16 products per 16-dim step for QK and per
+// 16-dim m-tile for PV: centroids hi, centroids lo, signs).
+//
+// Every mbarrier wait is bounded (~2 s of clock64); on timeout the warp
+// raises a device flag for ecc_device_status(), stops computing and drains
+// its outstanding copies (bounded) before exiting.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+
+#include "ecc_common.cuh"
+
+namespace ecc {
+
+int launch_status();
+int sm_count();
+
+__device__ int g_device_error;  // raised by a bounded wait that ran out
+
+namespace tmak {
+
+constexpr int kWarps = 12;          // warps per CTA (384 threads)
+constexpr int kStages = 3;          // ring stages per warp
+constexpr int kTile = 16;
+constexpr int kStageBytes = 3072;
+constexpr int kOffKC = 0, kOffKS = 1024, kOffVC = 1536, kOffVS = 2560;
+constexpr int kThreads = kWarps * 32;
+constexpr int kLutBytes = 65536;
+constexpr float kLn2f = 0.6931471805599453f;
+constexpr long long kWaitCycles = 4000000000ll;
+
+constexpr int kSmLut = 0;
+constexpr int kSmRing = kSmLut + kLutBytes;                        // [kWarps][kStages][3072]
+constexpr int kSmCent = kSmRing + kWarps * kStages * kStageBytes;  // [16] u32
+constexpr int kSmBar = kSmCent + 16 * 4;                           // [kWarps][kStages] u64
+constexpr int kSmBytes = kSmBar + kWarps * kStages * 8;
+static_assert(kSmRing % 1024 == 0 && kStageBytes % 128 == 0, "TMA destinations 128-B aligned");
+static_assert(kSmBar % 8 == 0, "mbarriers 8-B aligned");
+static_assert(kSmBytes <= 227 * 1024, "shared memory budget");
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait by one lane; false when it ran out (the device flag is raised).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    if (mbar_try(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try(bar, parity)) {
+        if (clock64() - t0 > kWaitCycles) {
+            atomicExch(&g_device_error, 1);
+            return false;
+        }
+    }
+    return true;
+}
+__device__ __forceinline__ void tma_4d(uint32_t dst, const CUtensorMap *map, int x, int y, int z, int w,
+                                       uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+        "%5}], [%6];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 r;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(a));
+    return r;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+    uint2 r;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "r"(a));
+    return r;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t r;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(r) : "r"(a));
+    return r;
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+// code-byte table entry: offset v*256 + lane*8 assembled by one prmt.  The
+// table is constant after the kernel's set-up barrier, so the load is not
+// volatile and may be scheduled freely (it depends on `word` anyway).
+__device__ __forceinline__ uint2 lut(uint32_t tab, uint32_t word, int byte_idx, uint32_t lane8) {
+    uint2 r;
+    asm("ld.shared.v2.u32 {%0,%1}, [%2];"
+        : "=r"(r.x), "=r"(r.y)
+        : "r"(tab + __byte_perm(word, lane8, 0x5504u | ((uint32_t)byte_idx << 4))));
+    return r;
+}
+// +-1 pair from bits p and p+16 of w (bit 1 -> +1.0)
+__device__ __forceinline__ uint32_t sign_pair(uint32_t w, int p) {
+    const uint32_t x = w << (15 - p);
+    return (~x & 0x80008000u) | 0x3C003C00u;
+}
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float h_lo(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w & 0xffffu))); }
+__device__ __forceinline__ float h_hi(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
+
+// Consumer lane state for one work item.
+struct Lane {
+    uint32_t qc[8][2], qs[8][2];
+    float qsum[2];
+    float o[8][4];
+    float mrun[2], lrun[2], zrun[2];
+    uint32_t tab, lane8, sel_half;
+    int g, c;
+    float scale_log2;
+
+    // One 16-token tile from shared stage `st`; tokens >= nvalid are masked.
+    __device__ __forceinline__ void tile(uint32_t st, int nvalid) {
+        const uint4 kca = lds128(st + kOffKC + 64 * g + 16 * c);
+        const uint4 kcb = lds128(st + kOffKC + 64 * (g + 8) + 16 * c);
+        const uint32_t ksa = lds32(st + kOffKS + 32 * g + 4 * c);
+        const uint32_t ksb = lds32(st + kOffKS + 32 * (g + 8) + 4 * c);
+        const uint2 kma = lds64(st + kOffKS + 32 * g + 16);
+        const uint2 kmb = lds64(st + kOffKS + 32 * (g + 8) + 16);
+        const bool va = g < nvalid, vb8 = g + 8 < nvalid;
+
+        float sc[4] = {0.f, 0.f, 0.f, 0.f}, ss[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint32_t kwa[4] = {kca.x, kca.y, kca.z, kca.w};
+        const uint32_t kwb[4] = {kcb.x, kcb.y, kcb.z, kcb.w};
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+            const int w = m >> 1, by = 2 * (m & 1);
+            const uint2 a0 = lut(tab, kwa[w], by, lane8);
+            const uint2 a1 = lut(tab, kwb[w], by, lane8);
+            const uint2 a2 = lut(tab, kwa[w], by + 1, lane8);
+            const uint2 a3 = lut(tab, kwb[w], by + 1, lane8);
+            mma16816(sc, a0.x, a1.x, a2.x, a3.x, qc[m][0], qc[m][1]);
+            mma16816(sc, a0.y, a1.y, a2.y, a3.y, qc[m][0], qc[m][1]);
+            mma16816(ss, sign_pair(ksa, 2 * m), sign_pair(ksb, 2 * m), sign_pair(ksa, 2 * m + 1),
+                     sign_pair(ksb, 2 * m + 1), qs[m][0], qs[m][1]);
+        }
+        float s2[4];
+        {
+            const float k_sa = h_lo(kma.x), k_za = h_hi(kma.x), k_aa = h_lo(kma.y);
+            const float k_sb = h_lo(kmb.x), k_zb = h_hi(kmb.x), k_ab = h_lo(kmb.y);
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const float xa = fmaf(k_sa, sc[e], fmaf(k_aa, ss[e], k_za * qsum[e]));
+                const float xb = fmaf(k_sb, sc[2 + e], fmaf(k_ab, ss[2 + e], k_zb * qsum[e]));
+                s2[e] = va ? xa * scale_log2 : -INFINITY;
+                s2[2 + e] = vb8 ? xb * scale_log2 : -INFINITY;
+            }
+        }
+        float corr[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            float mx = fmaxf(s2[e], s2[2 + e]);
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            const float mnew = fmaxf(mrun[e], mx);
+            corr[e] = ex2(mrun[e] - mnew);
+            mrun[e] = mnew;
+        }
+        float p[4];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            p[e] = ex2(s2[e] - mrun[e]);
+            p[2 + e] = ex2(s2[2 + e] - mrun[e]);
+        }
+        if (corr[0] != 1.0f || corr[1] != 1.0f) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                o[i][0] *= corr[0];
+                o[i][1] *= corr[1];
+                o[i][2] *= corr[0];
+                o[i][3] *= corr[1];
+            }
+        }
+        const uint2 vma = lds64(st + kOffVS + 32 * g + 16);
+        const uint2 vmb = lds64(st + kOffVS + 32 * (g + 8) + 16);
+        const float v_sa = h_lo(vma.x), v_za = h_hi(vma.x), v_aa = h_lo(vma.y);
+        const float v_sb = h_lo(vmb.x), v_zb = h_hi(vmb.x), v_ab = h_lo(vmb.y);
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            lrun[e] = fmaf(lrun[e], corr[e], p[e] + p[2 + e]);
+            zrun[e] = fmaf(zrun[e], corr[e], fmaf(p[e], v_za, p[2 + e] * v_zb));
+            pk[e] = pack_h2(p[e] * v_sa, p[e] * v_aa);
+            pk[2 + e] = pack_h2(p[2 + e] * v_sb, p[2 + e] * v_ab);
+        }
+        uint32_t bt[4];
+        {
+            const int srcA = 8 * c + (g >> 1), srcB = srcA + 4;
+            const bool odd = g & 1;
+            const uint32_t x0e = __shfl_sync(0xffffffffu, pk[0], srcA), x0o = __shfl_sync(0xffffffffu, pk[1], srcA);
+            const uint32_t x1e = __shfl_sync(0xffffffffu, pk[0], srcB), x1o = __shfl_sync(0xffffffffu, pk[1], srcB);
+            const uint32_t x2e = __shfl_sync(0xffffffffu, pk[2], srcA), x2o = __shfl_sync(0xffffffffu, pk[3], srcA);
+            const uint32_t x3e = __shfl_sync(0xffffffffu, pk[2], srcB), x3o = __shfl_sync(0xffffffffu, pk[3], srcB);
+            bt[0] = odd ? x0o : x0e;
+            bt[1] = odd ? x1o : x1e;
+            bt[2] = odd ? x2o : x2e;
+            bt[3] = odd ? x3o : x3e;
+        }
+        const uint32_t b1_0 = __byte_perm(bt[0], bt[1], 0x5410), b1_1 = __byte_perm(bt[2], bt[3], 0x5410);
+        const uint32_t b2_0 = __byte_perm(bt[0], bt[1], 0x7632), b2_1 = __byte_perm(bt[2], bt[3], 0x7632);
+
+        // V tokens 2c, 2c+1, 2c+8, 2c+9: code bytes 8g..8g+7, syndrome word g/2
+        uint2 vc[4];
+        uint32_t vs[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int tok = 2 * c + (u & 1) + 8 * (u >> 1);
+            vc[u] = lds64(st + kOffVC + 64 * tok + 8 * g);
+            vs[u] = lds32(st + kOffVS + 32 * tok + 4 * (g >> 1));
+        }
+        const uint32_t sA = __byte_perm(vs[0], vs[1], sel_half), sB = __byte_perm(vs[2], vs[3], sel_half);
+#pragma unroll
+        for (int w = 0; w < 2; ++w) {
+            const uint32_t xa0 = w ? vc[0].y : vc[0].x, xa1 = w ? vc[1].y : vc[1].x;
+            const uint32_t xb0 = w ? vc[2].y : vc[2].x, xb1 = w ? vc[3].y : vc[3].x;
+            constexpr uint32_t kLo = 0x0F0F0F0Fu, kHi = 0xF0F0F0F0u;
+            const uint32_t ia_e = (xa0 & kLo) | ((xa1 << 4) & kHi), ia_o = ((xa0 >> 4) & kLo) | (xa1 & kHi);
+            const uint32_t ib_e = (xb0 & kLo) | ((xb1 << 4) & kHi), ib_o = ((xb0 >> 4) & kLo) | (xb1 & kHi);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int i = 4 * w + k;
+                const uint2 r0 = lut(tab, ia_e, k, lane8);
+                const uint2 r1 = lut(tab, ia_o, k, lane8);
+                const uint2 r2 = lut(tab, ib_e, k, lane8);
+                const uint2 r3 = lut(tab, ib_o, k, lane8);
+                mma16816(o[i], r0.x, r1.x, r2.x, r3.x, b1_0, b1_1);
+                mma16816(o[i], r0.y, r1.y, r2.y, r3.y, b1_0, b1_1);
+                mma16816(o[i], sign_pair(sA, 2 * i), sign_pair(sA, 2 * i + 1), sign_pair(sB, 2 * i),
+                         sign_pair(sB, 2 * i + 1), b2_0, b2_1);
+            }
+        }
+    }
+};
+
+
+// warp that owns global tile t when T tiles are cut into NW equal ranges
+// (range w = [floor(w*T/NW), floor((w+1)*T/NW)))
+__host__ __device__ __forceinline__ int64_t owner_warp(int64_t t, int64_t T, int64_t NW) {
+    return ((t + 1) * NW - 1) / T;
+}
+
+template <int G>
+__global__ void __launch_bounds__(kThreads, 1)
+decode_tma_kernel(const __grid_constant__ CUtensorMap mkc, const __grid_constant__ CUtensorMap mks,
+                  const __grid_constant__ CUtensorMap mvc, const __grid_constant__ CUtensorMap mvs,
+                  const __half *__restrict__ q, float *__restrict__ pm, float *__restrict__ pl,
+                  float *__restrict__ po, int Hq, int Hkv, int64_t seq_len, int64_t tpr, int64_t T, int nslots,
+                  float scale_log2, int flags) {
+    extern __shared__ __align__(1024) uint8_t sm[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t sbase = smem_u32(sm);
+    uint32_t *s_cent = reinterpret_cast<uint32_t *>(sm + kSmCent);
+    const uint32_t ring = sbase + kSmRing + warp * kStages * kStageBytes;
+    const uint32_t bars = sbase + kSmBar + warp * kStages * 8;
+
+    if (threadIdx.x < 16) {
+        const float cv = lm(threadIdx.x);
+        const __half hi = __float2half_rn(cv);
+        const __half lo = __float2half_rn(cv - __half2float(hi));
+        s_cent[threadIdx.x] = (uint32_t)__half_as_ushort(hi) | ((uint32_t)__half_as_ushort(lo) << 16);
+    }
+    if (lane == 0) {
+        for (int s = 0; s < kStages; ++s) mbar_init(bars + 8 * s, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    for (int v = warp; v < 256; v += kWarps) {
+        const uint32_t e0 = s_cent[v & 15], e1 = s_cent[v >> 4];
+        uint2 e;
+        e.x = __byte_perm(e0, e1, 0x5410);
+        e.y = __byte_perm(e0, e1, 0x7632);
+        reinterpret_cast<uint2 *>(sm + kSmLut + v * 256)[lane] = e;
+    }
+    __syncthreads();
+
+    // at most one warp per tile, so that every range is non-empty and the
+    // partial slots of a row have no holes
+    const int64_t NW = min((int64_t)gridDim.x * kWarps, T);
+    const int64_t wid = (int64_t)blockIdx.x * kWarps + warp;
+    if (wid >= NW) return;
+    const int64_t tbeg = wid * T / NW, tend = (wid + 1) * T / NW;
+
+    // issue the four boxes of global tile t into stage s (one lane)
+    auto issue = [&](int64_t t, int s) {
+        const int64_t r = t / tpr;
+        const int tb = (int)((t - r * tpr) * kTile);
+        const int kvh = (int)(r % Hkv), b = (int)(r / Hkv);
+        const uint32_t bar = bars + 8 * s, dst = ring + s * kStageBytes;
+        fence_proxy_async();  // this warp's earlier reads of the stage precede the overwrite
+        mbar_expect_tx(bar, kStageBytes);
+        tma_4d(dst + kOffKC, &mkc, 0, tb, kvh, b, bar);
+        tma_4d(dst + kOffKS, &mks, 64, tb, kvh, b, bar);
+        tma_4d(dst + kOffVC, &mvc, 0, tb, kvh, b, bar);
+        tma_4d(dst + kOffVS, &mvs, 64, tb, kvh, b, bar);
+    };
+    const int64_t ntiles = tend - tbeg;
+    if (lane == 0)
+        for (int s = 0; s < kStages && s < ntiles; ++s) issue(tbeg + s, s);
+
+    Lane L;
+    L.g = lane >> 2;
+    L.c = lane & 3;
+    L.lane8 = (uint32_t)lane * 8u;
+    L.tab = sbase + kSmLut;
+    L.sel_half = (L.g & 1) ? 0x7632u : 0x5410u;
+    L.scale_log2 = scale_log2;
+    bool ok = true;
+    int64_t j = 0;  // tile index within this warp's range
+    while (j < ntiles) {
+        // ---------------- new row segment ----------------
+        const int64_t t0 = tbeg + j;
+        const int64_t r = t0 / tpr;
+        const int64_t seg_end = min(tend, (r + 1) * tpr);
+        const int kvh = (int)(r % Hkv), b = (int)(r / Hkv);
+        const int h0 = kvh * G;
+        {
+            // lane (g, c) holds dims 32c..32c+31 of query head g of the group
+            float x[32];
+            if (L.g < G) {
+                const uint4 *src = reinterpret_cast<const uint4 *>(q + ((int64_t)b * Hq + h0 + L.g) * kD + 32 * L.c);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const uint4 u = __ldg(src + k);
+                    const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                    for (int m = 0; m < 4; ++m) {
+                        x[8 * k + 2 * m] = h_lo(wv[m]);
+                        x[8 * k + 2 * m + 1] = h_hi(wv[m]);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int k = 0; k < 32; ++k) x[k] = 0.0f;
+            }
+            if (flags & ECC_DECODE_ROTATE_Q) {  // q_rot = fp16(WHT(q)), like patch.py:106
+#pragma unroll
+                for (int s = 1; s < 32; s <<= 1)
+#pragma unroll
+                    for (int k = 0; k < 32; ++k)
+                        if ((k & s) == 0) {
+                            const float a = x[k], bb = x[k + s];
+                            x[k] = __fadd_rn(a, bb);
+                            x[k + s] = __fsub_rn(a, bb);
+                        }
+#pragma unroll
+                for (int s = 1; s <= 2; s <<= 1) {  // strides 32, 64: partner lane c ^ s
+                    const float sgn = (L.c & s) ? -1.0f : 1.0f;
+#pragma unroll
+                    for (int k = 0; k < 32; ++k) {
+                        const float p = __shfl_xor_sync(0xffffffffu, x[k], s);
+                        x[k] = __fmaf_rn(sgn, x[k], p);
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < 32; ++k) {
+                    const float v = x[k];
+                    const float q0 = __fmul_rn(v, kInvSqrt128);
+                    const float rem = __fmaf_rn(-q0, kSqrt128, v);
+                    x[k] = __half2float(__float2half_rn(__fmaf_rn(rem, kInvSqrt128, q0)));
+                }
+            }
+#pragma unroll
+            for (int m = 0; m < 8; ++m) {
+                L.qc[m][0] = pack_h2(x[4 * m], x[4 * m + 1]);
+                L.qc[m][1] = pack_h2(x[4 * m + 2], x[4 * m + 3]);
+                L.qs[m][0] = pack_h2(x[2 * m], x[2 * m + 16]);
+                L.qs[m][1] = pack_h2(x[2 * m + 1], x[2 * m + 17]);
+            }
+            float sum = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 32; ++k) sum += x[k];
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            L.qsum[0] = __shfl_sync(0xffffffffu, sum, 4 * (2 * L.c));       // head 2c
+            L.qsum[1] = __shfl_sync(0xffffffffu, sum, 4 * (2 * L.c + 1));   // head 2c+1
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) L.o[i][k] = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            L.mrun[e] = -INFINITY;
+            L.lrun[e] = 0.0f;
+            L.zrun[e] = 0.0f;
+        }
+        // ---------------- tiles of the segment ----------------
+        for (; tbeg + j < seg_end; ++j) {
+            const int64_t t = tbeg + j;
+            const int s = (int)(j % kStages);
+            bool ready = true;
+            if (lane == 0) ready = ok && mbar_wait(bars + 8 * s, (uint32_t)((j / kStages) & 1));
+            ready = __shfl_sync(0xffffffffu, ready, 0);  // also orders the warp after lane 0's wait
+            ok = ok && ready;
+            if (ok) {
+                const int64_t tok0 = (t - r * tpr) * kTile;
+                L.tile(ring + s * kStageBytes, (int)min((int64_t)kTile, seq_len - tok0));
+            }
+            __syncwarp();
+            if (lane == 0 && ok && j + kStages < ntiles) issue(tbeg + j + kStages, s);
+        }
+        // ---------------- partial of the segment ----------------
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+#pragma unroll
+            for (int off = 4; off < 32; off <<= 1) {
+                L.lrun[e] += __shfl_xor_sync(0xffffffffu, L.lrun[e], off);
+                L.zrun[e] += __shfl_xor_sync(0xffffffffu, L.zrun[e], off);
+            }
+        }
+        const int64_t slot = wid - owner_warp(r * tpr, T, NW);
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int h = 2 * L.c + e;
+            if (h >= G) continue;
+            const int64_t pr = ((int64_t)b * Hq + h0 + h) * nslots;
+            float *pod = po + (pr + slot) * kD;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int d0 = 16 * L.g + 2 * i;
+                pod[d0] = L.o[i][e] + L.zrun[e];
+                pod[d0 + 1] = L.o[i][2 + e] + L.zrun[e];
+            }
+            if (L.g == 0) {
+                pm[pr + slot] = (L.mrun[e] == -INFINITY) ? -INFINITY : L.mrun[e] * kLn2f;
+                pl[pr + slot] = L.lrun[e];
+                if (seg_end == (r + 1) * tpr) {  // last segment of the row: the rest are empty
+                    for (int64_t k = slot + 1; k < nslots; ++k) {
+                        pm[pr + k] = -INFINITY;
+                        pl[pr + k] = 0.0f;
+                    }
+                }
+            }
+        }
+    }
+    if (!ok && lane == 0) {
+        // drain the copies still in flight before the warp exits
+        for (int64_t k = max((int64_t)0, j); k < min(ntiles, j + kStages); ++k) {
+            const uint32_t bar = bars + 8 * (int)(k % kStages);
+            const long long c0 = clock64();
+            while (!mbar_try(bar, (uint32_t)((k / kStages) & 1)) && clock64() - c0 < kWaitCycles) {
+            }
+        }
+    }
+}
+
+// ---- host ----
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+static std::mutex g_encode_mu;
+
+static int get_encode() {
+    std::lock_guard<std::mutex> lk(g_encode_mu);
+    if (!g_encode) {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult qr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qr) != cudaSuccess ||
+            qr != cudaDriverEntryPointSuccess || !fn)
+            return ECC_ERR_CUDA;
+        g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    return ECC_OK;
+}
+
+// 4-D map over a block pool: (byte in block, token, kv head, batch).
+static int make_map(CUtensorMap *m, const void *base, int64_t seq_len, int Hkv, int B, int64_t bs_h, int64_t bs_b,
+                    uint32_t box_x) {
+    cuuint64_t dims[4] = {128, (cuuint64_t)seq_len, (cuuint64_t)Hkv, (cuuint64_t)B};
+    cuuint64_t sh = (cuuint64_t)bs_h * 128, sb = (cuuint64_t)bs_b * 128;
+    if (Hkv == 1) sh = (cuuint64_t)seq_len * 128;  // stride of an extent-1 dim is unused
+    if (B == 1) sb = sh * (cuuint64_t)Hkv;
+    cuuint64_t strides[3] = {128, sh, sb};
+    cuuint32_t box[4] = {box_x, (cuuint32_t)kTile, 1, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void *>(base), dims, strides, box,
+                                estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? ECC_OK : ECC_ERR_CUDA;
+}
+
+template <int G>
+static int launch_g(const CUtensorMap &kc, const CUtensorMap &ks, const CUtensorMap &vc, const CUtensorMap &vs,
+                    const void *q, float *pm, float *pl, float *po, int Hq, int Hkv, int64_t seq_len, int64_t tpr,
+                    int64_t T, int grid, int ns, float scale_log2, int flags, cudaStream_t s) {
+    static bool configured[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        if (cudaFuncSetAttribute(decode_tma_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmBytes) !=
+            cudaSuccess)
+            return ECC_ERR_CUDA;
+        configured[dev] = true;
+    }
+    decode_tma_kernel<G><<<grid, kThreads, kSmBytes, s>>>(kc, ks, vc, vs, reinterpret_cast<const __half *>(q), pm,
+                                                         pl, po, Hq, Hkv, seq_len, tpr, T, ns, scale_log2, flags);
+    return launch_status();
+}
+
+// Grid and partial-slot count of the balanced tile partition for a shape.
+struct Plan {
+    int grid;
+    int64_t tpr, T;
+    int nslots;
+};
+static Plan make_plan(int B, int Hkv, int64_t seq_len) {
+    Plan p;
+    p.tpr = (std::max<int64_t>(seq_len, 1) + kTile - 1) / kTile;
+    const int64_t rows = (int64_t)B * Hkv;
+    p.T = rows * p.tpr;
+    p.grid = (int)std::max<int64_t>(1, std::min<int64_t>(sm_count(), (p.T + kWarps - 1) / kWarps));
+    const int64_t NW = std::min<int64_t>((int64_t)p.grid * kWarps, p.T);
+    int64_t mx = 1;
+    for (int64_t r = 0; r < rows; ++r) {
+        const int64_t n = owner_warp(r * p.tpr + p.tpr - 1, p.T, NW) - owner_warp(r * p.tpr, p.T, NW) + 1;
+        mx = std::max(mx, n);
+    }
+    p.nslots = (int)mx;
+    return p;
+}
+
+}  // namespace tmak
+
+// Partial slots per (b, query head) of the balanced partition: the split
+// count ecc_decode uses by default.
+int tma_default_splits(int B, int Hkv, int64_t seq_len) { return tmak::make_plan(B, Hkv, seq_len).nslots; }
+
+// Returns ECC_OK when launched, a positive value when the shape is not one the
+// TMA kernel handles (the caller then uses another kernel), or an error.
+int launch_decode_tma(const void *q, const void *kb, const void *vb, int64_t bs_b, int64_t bs_h, float *pm,
+                      float *pl, float *po, int B, int Hq, int Hkv, int64_t seq_len, int64_t chunk, int ns,
+                      float scale_log2, int flags, cudaStream_t s) {
+    using namespace tmak;
+    (void)chunk;
+    const int G = Hq / Hkv;
+    if (G < 1 || G > 8 || seq_len < 1 || seq_len > 0x7fffffffll) return 1;
+    if (((uintptr_t)kb % 16) || ((uintptr_t)vb % 16) || ((uintptr_t)q % 16)) return 1;
+    const Plan plan = make_plan(B, Hkv, seq_len);
+    if (plan.nslots != ns) return 1;  // the caller asked for another split count
+    if (get_encode() != ECC_OK) return 1;
+    CUtensorMap kc, ks, vc, vs;
+    if (make_map(&kc, kb, seq_len, Hkv, B, bs_h, bs_b, 64) != ECC_OK ||
+        make_map(&ks, kb, seq_len, Hkv, B, bs_h, bs_b, 32) != ECC_OK ||
+        make_map(&vc, vb, seq_len, Hkv, B, bs_h, bs_b, 64) != ECC_OK ||
+        make_map(&vs, vb, seq_len, Hkv, B, bs_h, bs_b, 32) != ECC_OK)
+        return 1;
+    switch (G) {
+#define ECC_TMA_CASE(N) \
+    case N: return launch_g<N>(kc, ks, vc, vs, q, pm, pl, po, Hq, Hkv, seq_len, plan.tpr, plan.T, plan.grid, ns, scale_log2, flags, s);
+        ECC_TMA_CASE(1) ECC_TMA_CASE(2) ECC_TMA_CASE(3) ECC_TMA_CASE(4)
+        ECC_TMA_CASE(5) ECC_TMA_CASE(6) ECC_TMA_CASE(7)
+        default: return launch_g<8>(kc, ks, vc, vs, q, pm, pl, po, Hq, Hkv, seq_len, plan.tpr, plan.T, plan.grid, ns,
+                                    scale_log2, flags, s);
+#undef ECC_TMA_CASE
+    }
+}
+
+}  // namespace ecc
+
+extern "C" int ecc_device_status(int reset) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, ecc::g_device_error, sizeof(int)) != cudaSuccess) return ECC_ERR_CUDA;
+    if (reset) {
+        const int z = 0;
+        if (cudaMemcpyToSymbol(ecc::g_device_error, &z, sizeof(int)) != cudaSuccess) return ECC_ERR_CUDA;
+    }
+    return v;
+}

@@ -36,6 +36,8 @@ library_path = os.path.join(_HERE, _LIB_NAME)
 ROTATE_Q = 1
 UNROTATE_OUT = 2
 CUDA_CORES = 4
+REGISTER_PATH = 8
+_KERNEL_FLAGS = {"auto": 0, "tma": 0, "register": REGISTER_PATH, "cuda_cores": CUDA_CORES}
 D = 128
 BLOCK_BYTES = 128
 
@@ -66,6 +68,7 @@ def _load():
         "ecc_decode_default_splits": ([i32, i32, i64], i32),
         "ecc_decode_partials": ([p, p, p, i64, i64, p, p, p, i32, i32, i32, i64, f32, i32, i32, p], i32),
         "ecc_lse_merge": ([p, p, p, i64, i32, p, i32, p], i32),
+        "ecc_device_status": ([i32], i32),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -304,14 +307,18 @@ def _query(q: torch.Tensor):
 def decode_attention(query: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, seq_len: int,
                      sm_scale: float | None = None, rotate_q: bool = False, unrotate_out: bool = False,
                      num_splits: int = 0, out: torch.Tensor | None = None,
-                     workspace: torch.Tensor | None = None, cuda_cores: bool = False) -> torch.Tensor:
+                     workspace: torch.Tensor | None = None, cuda_cores: bool = False,
+                     kernel: str = "auto") -> torch.Tensor:
     """One decode step of GQA attention over block pools [B, Hkv, Lcap, 128].
 
     query [B, Hq, 1, 128] (or [B, Hq, 128]) fp16 -> [B, Hq, 1, 128] fp16.
     Query head h reads kv head h // (Hq // Hkv).  ``sm_scale`` defaults to
-    1/sqrt(128) (custom_kv/fused_decode.py:57).  ``cuda_cores`` selects the
-    CUDA-core kernel (always used for more than 8 query heads per kv head)
-    instead of the tensor-core one."""
+    1/sqrt(128) (custom_kv/fused_decode.py:57).  ``kernel`` picks the
+    implementation: "auto"/"tma" (TMA-fed warp-specialised tensor-core kernel,
+    falling back to "register" for pool layouts a tensor map cannot describe),
+    "register" (tensor cores with per-lane global loads) or "cuda_cores"
+    (always used for more than 8 query heads per kv head); ``cuda_cores=True``
+    is a shorthand for the last."""
     q3 = _query(query)
     kbs = _pool_strides(k_pool, "k_pool")
     vbs = _pool_strides(v_pool, "v_pool")
@@ -330,6 +337,7 @@ def decode_attention(query: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Te
     elif not out.is_contiguous() or out.dtype != torch.float16 or out.numel() != B * hq * D:
         raise RuntimeError("out must be a contiguous float16 tensor of B*Hq*128 elements")
     flags = (ROTATE_Q if rotate_q else 0) | (UNROTATE_OUT if unrotate_out else 0) | (CUDA_CORES if cuda_cores else 0)
+    flags |= _KERNEL_FLAGS[kernel]
     scale = float(sm_scale) if sm_scale is not None else 0.0
     need = decode_workspace_size(B, hq, hkv, seq_len, num_splits)
     with torch.cuda.device(q3.device):
@@ -344,7 +352,7 @@ def decode_attention(query: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Te
 
 def decode_partials(query: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, seq_len: int,
                     num_splits: int, sm_scale: float | None = None, rotate_q: bool = False,
-                    cuda_cores: bool = False):
+                    cuda_cores: bool = False, kernel: str = "auto"):
     """Split partials (m, l, o) of one decode step over token positions
     [0, seq_len) of the pools: m, l [B, Hq, num_splits] fp32 (m in natural-log
     units), o [B, Hq, num_splits, 128] fp32 unnormalised."""
@@ -365,8 +373,8 @@ def decode_partials(query: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Ten
         rc = _lib.ecc_decode_partials(_ptr(q3), _ptr(k_pool), _ptr(v_pool), kbs[0], kbs[1], _ptr(pm), _ptr(pl),
                                       _ptr(po), B, hq, hkv, int(seq_len),
                                       float(sm_scale) if sm_scale is not None else 0.0,
-                                      (ROTATE_Q if rotate_q else 0) | (CUDA_CORES if cuda_cores else 0),
-                                      int(num_splits), _stream(q3))
+                                      (ROTATE_Q if rotate_q else 0) | (CUDA_CORES if cuda_cores else 0)
+                                      | _KERNEL_FLAGS[kernel], int(num_splits), _stream(q3))
     _check(rc, "decode_partials")
     return pm, pl, po
 
@@ -394,3 +402,12 @@ def lse_merge(pm: torch.Tensor, pl: torch.Tensor, po: torch.Tensor, unrotate_out
 
 def version() -> int:
     return int(_lib.ecc_version())
+
+
+def device_status(reset: bool = False) -> int:
+    """1 if a kernel on the current device gave up a bounded wait since the
+    last reset (it returned early instead of hanging), else 0."""
+    rc = int(_lib.ecc_device_status(1 if reset else 0))
+    if rc < 0:
+        _check(rc, "device_status")
+    return rc

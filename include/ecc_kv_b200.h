@@ -43,12 +43,20 @@ enum {
 #define ECC_DECODE_UNROTATE_OUT 2 /* apply the WHT to the output (values stored rotated) */
 #define ECC_DECODE_CUDA_CORES 4   /* use the CUDA-core kernel instead of the tensor-core one
                                      (groups of more than 8 query heads always use it) */
+#define ECC_DECODE_REGISTER_PATH 8 /* tensor-core kernel with per-lane global loads instead of the
+                                      TMA-fed warp-specialised one (used automatically when a
+                                      pool layout cannot be described by a tensor map) */
 
 /* Name of an error code (static string). */
 const char *ecc_strerror(int code);
 
 /* Library version, e.g. 100 for 0.1.0. */
 int ecc_version(void);
+
+/* 1 if a kernel of this library on the current device ran out of a bounded
+ * wait (and returned early instead of hanging) since the last reset, else 0;
+ * reset != 0 clears the flag.  Synchronous. */
+int ecc_device_status(int reset);
 
 /* ---- WHT ------------------------------------------------------------------
  * In-place normalised Walsh-Hadamard transform of n rows of length d (power
