@@ -51,6 +51,7 @@ constexpr int kLutBytes = 65536;
 constexpr float kLn2f = 0.6931471805599453f;
 constexpr long long kWaitCycles = 4000000000ll;
 
+constexpr int kSmemReserve = 1024;  // shared-window offset of dynamic shared memory
 constexpr int kSmLut = 0;
 constexpr int kSmRing = kSmLut + kLutBytes;                        // [kWarps][kStages][3072]
 constexpr int kSmCent = kSmRing + kWarps * kStages * kStageBytes;  // [16] u32
@@ -131,13 +132,17 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
     return *reinterpret_cast<uint32_t *>(&h);
 }
 // code-byte table entry: offset v*256 + lane*8 assembled by one prmt.  The
-// table is constant after the kernel's set-up barrier, so the load is not
-// volatile and may be scheduled freely (it depends on `word` anyway).
-__device__ __forceinline__ uint2 lut(uint32_t tab, uint32_t word, int byte_idx, uint32_t lane8) {
+// table sits at the start of the dynamic shared memory, whose shared-window
+// address is the per-block reserve kSmemReserve (checked on the host against
+// cudaDevAttrReservedSharedMemoryPerBlock and again by the kernel), so the
+// base folds into the load's immediate offset.  The table is constant after
+// the kernel's set-up barrier, so the load is not volatile and may be
+// scheduled freely (it depends on `word` anyway).
+__device__ __forceinline__ uint2 lut(uint32_t word, int byte_idx, uint32_t lane8) {
     uint2 r;
-    asm("ld.shared.v2.u32 {%0,%1}, [%2];"
+    asm("ld.shared.v2.u32 {%0,%1}, [%2+%3];"
         : "=r"(r.x), "=r"(r.y)
-        : "r"(tab + __byte_perm(word, lane8, 0x5504u | ((uint32_t)byte_idx << 4))));
+        : "r"(__byte_perm(word, lane8, 0x5504u | ((uint32_t)byte_idx << 4))), "n"(kSmemReserve + kSmLut));
     return r;
 }
 // +-1 pair from bits p and p+16 of w (bit 1 -> +1.0)
@@ -153,13 +158,36 @@ __device__ __forceinline__ float ex2(float x) {
 __device__ __forceinline__ float h_lo(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w & 0xffffu))); }
 __device__ __forceinline__ float h_hi(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
 
-// Consumer lane state for one work item.
+// Sign bit p of both fp16 halves of x kept in place: each half is 0 or the
+// fp16 value whose only set bit is p (p <= 14), a power of two sign_weight(p).
+// Bit 15 is the fp16 sign bit, so that one moves to bit 14 first.
+__device__ __forceinline__ uint32_t sign_bits(uint32_t x, int p) {
+    return p == 15 ? ((x >> 1) & 0x40004000u) : (x & (0x00010001u << p));
+}
+// 1 / (value of the fp16 with only bit p set), bit 15 taken as bit 14
+__host__ __device__ constexpr float sign_unweight(int p) {
+    return p == 15 ? 0.5f
+         : p == 14 ? 0.5f
+         : p == 13 ? 128.0f
+         : p == 12 ? 2048.0f
+         : p == 11 ? 8192.0f
+         : p == 10 ? 16384.0f
+                   : (float)(1u << (24 - p));  // subnormal 2^(p-24)
+}
+
+// Consumer lane state for one work item.  For groups of at most 4 query heads
+// the PV products use the idle columns 4..7 of the n8 operand for the V sign
+// term: lanes g < 4 of the P operand carry p * vscale of head g (columns
+// 0..3, centroid products), lanes g >= 4 carry 2 p * valpha of head g - 4
+// (columns 4..7, sign-bit products with the bits masked in place, so each
+// accumulator row has one power-of-two weight, removed at the end).
+template <int G>
 struct Lane {
     uint32_t qc[8][2], qs[8][2];
     float qsum[2];
-    float o[8][4];
+    float o[16][4];  // PV accumulators, one per dim of the lane's 16 (rows g: hi + sign, g+8: lo)
     float mrun[2], lrun[2], zrun[2];
-    uint32_t tab, lane8, sel_half;
+    uint32_t lane8, sel_half;
     int g, c;
     float scale_log2;
 
@@ -173,21 +201,26 @@ struct Lane {
         const uint2 kmb = lds64(st + kOffKS + 32 * (g + 8) + 16);
         const bool va = g < nvalid, vb8 = g + 8 < nvalid;
 
-        float sc[4] = {0.f, 0.f, 0.f, 0.f}, ss[4] = {0.f, 0.f, 0.f, 0.f};
+        // Centroid products: rows g / g+8 of the A operand carry the fp16 hi /
+        // lo parts of one token's centroids, so each table entry (hi, lo)
+        // lands in the operand registers as loaded; one product per 8 tokens.
+        float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f}, ss[4] = {0.f, 0.f, 0.f, 0.f};
         const uint32_t kwa[4] = {kca.x, kca.y, kca.z, kca.w};
         const uint32_t kwb[4] = {kcb.x, kcb.y, kcb.z, kcb.w};
 #pragma unroll
         for (int m = 0; m < 8; ++m) {
             const int w = m >> 1, by = 2 * (m & 1);
-            const uint2 a0 = lut(tab, kwa[w], by, lane8);
-            const uint2 a1 = lut(tab, kwb[w], by, lane8);
-            const uint2 a2 = lut(tab, kwa[w], by + 1, lane8);
-            const uint2 a3 = lut(tab, kwb[w], by + 1, lane8);
-            mma16816(sc, a0.x, a1.x, a2.x, a3.x, qc[m][0], qc[m][1]);
-            mma16816(sc, a0.y, a1.y, a2.y, a3.y, qc[m][0], qc[m][1]);
+            const uint2 xa = lut(kwa[w], by, lane8);      // token g, k slots 2c, 2c+1
+            const uint2 ya = lut(kwa[w], by + 1, lane8);  // token g, k slots 2c+8, 2c+9
+            const uint2 xb = lut(kwb[w], by, lane8);      // token g+8
+            const uint2 yb = lut(kwb[w], by + 1, lane8);
+            mma16816(sa, xa.x, xa.y, ya.x, ya.y, qc[m][0], qc[m][1]);
+            mma16816(sb, xb.x, xb.y, yb.x, yb.y, qc[m][0], qc[m][1]);
             mma16816(ss, sign_pair(ksa, 2 * m), sign_pair(ksb, 2 * m), sign_pair(ksa, 2 * m + 1),
                      sign_pair(ksb, 2 * m + 1), qs[m][0], qs[m][1]);
         }
+        // q.C of token g (head 2c+e) = hi row + lo row
+        const float sc[4] = {sa[0] + sa[2], sa[1] + sa[3], sb[0] + sb[2], sb[1] + sb[3]};
         float s2[4];
         {
             const float k_sa = h_lo(kma.x), k_za = h_hi(kma.x), k_aa = h_lo(kma.y);
@@ -219,7 +252,7 @@ struct Lane {
         }
         if (corr[0] != 1.0f || corr[1] != 1.0f) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
+            for (int i = 0; i < 16; ++i) {
                 o[i][0] *= corr[0];
                 o[i][1] *= corr[1];
                 o[i][2] *= corr[0];
@@ -231,16 +264,24 @@ struct Lane {
         const float v_sa = h_lo(vma.x), v_za = h_hi(vma.x), v_aa = h_lo(vma.y);
         const float v_sb = h_lo(vmb.x), v_zb = h_hi(vmb.x), v_ab = h_lo(vmb.y);
         uint32_t pk[4];
+        constexpr bool kSplitCols = G <= 4;
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
             lrun[e] = fmaf(lrun[e], corr[e], p[e] + p[2 + e]);
-            zrun[e] = fmaf(zrun[e], corr[e], fmaf(p[e], v_za, p[2 + e] * v_zb));
-            pk[e] = pack_h2(p[e] * v_sa, p[e] * v_aa);
-            pk[2 + e] = pack_h2(p[2 + e] * v_sb, p[2 + e] * v_ab);
+            if constexpr (kSplitCols) {
+                // sign s = 2b - 1: the -valpha part joins the zero point
+                zrun[e] = fmaf(zrun[e], corr[e], fmaf(p[e], v_za - v_aa, p[2 + e] * (v_zb - v_ab)));
+                pk[e] = pack_h2(p[e] * v_sa, 2.0f * (p[e] * v_aa));
+                pk[2 + e] = pack_h2(p[2 + e] * v_sb, 2.0f * (p[2 + e] * v_ab));
+            } else {
+                zrun[e] = fmaf(zrun[e], corr[e], fmaf(p[e], v_za, p[2 + e] * v_zb));
+                pk[e] = pack_h2(p[e] * v_sa, p[e] * v_aa);
+                pk[2 + e] = pack_h2(p[2 + e] * v_sb, p[2 + e] * v_ab);
+            }
         }
         uint32_t bt[4];
         {
-            const int srcA = 8 * c + (g >> 1), srcB = srcA + 4;
+            const int srcA = 8 * c + ((kSplitCols ? (g & 3) : g) >> 1), srcB = srcA + 4;
             const bool odd = g & 1;
             const uint32_t x0e = __shfl_sync(0xffffffffu, pk[0], srcA), x0o = __shfl_sync(0xffffffffu, pk[1], srcA);
             const uint32_t x1e = __shfl_sync(0xffffffffu, pk[0], srcB), x1o = __shfl_sync(0xffffffffu, pk[1], srcB);
@@ -251,8 +292,21 @@ struct Lane {
             bt[2] = odd ? x2o : x2e;
             bt[3] = odd ? x3o : x3e;
         }
-        const uint32_t b1_0 = __byte_perm(bt[0], bt[1], 0x5410), b1_1 = __byte_perm(bt[2], bt[3], 0x5410);
-        const uint32_t b2_0 = __byte_perm(bt[0], bt[1], 0x7632), b2_1 = __byte_perm(bt[2], bt[3], 0x7632);
+        uint32_t b1_0, b1_1, b2_0, b2_1;
+        if constexpr (kSplitCols) {
+            const bool cent = g < 4;
+            const uint32_t sel = cent ? 0x5410u : 0x7632u;
+            const uint32_t y0 = __byte_perm(bt[0], bt[1], sel), y1 = __byte_perm(bt[2], bt[3], sel);
+            b1_0 = cent ? y0 : 0u;
+            b1_1 = cent ? y1 : 0u;
+            b2_0 = cent ? 0u : y0;
+            b2_1 = cent ? 0u : y1;
+        } else {
+            b1_0 = __byte_perm(bt[0], bt[1], 0x5410);
+            b1_1 = __byte_perm(bt[2], bt[3], 0x5410);
+            b2_0 = __byte_perm(bt[0], bt[1], 0x7632);
+            b2_1 = __byte_perm(bt[2], bt[3], 0x7632);
+        }
 
         // V tokens 2c, 2c+1, 2c+8, 2c+9: code bytes 8g..8g+7, syndrome word g/2
         uint2 vc[4];
@@ -273,15 +327,26 @@ struct Lane {
             const uint32_t ib_e = (xb0 & kLo) | ((xb1 << 4) & kHi), ib_o = ((xb0 >> 4) & kLo) | (xb1 & kHi);
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
+                // dims 16g + 2i (even) and 16g + 2i + 1 (odd); accumulator 2i
+                // (2i+1) holds the even (odd) dim: rows g the fp16 hi part and
+                // the sign term, rows g+8 the lo part
                 const int i = 4 * w + k;
-                const uint2 r0 = lut(tab, ia_e, k, lane8);
-                const uint2 r1 = lut(tab, ia_o, k, lane8);
-                const uint2 r2 = lut(tab, ib_e, k, lane8);
-                const uint2 r3 = lut(tab, ib_o, k, lane8);
-                mma16816(o[i], r0.x, r1.x, r2.x, r3.x, b1_0, b1_1);
-                mma16816(o[i], r0.y, r1.y, r2.y, r3.y, b1_0, b1_1);
-                mma16816(o[i], sign_pair(sA, 2 * i), sign_pair(sA, 2 * i + 1), sign_pair(sB, 2 * i),
-                         sign_pair(sB, 2 * i + 1), b2_0, b2_1);
+                const uint2 r0 = lut(ia_e, k, lane8);  // even dim, tokens 2c, 2c+1
+                const uint2 r2 = lut(ib_e, k, lane8);  // even dim, tokens 2c+8, 2c+9
+                const uint2 r1 = lut(ia_o, k, lane8);  // odd dim
+                const uint2 r3 = lut(ib_o, k, lane8);
+                mma16816(o[2 * i], r0.x, r0.y, r2.x, r2.y, b1_0, b1_1);
+                mma16816(o[2 * i + 1], r1.x, r1.y, r3.x, r3.y, b1_0, b1_1);
+                if constexpr (kSplitCols) {
+                    // columns 4..7 of accumulator 2i: rows g the even dim's
+                    // sign term, rows g+8 the odd dim's
+                    mma16816(o[2 * i], sign_bits(sA, 2 * i), sign_bits(sA, 2 * i + 1), sign_bits(sB, 2 * i),
+                             sign_bits(sB, 2 * i + 1), b2_0, b2_1);
+                } else {
+                    mma16816(o[2 * i], sign_pair(sA, 2 * i), 0u, sign_pair(sB, 2 * i), 0u, b2_0, b2_1);
+                    mma16816(o[2 * i + 1], sign_pair(sA, 2 * i + 1), 0u, sign_pair(sB, 2 * i + 1), 0u, b2_0,
+                             b2_1);
+                }
             }
         }
     }
@@ -299,11 +364,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 decode_tma_kernel(const __grid_constant__ CUtensorMap mkc, const __grid_constant__ CUtensorMap mks,
                   const __grid_constant__ CUtensorMap mvc, const __grid_constant__ CUtensorMap mvs,
                   const __half *__restrict__ q, float *__restrict__ pm, float *__restrict__ pl,
-                  float *__restrict__ po, int Hq, int Hkv, int64_t seq_len, int64_t tpr, int64_t T, int nslots,
+                  float *__restrict__ po, int Hq, int Hkv, int64_t seq_len, int tpr, int64_t T, int nslots,
                   float scale_log2, int flags) {
     extern __shared__ __align__(1024) uint8_t sm[];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // broadcast from lane 0 so that the compiler treats the warp index, and
+    // the tile cursors derived from it, as warp-uniform values
+    const int warp = __shfl_sync(0xffffffffu, (int)(threadIdx.x >> 5), 0), lane = threadIdx.x & 31;
     const uint32_t sbase = smem_u32(sm);
+    if (sbase != (uint32_t)kSmemReserve) {  // the table loads assume this base
+        if (threadIdx.x == 0) atomicExch(&g_device_error, 2);
+        return;
+    }
     uint32_t *s_cent = reinterpret_cast<uint32_t *>(sm + kSmCent);
     const uint32_t ring = sbase + kSmRing + warp * kStages * kStageBytes;
     const uint32_t bars = sbase + kSmBar + warp * kStages * 8;
@@ -333,46 +404,69 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap mkc, const __grid_constant
     const int64_t NW = min((int64_t)gridDim.x * kWarps, T);
     const int64_t wid = (int64_t)blockIdx.x * kWarps + warp;
     if (wid >= NW) return;
-    const int64_t tbeg = wid * T / NW, tend = (wid + 1) * T / NW;
+    const int64_t tbeg = wid * T / NW;
+    const int ntiles = (int)((wid + 1) * T / NW - tbeg);
+    const int row_tok = tpr * kTile;  // tokens of a row rounded up to whole tiles
 
-    // issue the four boxes of global tile t into stage s (one lane)
-    auto issue = [&](int64_t t, int s) {
-        const int64_t r = t / tpr;
-        const int tb = (int)((t - r * tpr) * kTile);
-        const int kvh = (int)(r % Hkv), b = (int)(r / Hkv);
-        const uint32_t bar = bars + 8 * s, dst = ring + s * kStageBytes;
-        fence_proxy_async();  // this warp's earlier reads of the stage precede the overwrite
-        mbar_expect_tx(bar, kStageBytes);
-        tma_4d(dst + kOffKC, &mkc, 0, tb, kvh, b, bar);
-        tma_4d(dst + kOffKS, &mks, 64, tb, kvh, b, bar);
-        tma_4d(dst + kOffVC, &mvc, 0, tb, kvh, b, bar);
-        tma_4d(dst + kOffVS, &mvs, 64, tb, kvh, b, bar);
+    // Producer cursor: (token base, kv head, batch) of the next tile to issue.
+    // Kept by every lane (uniform arithmetic, no divisions per tile); lane 0
+    // issues.
+    int p_tb, p_kvh, p_b;
+    {
+        const int64_t r0 = tbeg / tpr;
+        p_tb = (int)(tbeg - r0 * tpr) * kTile;
+        p_kvh = (int)(r0 % Hkv);
+        p_b = (int)(r0 / Hkv);
+    }
+    auto issue_next = [&](int s) {
+        if (lane == 0) {
+            const uint32_t bar = bars + 8 * s, dst = ring + s * kStageBytes;
+            fence_proxy_async();  // this warp's earlier reads of the stage precede the overwrite
+            mbar_expect_tx(bar, kStageBytes);
+            tma_4d(dst + kOffKC, &mkc, 0, p_tb, p_kvh, p_b, bar);
+            tma_4d(dst + kOffKS, &mks, 64, p_tb, p_kvh, p_b, bar);
+            tma_4d(dst + kOffVC, &mvc, 0, p_tb, p_kvh, p_b, bar);
+            tma_4d(dst + kOffVS, &mvs, 64, p_tb, p_kvh, p_b, bar);
+        }
+        p_tb += kTile;
+        if (p_tb >= row_tok) {
+            p_tb = 0;
+            if (++p_kvh == Hkv) {
+                p_kvh = 0;
+                ++p_b;
+            }
+        }
     };
-    const int64_t ntiles = tend - tbeg;
-    if (lane == 0)
-        for (int s = 0; s < kStages && s < ntiles; ++s) issue(tbeg + s, s);
+    for (int s = 0; s < kStages && s < ntiles; ++s) issue_next(s);
 
-    Lane L;
+    Lane<G> L;
     L.g = lane >> 2;
     L.c = lane & 3;
     L.lane8 = (uint32_t)lane * 8u;
-    L.tab = sbase + kSmLut;
     L.sel_half = (L.g & 1) ? 0x7632u : 0x5410u;
     L.scale_log2 = scale_log2;
     bool ok = true;
-    int64_t j = 0;  // tile index within this warp's range
+    int jfail = -1;        // first tile whose wait ran out
+    int j = 0;             // tiles of this warp's range consumed so far
+    int stage = 0;         // ring stage of tile j
+    uint32_t phase = 0;    // mbarrier parity of tile j
+    int64_t r = tbeg / tpr;                  // row of tile j
+    int tok0 = (int)(tbeg - r * tpr) * kTile;  // first token of tile j within its row
     while (j < ntiles) {
         // ---------------- new row segment ----------------
-        const int64_t t0 = tbeg + j;
-        const int64_t r = t0 / tpr;
-        const int64_t seg_end = min(tend, (r + 1) * tpr);
+        const int seg_tiles = min(ntiles - j, (row_tok - tok0) / kTile);
+        const bool row_ends = (tok0 + seg_tiles * kTile == row_tok);
         const int kvh = (int)(r % Hkv), b = (int)(r / Hkv);
         const int h0 = kvh * G;
         {
-            // lane (g, c) holds dims 32c..32c+31 of query head g of the group
+            // lane (g, c) holds dims 32c..32c+31 of query head g of the group;
+            // with the split columns (G <= 4) lanes g >= 4 repeat head g - 4,
+            // so that the softmax state of columns 4..7 (the V sign products)
+            // is that of the head they belong to
             float x[32];
-            if (L.g < G) {
-                const uint4 *src = reinterpret_cast<const uint4 *>(q + ((int64_t)b * Hq + h0 + L.g) * kD + 32 * L.c);
+            const int qh = (G <= 4) ? (L.g & 3) : L.g;
+            if (qh < G) {
+                const uint4 *src = reinterpret_cast<const uint4 *>(q + ((int64_t)b * Hq + h0 + qh) * kD + 32 * L.c);
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
                     const uint4 u = __ldg(src + k);
@@ -430,7 +524,7 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap mkc, const __grid_constant
             L.qsum[1] = __shfl_sync(0xffffffffu, sum, 4 * (2 * L.c + 1));   // head 2c+1
         }
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+        for (int i = 0; i < 16; ++i)
 #pragma unroll
             for (int k = 0; k < 4; ++k) L.o[i][k] = 0.0f;
 #pragma unroll
@@ -440,19 +534,22 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap mkc, const __grid_constant
             L.zrun[e] = 0.0f;
         }
         // ---------------- tiles of the segment ----------------
-        for (; tbeg + j < seg_end; ++j) {
-            const int64_t t = tbeg + j;
-            const int s = (int)(j % kStages);
+        for (int u = 0; u < seg_tiles; ++u) {
             bool ready = true;
-            if (lane == 0) ready = ok && mbar_wait(bars + 8 * s, (uint32_t)((j / kStages) & 1));
-            ready = __shfl_sync(0xffffffffu, ready, 0);  // also orders the warp after lane 0's wait
+            if (lane == 0) ready = ok && mbar_wait(bars + 8 * stage, phase);
+            ready = __shfl_sync(0xffffffffu, ready, 0);
+            __syncwarp();  // orders the warp's reads of the stage after lane 0's wait
+            if (ok && !ready) jfail = j;
             ok = ok && ready;
-            if (ok) {
-                const int64_t tok0 = (t - r * tpr) * kTile;
-                L.tile(ring + s * kStageBytes, (int)min((int64_t)kTile, seq_len - tok0));
-            }
+            if (ok) L.tile(ring + stage * kStageBytes, (int)min((int64_t)kTile, seq_len - tok0));
             __syncwarp();
-            if (lane == 0 && ok && j + kStages < ntiles) issue(tbeg + j + kStages, s);
+            if (ok && j + kStages < ntiles) issue_next(stage);
+            ++j;
+            tok0 += kTile;
+            if (++stage == kStages) {
+                stage = 0;
+                phase ^= 1u;
+            }
         }
         // ---------------- partial of the segment ----------------
 #pragma unroll
@@ -463,35 +560,55 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap mkc, const __grid_constant
                 L.zrun[e] += __shfl_xor_sync(0xffffffffu, L.zrun[e], off);
             }
         }
-        const int64_t slot = wid - owner_warp(r * tpr, T, NW);
+        const int slot = (int)(wid - owner_warp(r * tpr, T, NW));
+        const int64_t prow = ((int64_t)b * Hq + h0) * nslots + slot;  // partial of head h0 of the group
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            // sign terms of dims 16g + 2i, +1: from lane c + 2 (columns
+            // 4..7) when the group uses the split columns, else already in
+            // the accumulators
+            float sg[4] = {0.f, 0.f, 0.f, 0.f};
+            if constexpr (G <= 4) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    sg[k] = __shfl_down_sync(0xffffffffu, L.o[2 * i][k], 2) * sign_unweight(k < 2 ? 2 * i : 2 * i + 1);
+            }
+            const int d0 = 16 * L.g + 2 * i;
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int h = 2 * L.c + e;
+                if (h >= G) continue;
+                float *pod = po + (prow + (int64_t)h * nslots) * kD;
+                pod[d0] = (L.o[2 * i][e] + L.o[2 * i][2 + e]) + (sg[e] + L.zrun[e]);
+                pod[d0 + 1] = (L.o[2 * i + 1][e] + L.o[2 * i + 1][2 + e]) + (sg[2 + e] + L.zrun[e]);
+            }
+        }
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
             const int h = 2 * L.c + e;
             if (h >= G) continue;
             const int64_t pr = ((int64_t)b * Hq + h0 + h) * nslots;
-            float *pod = po + (pr + slot) * kD;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int d0 = 16 * L.g + 2 * i;
-                pod[d0] = L.o[i][e] + L.zrun[e];
-                pod[d0 + 1] = L.o[i][2 + e] + L.zrun[e];
-            }
             if (L.g == 0) {
                 pm[pr + slot] = (L.mrun[e] == -INFINITY) ? -INFINITY : L.mrun[e] * kLn2f;
                 pl[pr + slot] = L.lrun[e];
-                if (seg_end == (r + 1) * tpr) {  // last segment of the row: the rest are empty
-                    for (int64_t k = slot + 1; k < nslots; ++k) {
+                if (row_ends) {  // last segment of the row: the rest are empty
+                    for (int k = slot + 1; k < nslots; ++k) {
                         pm[pr + k] = -INFINITY;
                         pl[pr + k] = 0.0f;
                     }
                 }
             }
         }
+        if (row_ends) {
+            ++r;
+            tok0 = 0;
+        }
     }
     if (!ok && lane == 0) {
-        // drain the copies still in flight before the warp exits
-        for (int64_t k = max((int64_t)0, j); k < min(ntiles, j + kStages); ++k) {
-            const uint32_t bar = bars + 8 * (int)(k % kStages);
+        // drain the copies still in flight before the warp exits: tiles
+        // jfail .. min(ntiles, jfail + kStages) - 1 were issued and not consumed
+        for (int k = jfail; k < min(ntiles, jfail + kStages); ++k) {
+            const uint32_t bar = bars + 8 * (k % kStages);
             const long long c0 = clock64();
             while (!mbar_try(bar, (uint32_t)((k / kStages) & 1)) && clock64() - c0 < kWaitCycles) {
             }
@@ -534,7 +651,7 @@ static int make_map(CUtensorMap *m, const void *base, int64_t seq_len, int Hkv, 
 
 template <int G>
 static int launch_g(const CUtensorMap &kc, const CUtensorMap &ks, const CUtensorMap &vc, const CUtensorMap &vs,
-                    const void *q, float *pm, float *pl, float *po, int Hq, int Hkv, int64_t seq_len, int64_t tpr,
+                    const void *q, float *pm, float *pl, float *po, int Hq, int Hkv, int64_t seq_len, int tpr,
                     int64_t T, int grid, int ns, float scale_log2, int flags, cudaStream_t s) {
     static bool configured[64] = {false};
     int dev = 0;
@@ -548,6 +665,20 @@ static int launch_g(const CUtensorMap &kc, const CUtensorMap &ks, const CUtensor
     decode_tma_kernel<G><<<grid, kThreads, kSmBytes, s>>>(kc, ks, vc, vs, reinterpret_cast<const __half *>(q), pm,
                                                          pl, po, Hq, Hkv, seq_len, tpr, T, ns, scale_log2, flags);
     return launch_status();
+}
+
+// The table loads address shared memory with kSmemReserve folded in; the
+// driver reports that reserve per device.
+static bool reserve_matches() {
+    static int known[64];  // 0 unknown, 1 matches, 2 differs
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+    if (!known[dev]) {
+        int v = -1;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrReservedSharedMemoryPerBlock, dev) != cudaSuccess) return false;
+        known[dev] = (v == kSmemReserve) ? 1 : 2;
+    }
+    return known[dev] == 1;
 }
 
 // Grid and partial-slot count of the balanced tile partition for a shape.
@@ -586,10 +717,11 @@ int launch_decode_tma(const void *q, const void *kb, const void *vb, int64_t bs_
     using namespace tmak;
     (void)chunk;
     const int G = Hq / Hkv;
-    if (G < 1 || G > 8 || seq_len < 1 || seq_len > 0x7fffffffll) return 1;
+    if (G < 1 || G > 8 || seq_len < 1 || seq_len > (1ll << 30)) return 1;
     if (((uintptr_t)kb % 16) || ((uintptr_t)vb % 16) || ((uintptr_t)q % 16)) return 1;
     const Plan plan = make_plan(B, Hkv, seq_len);
     if (plan.nslots != ns) return 1;  // the caller asked for another split count
+    if (!reserve_matches()) return 1;
     if (get_encode() != ECC_OK) return 1;
     CUtensorMap kc, ks, vc, vs;
     if (make_map(&kc, kb, seq_len, Hkv, B, bs_h, bs_b, 64) != ECC_OK ||
@@ -599,10 +731,10 @@ int launch_decode_tma(const void *q, const void *kb, const void *vb, int64_t bs_
         return 1;
     switch (G) {
 #define ECC_TMA_CASE(N) \
-    case N: return launch_g<N>(kc, ks, vc, vs, q, pm, pl, po, Hq, Hkv, seq_len, plan.tpr, plan.T, plan.grid, ns, scale_log2, flags, s);
+    case N: return launch_g<N>(kc, ks, vc, vs, q, pm, pl, po, Hq, Hkv, seq_len, (int)plan.tpr, plan.T, plan.grid, ns, scale_log2, flags, s);
         ECC_TMA_CASE(1) ECC_TMA_CASE(2) ECC_TMA_CASE(3) ECC_TMA_CASE(4)
         ECC_TMA_CASE(5) ECC_TMA_CASE(6) ECC_TMA_CASE(7)
-        default: return launch_g<8>(kc, ks, vc, vs, q, pm, pl, po, Hq, Hkv, seq_len, plan.tpr, plan.T, plan.grid, ns,
+        default: return launch_g<8>(kc, ks, vc, vs, q, pm, pl, po, Hq, Hkv, seq_len, (int)plan.tpr, plan.T, plan.grid, ns,
                                     scale_log2, flags, s);
 #undef ECC_TMA_CASE
     }
