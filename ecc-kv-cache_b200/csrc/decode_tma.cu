@@ -200,6 +200,17 @@ struct Lane {
         const uint2 kma = lds64(st + kOffKS + 32 * g + 16);
         const uint2 kmb = lds64(st + kOffKS + 32 * (g + 8) + 16);
         const bool va = g < nvalid, vb8 = g + 8 < nvalid;
+        // V tokens 2c, 2c+1, 2c+8, 2c+9: code bytes 8g..8g+7, syndrome word g/2
+        uint2 vc[4];
+        uint32_t vs[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int tok = 2 * c + (u & 1) + 8 * (u >> 1);
+            vc[u] = lds64(st + kOffVC + 64 * tok + 8 * g);
+            vs[u] = lds32(st + kOffVS + 32 * tok + 4 * (g >> 1));
+        }
+        const uint2 vma = lds64(st + kOffVS + 32 * g + 16);
+        const uint2 vmb = lds64(st + kOffVS + 32 * (g + 8) + 16);
 
         // Centroid products: rows g / g+8 of the A operand carry the fp16 hi /
         // lo parts of one token's centroids, so each table entry (hi, lo)
@@ -259,8 +270,6 @@ struct Lane {
                 o[i][3] *= corr[1];
             }
         }
-        const uint2 vma = lds64(st + kOffVS + 32 * g + 16);
-        const uint2 vmb = lds64(st + kOffVS + 32 * (g + 8) + 16);
         const float v_sa = h_lo(vma.x), v_za = h_hi(vma.x), v_aa = h_lo(vma.y);
         const float v_sb = h_lo(vmb.x), v_zb = h_hi(vmb.x), v_ab = h_lo(vmb.y);
         uint32_t pk[4];
@@ -308,15 +317,6 @@ struct Lane {
             b2_1 = __byte_perm(bt[2], bt[3], 0x7632);
         }
 
-        // V tokens 2c, 2c+1, 2c+8, 2c+9: code bytes 8g..8g+7, syndrome word g/2
-        uint2 vc[4];
-        uint32_t vs[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int tok = 2 * c + (u & 1) + 8 * (u >> 1);
-            vc[u] = lds64(st + kOffVC + 64 * tok + 8 * g);
-            vs[u] = lds32(st + kOffVS + 32 * tok + 4 * (g >> 1));
-        }
         const uint32_t sA = __byte_perm(vs[0], vs[1], sel_half), sB = __byte_perm(vs[2], vs[3], sel_half);
 #pragma unroll
         for (int w = 0; w < 2; ++w) {
