@@ -216,8 +216,160 @@ __device__ __noinline__ int exact_code(float d, float scale) {
     return best;
 }
 
+// One warp's kVecPerWarp vectors of tile `tile`.  The fast pass (kExact =
+// false) gives up and returns false, before writing anything, when any of the
+// warp's elements needs the exact treatment (a quotient within kBand of a
+// decision threshold, or a std near an fp32 rounding midpoint); the exact
+// pass handles those elements one by one.  Keeping the exact code out of the
+// fast pass keeps the hot loop small.
+template <bool kRotate, bool kExact>
+__device__ __forceinline__ bool compress_warp(const __half *__restrict__ x, int64_t xs_b, int64_t xs_h, int64_t xs_l,
+                                              uint8_t *__restrict__ blocks, int64_t bs_b, int64_t bs_h,
+                                              FastDiv div_h, FastDiv div_l, uint32_t n_vec, uint32_t tile,
+                                              const QEntry *tab, uint32_t *st) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane & 3, vsub = lane >> 2, base = lane & ~3;
+    const uint32_t vi = tile * kVecPerTile + warp * kVecPerWarp + vsub;
+    const bool valid = vi < n_vec;
+    const uint32_t row = fdiv(valid ? vi : 0u, div_l);
+    const int64_t l = (valid ? vi : 0u) - row * div_l.d;
+    const uint32_t bq = fdiv(row, div_h);
+    const int64_t b = bq, h = row - bq * div_h.d;
+
+    float v[4][8];
+    {
+        const __half *src = x + b * xs_b + h * xs_h + l * xs_l + 8 * g;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            uint4 raw = make_uint4(0, 0, 0, 0);
+            if (valid) raw = __ldcs(reinterpret_cast<const uint4 *>(src + 32 * c));
+            float2 f;
+            f = h2_to_f2(raw.x); v[c][0] = f.x; v[c][1] = f.y;
+            f = h2_to_f2(raw.y); v[c][2] = f.x; v[c][3] = f.y;
+            f = h2_to_f2(raw.z); v[c][4] = f.x; v[c][5] = f.y;
+            f = h2_to_f2(raw.w); v[c][6] = f.x; v[c][7] = f.y;
+        }
+    }
+    if (kRotate) wht_group(v, g);
+
+    // mean (zero point), ops_cpu.py:72
+    const float zero = __fmul_rn(tsum_group(v, base), 0.0078125f);
+
+    // unbiased std, ops_cpu.py:73
+    const double md = (double)zero;
+    double acc = 0.0;
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const double dx = (double)v[c][i] - md;
+            acc = fma(dx, dx, acc);
+        }
+    acc += __shfl_xor_sync(kFull, acc, 1);
+    acc += __shfl_xor_sync(kFull, acc, 2);
+    double sd = __dsqrt_rn(__ddiv_rn(acc, 127.0));
+    float s32 = __double2float_rn(sd);
+    {
+        const double lo = (double)s32;
+        const double nb = (double)(lo <= sd ? nextafterf(s32, INFINITY) : nextafterf(s32, 0.0f));
+        const double mid = 0.5 * (lo + nb);
+        const bool amb = fabs(sd - mid) <= 1e-12 * sd;
+        if (!kExact && __any_sync(kFull, amb)) return false;  // rare: the exact pass re-sums
+        if (kExact && __any_sync(kFull, amb)) {  // re-sum in element order
+            double ex = 0.0;
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+#pragma unroll 1
+                for (int gg = 0; gg < 4; ++gg)
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float xv = __shfl_sync(kFull, v[c][i], base + gg);
+                        const double dx = __dsub_rn((double)xv, md);
+                        ex = __dadd_rn(ex, __dmul_rn(dx, dx));
+                    }
+            if (amb) {
+                sd = __dsqrt_rn(__ddiv_rn(ex, 127.0));
+                s32 = __double2float_rn(sd);
+            }
+        }
+    }
+    const float scale = __double2float_rn(__dadd_rn((double)s32, 1e-8));
+    const float rs = __frcp_rn(scale);
+
+    // quantise, residual, syndrome
+    uint32_t codes[4] = {0u, 0u, 0u, 0u};
+    uint32_t bits = 0u;
+    bool band = false;  // an element lies within kBand of a decision threshold
+    const QEntry *mytab = tab + (lane & (kReplicas - 1));
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float xv = v[c][i];
+            const float d = __fsub_rn(xv, zero);
+            const float u = __fmul_rn(d, rs);
+            const unsigned cell = min((unsigned)cell_of(u), (unsigned)(kCells - 1));
+            const QEntry e = mytab[cell * kReplicas];
+            const bool hi = u > e.thr;
+            float cq = hi ? e.c_hi : e.c_lo;
+            int q = e.q_lo + (hi ? 1 : 0);
+            if constexpr (kExact) {
+                if (fabsf(__fsub_rn(u, e.thr)) < kBand) {
+                    q = exact_code(d, scale);
+                    cq = lm(0);
+#pragma unroll
+                    for (int k = 1; k < 16; ++k) cq = (q == k) ? lm(k) : cq;
+                }
+            } else {
+                band = band || (fabsf(__fsub_rn(u, e.thr)) < kBand);
+            }
+            const float kt = __fadd_rn(__fmul_rn(cq, scale), zero);
+            const float eps = __fsub_rn(xv, kt);
+            bits |= (eps >= 0.0f ? 1u : 0u) << (8 * c + i);
+            codes[c] |= (uint32_t)q << (4 * i);
+            v[c][i] = fabsf(eps);
+        }
+    if (!kExact && __any_sync(kFull, band)) return false;  // the exact pass redoes the warp's vectors
+    const float alpha = __fmul_rn(tsum_group(v, base), 0.0078125f);
+
+    // stage: code word 4c+g and syndrome byte 4c+g of this vector
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        st[4 * c + g] = codes[c];
+        reinterpret_cast<uint8_t *>(st + 16)[4 * c + g] = (uint8_t)(bits >> (8 * c));
+    }
+    __syncwarp();
+    if (valid) {
+        uint8_t *dst = blocks + (b * bs_b + h * bs_h + l) * kBlockBytes;
+        const uint4 w0 = *reinterpret_cast<const uint4 *>(st + 4 * g);
+        uint4 w1;
+        if (g == 0) {
+            w1 = *reinterpret_cast<const uint4 *>(st + 16);
+        } else if (g == 1) {
+            const uint32_t hs = __half_as_ushort(__float2half_rn(scale));
+            const uint32_t hz = __half_as_ushort(__float2half_rn(zero));
+            const uint32_t ha = __half_as_ushort(__float2half_rn(alpha));
+            w1 = make_uint4(hs | (hz << 16), ha, 0u, 0u);
+        } else {
+            w1 = make_uint4(0u, 0u, 0u, 0u);
+        }
+        __stcs(reinterpret_cast<uint4 *>(dst + 16 * g), w0);
+        __stcs(reinterpret_cast<uint4 *>(dst + 64 + 16 * g), w1);
+    }
+    __syncwarp();
+    return true;
+}
+
 template <bool kRotate>
-__global__ void __launch_bounds__(kCompressWarps * 32)
+__device__ __noinline__ void compress_warp_exact(const __half *__restrict__ x, int64_t xs_b, int64_t xs_h,
+                                                 int64_t xs_l, uint8_t *__restrict__ blocks, int64_t bs_b,
+                                                 int64_t bs_h, FastDiv div_h, FastDiv div_l, uint32_t n_vec,
+                                                 uint32_t tile, const QEntry *tab, uint32_t *st) {
+    compress_warp<kRotate, true>(x, xs_b, xs_h, xs_l, blocks, bs_b, bs_h, div_h, div_l, n_vec, tile, tab, st);
+}
+
+template <bool kRotate>
+__global__ void __launch_bounds__(kCompressWarps * 32, 3)
 compress_kernel(const __half *__restrict__ x, int64_t xs_b, int64_t xs_h, int64_t xs_l,
                 uint8_t *__restrict__ blocks, int64_t bs_b, int64_t bs_h, FastDiv div_h, FastDiv div_l,
                 uint32_t n_vec) {
@@ -227,132 +379,13 @@ compress_kernel(const __half *__restrict__ x, int64_t xs_b, int64_t xs_h, int64_
     __syncthreads();
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int g = lane & 3, vsub = lane >> 2, base = lane & ~3;
-    uint32_t *st = stage[warp][vsub];
+    uint32_t *st = stage[warp][lane >> 2];
     const uint32_t n_tiles = (n_vec + kVecPerTile - 1) / kVecPerTile;
-
     for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-        const uint32_t vi = tile * kVecPerTile + warp * kVecPerWarp + vsub;
-        const bool valid = vi < n_vec;
-        const uint32_t row = fdiv(valid ? vi : 0u, div_l);
-        const int64_t l = (valid ? vi : 0u) - row * div_l.d;
-        const uint32_t bq = fdiv(row, div_h);
-        const int64_t b = bq, h = row - bq * div_h.d;
-
-        float v[4][8];
-        {
-            const __half *src = x + b * xs_b + h * xs_h + l * xs_l + 8 * g;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                uint4 raw = make_uint4(0, 0, 0, 0);
-                if (valid) raw = __ldcs(reinterpret_cast<const uint4 *>(src + 32 * c));
-                float2 f;
-                f = h2_to_f2(raw.x); v[c][0] = f.x; v[c][1] = f.y;
-                f = h2_to_f2(raw.y); v[c][2] = f.x; v[c][3] = f.y;
-                f = h2_to_f2(raw.z); v[c][4] = f.x; v[c][5] = f.y;
-                f = h2_to_f2(raw.w); v[c][6] = f.x; v[c][7] = f.y;
-            }
-        }
-        if (kRotate) wht_group(v, g);
-
-        // mean (zero point), ops_cpu.py:72
-        const float zero = __fmul_rn(tsum_group(v, base), 0.0078125f);
-
-        // unbiased std, ops_cpu.py:73
-        const double md = (double)zero;
-        double acc = 0.0;
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const double dx = (double)v[c][i] - md;
-                acc = fma(dx, dx, acc);
-            }
-        acc += __shfl_xor_sync(kFull, acc, 1);
-        acc += __shfl_xor_sync(kFull, acc, 2);
-        double sd = __dsqrt_rn(__ddiv_rn(acc, 127.0));
-        float s32 = __double2float_rn(sd);
-        {
-            const double lo = (double)s32;
-            const double nb = (double)(lo <= sd ? nextafterf(s32, INFINITY) : nextafterf(s32, 0.0f));
-            const double mid = 0.5 * (lo + nb);
-            const bool amb = fabs(sd - mid) <= 1e-12 * sd;
-            if (__any_sync(kFull, amb)) {  // rare: re-sum in element order
-                double ex = 0.0;
-#pragma unroll
-                for (int c = 0; c < 4; ++c)
-#pragma unroll 1
-                    for (int gg = 0; gg < 4; ++gg)
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const float xv = __shfl_sync(kFull, v[c][i], base + gg);
-                            const double dx = __dsub_rn((double)xv, md);
-                            ex = __dadd_rn(ex, __dmul_rn(dx, dx));
-                        }
-                if (amb) {
-                    sd = __dsqrt_rn(__ddiv_rn(ex, 127.0));
-                    s32 = __double2float_rn(sd);
-                }
-            }
-        }
-        const float scale = __double2float_rn(__dadd_rn((double)s32, 1e-8));
-        const float rs = __frcp_rn(scale);
-
-        // quantise, residual, syndrome
-        uint32_t codes[4] = {0u, 0u, 0u, 0u};
-        uint32_t bits = 0u;
-        const QEntry *mytab = tab + (lane & (kReplicas - 1));
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float xv = v[c][i];
-                const float d = __fsub_rn(xv, zero);
-                const float u = __fmul_rn(d, rs);
-                const unsigned cell = min((unsigned)cell_of(u), (unsigned)(kCells - 1));
-                const QEntry e = mytab[cell * kReplicas];
-                const bool hi = u > e.thr;
-                float cq = hi ? e.c_hi : e.c_lo;
-                int q = e.q_lo + (hi ? 1 : 0);
-                if (fabsf(__fsub_rn(u, e.thr)) < kBand) {
-                    q = exact_code(d, scale);
-                    cq = lm(0);
-#pragma unroll
-                    for (int k = 1; k < 16; ++k) cq = (q == k) ? lm(k) : cq;
-                }
-                const float kt = __fadd_rn(__fmul_rn(cq, scale), zero);
-                const float eps = __fsub_rn(xv, kt);
-                bits |= (eps >= 0.0f ? 1u : 0u) << (8 * c + i);
-                codes[c] |= (uint32_t)q << (4 * i);
-                v[c][i] = fabsf(eps);
-            }
-        const float alpha = __fmul_rn(tsum_group(v, base), 0.0078125f);
-
-        // stage: code word 4c+g and syndrome byte 4c+g of this vector
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            st[4 * c + g] = codes[c];
-            reinterpret_cast<uint8_t *>(st + 16)[4 * c + g] = (uint8_t)(bits >> (8 * c));
-        }
-        __syncwarp();
-        if (valid) {
-            uint8_t *dst = blocks + (b * bs_b + h * bs_h + l) * kBlockBytes;
-            const uint4 w0 = *reinterpret_cast<const uint4 *>(st + 4 * g);
-            uint4 w1;
-            if (g == 0) {
-                w1 = *reinterpret_cast<const uint4 *>(st + 16);
-            } else if (g == 1) {
-                const uint32_t hs = __half_as_ushort(__float2half_rn(scale));
-                const uint32_t hz = __half_as_ushort(__float2half_rn(zero));
-                const uint32_t ha = __half_as_ushort(__float2half_rn(alpha));
-                w1 = make_uint4(hs | (hz << 16), ha, 0u, 0u);
-            } else {
-                w1 = make_uint4(0u, 0u, 0u, 0u);
-            }
-            __stcs(reinterpret_cast<uint4 *>(dst + 16 * g), w0);
-            __stcs(reinterpret_cast<uint4 *>(dst + 64 + 16 * g), w1);
-        }
-        __syncwarp();
+        if (!compress_warp<kRotate, false>(x, xs_b, xs_h, xs_l, blocks, bs_b, bs_h, div_h, div_l, n_vec, tile, tab,
+                                           st))
+            compress_warp_exact<kRotate>(x, xs_b, xs_h, xs_l, blocks, bs_b, bs_h, div_h, div_l, n_vec, tile, tab,
+                                         st);
     }
 }
 
