@@ -42,6 +42,15 @@ B, HQ, HKV, D, CTX = 8, 32, 8, 128, 65536
 BLOCK = 128
 COMPRESS_TOKENS = 131072
 
+# DRAM bytes per unit measured with ncu (dram__bytes_read.sum +
+# dram__bytes_write.sum of one launch divided by the units it processed), see
+# profiles/decode_tma_b8_hq32_hkv8_ctx64k.md and profiles/compress_8x131072.md.
+# Decode: per (token, kv head), algorithmic 256 B.  Compress: per vector,
+# algorithmic 384 B; the output blocks of a launch partly stay in the 126 MB L2
+# when the launch ends, so DRAM writes are counted below 128 B per vector.
+DECODE_DRAM_BYTES_PER_UNIT = (1.074092e9 + 4.958208e6) / (B * HKV * 65542)
+COMPRESS_DRAM_BYTES_PER_VECTOR = (268.526080e6 + 97.954304e6) / (HKV * COMPRESS_TOKENS)
+
 
 def peaks():
     try:
@@ -110,6 +119,52 @@ def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
 
 
+def compress_bench(ops, workloads, dev, stream, K, peak, peak_kind):
+    """Compress throughput: 8 KV heads x 131072 tokens of heavy-tailed fp16,
+    K then V, each one launch of 1 048 576 vectors into a block pool."""
+    import torch
+    ck, cv = workloads.make_c2(seed=0, L=COMPRESS_TOKENS, device=dev)
+    cpool_k = torch.empty((1, HKV, COMPRESS_TOKENS, BLOCK), dtype=torch.uint8, device=dev)
+    cpool_v = torch.empty_like(cpool_k)
+    for _ in range(3):
+        ops.compress_into(ck, cpool_k, rotate=True)
+        ops.compress_into(cv, cpool_v, rotate=True)
+    reps = max(5, min(50, K))
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    torch.cuda.synchronize()
+    for a, b in evs:
+        a.record(stream)
+        ops.compress_into(ck, cpool_k, rotate=True)
+        ops.compress_into(cv, cpool_v, rotate=True)
+        b.record(stream)
+    torch.cuda.synchronize()
+    cms = [a.elapsed_time(b) for a, b in evs]
+    c_avg = sum(cms) / len(cms)
+    n_vec = 2 * HKV * COMPRESS_TOKENS
+    cbytes = n_vec * (2 * D + BLOCK)
+    c_gbs = cbytes / (c_avg / 1e3) / 1e9
+    return {"workload": "compress 8 KV heads x 131072 tokens, K and V, fp16 N(0,1) + Student-t(3) on 3% of "
+                        "channels -> 128-B blocks",
+            "tok_s": HKV * COMPRESS_TOKENS / (c_avg / 1e3), "vectors_per_s": n_vec / (c_avg / 1e3),
+            "ms_per_pass": c_avg, "gbs": c_gbs,
+            "roofline": {"bound": "hbm", "achieved": c_gbs, "peak": peak, "unit": "GB/s",
+                         "frac": c_gbs / peak,
+                         "traffic": COMPRESS_DRAM_BYTES_PER_VECTOR * HKV * COMPRESS_TOKENS,
+                         "note": f"per launch of {HKV * COMPRESS_TOKENS} vectors: 384 B per vector (256 B fp16 "
+                                 f"in + 128 B block out); traffic from ncu; peak {peak_kind}"}}
+
+
+def run_compress_only(args):
+    import torch
+    import custom_ecc_cuda as ops
+    import workloads
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peak, peak_kind = peaks()
+    comp = compress_bench(ops, workloads, dev, torch.cuda.current_stream(dev), args.steps, peak, peak_kind)
+    print(json.dumps({"compress": comp}), flush=True)
+
+
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
@@ -146,8 +201,11 @@ def run_ours(args):
     new_v = torch.randn((n_steps, B, HKV, 1, D), generator=gen, device=dev).half()
     qs = torch.stack([workloads.make_queries(i, B, HQ, device=dev) for i in range(n_steps)])
     out = torch.empty((B, HQ, 1, D), dtype=torch.float16, device=dev)
-    splits = ops.default_splits(B, HKV, CTX)
-    nspl = splits
+    # one rank: the library's default split count (the TMA kernel's balanced
+    # partition for each step's length); sharded: a fixed count that covers
+    # the partition of every length the run reaches
+    splits = 0
+    nspl = max(ops.default_splits(B, HKV, s) for s in (CTX, CTX + (cap - CTX) // 2, cap)) + 1
     stream = torch.cuda.current_stream(dev)
 
     if world > 1:
@@ -265,33 +323,7 @@ def run_ours(args):
     if world == 1 and not args.skip_compress:
         del kpool, vpool
         torch.cuda.empty_cache()
-        ck, cv = workloads.make_c2(seed=0, L=COMPRESS_TOKENS, device=dev)
-        cpool_k = torch.empty((1, HKV, COMPRESS_TOKENS, BLOCK), dtype=torch.uint8, device=dev)
-        cpool_v = torch.empty_like(cpool_k)
-        for _ in range(3):
-            ops.compress_into(ck, cpool_k, rotate=True)
-            ops.compress_into(cv, cpool_v, rotate=True)
-        reps = max(5, min(50, K))
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
-        barrier()
-        for a, b in evs:
-            a.record(stream)
-            ops.compress_into(ck, cpool_k, rotate=True)
-            ops.compress_into(cv, cpool_v, rotate=True)
-            b.record(stream)
-        barrier()
-        cms = [a.elapsed_time(b) for a, b in evs]
-        c_avg = sum(cms) / len(cms)
-        n_vec = 2 * HKV * COMPRESS_TOKENS
-        cbytes = n_vec * (2 * D + BLOCK)
-        c_gbs = cbytes / (c_avg / 1e3) / 1e9
-        comp = {"workload": "compress 8 KV heads x 131072 tokens, K and V, fp16 N(0,1) + Student-t(3) on 3% of "
-                            "channels -> 128-B blocks",
-                "tok_s": HKV * COMPRESS_TOKENS / (c_avg / 1e3), "vectors_per_s": n_vec / (c_avg / 1e3),
-                "ms_per_pass": c_avg, "gbs": c_gbs,
-                "roofline": {"bound": "hbm", "achieved": c_gbs, "peak": peak, "unit": "GB/s",
-                             "frac": c_gbs / peak, "traffic": None,
-                             "note": f"384 B per vector (256 B fp16 in + 128 B block out); peak {peak_kind}"}}
+        comp = compress_bench(ops, workloads, dev, stream, K, peak, peak_kind)
 
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:
@@ -305,13 +337,15 @@ def run_ours(args):
             "config": {"workload": f"decode step: B{B} Hq{HQ}/Hkv{HKV} D{D}, {CTX}-token compressed context "
                                    f"per rank growing 1 token/step, append + fused decode",
                        "batch": B, "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "context_per_rank": CTX,
-                       "parallelism": "seq-chunk" if world > 1 else "single", "num_splits": splits,
+                       "parallelism": "seq-chunk" if world > 1 else "single",
+                       "num_splits": nspl if world > 1 else "default (balanced tile partition)",
                        "l2": "inputs 1.07 GB/rank > L2 (no flush needed)"},
             "decode_tok_s": tok_s, "pct_peak": value / world / peak,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": args.traffic,
-                         "note": f"decode (split partials + merge) per launch: 256 B per (token, kv head), "
-                                 f"{B * HKV} (b, kv head) rows x mean {mean_ctx:.0f} tokens; peak {peak_kind}"},
+                         "frac": achieved / peak, "traffic": DECODE_DRAM_BYTES_PER_UNIT * B * HKV * mean_ctx,
+                         "note": f"decode (split partials + merge) per step: 256 B per (token, kv head), "
+                                 f"{B * HKV} (b, kv head) rows x mean {mean_ctx:.0f} tokens; traffic from ncu "
+                                 f"(per launch of the decode kernel); peak {peak_kind}"},
             "gpu_launches": K * (4 if (world == 1 or rank == world - 1) else 2),
             "clocks": clocks, "e2e": e2e, "compress": comp, "cpu_baseline": cpu,
         }
@@ -341,19 +375,24 @@ def _cpu_sample(tokens: int, seed: int = 0):
     return ecc_oracle, np, q, kb, vb
 
 
-def cpu_baseline(tokens: int):
+def cpu_baseline(tokens: int, min_seconds: float = 10.0):
     """Oracle decode (cpu_reference_decode restated in C, GQA) on one batch
-    row x 8 KV heads x `tokens` tokens, all host threads."""
+    row x 8 KV heads x `tokens` tokens with all host threads, repeated until
+    at least `min_seconds` of CPU work has been timed."""
     orc, np, q, kb, vb = _cpu_sample(tokens)
     threads = len(os.sched_getaffinity(0))
     orc.decode(q, kb[:, :, :64], vb[:, :, :64], hkv=HKV, seq_len=64, threads=threads)
-    t0 = time.perf_counter()
-    orc.decode(q, kb, vb, hkv=HKV, seq_len=tokens, rotate_q=True, unrotate_out=True, threads=threads)
-    dt = time.perf_counter() - t0
-    gbs = HKV * tokens * 2 * BLOCK / dt / 1e9
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        orc.decode(q, kb, vb, hkv=HKV, seq_len=tokens, rotate_q=True, unrotate_out=True, threads=threads)
+        reps += 1
+        dt = time.perf_counter() - t0
+        if dt >= min_seconds and reps >= 2:
+            break
+    gbs = HKV * tokens * 2 * BLOCK * reps / dt / 1e9
     return {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
             "sample": f"oracle decode (C port of cpu_reference_decode) of 1 batch row x {HQ} q heads / {HKV} kv "
-                      f"heads x {tokens} tokens ({dt:.2f} s)"}
+                      f"heads x {tokens} tokens, {reps} times ({dt:.1f} s)"}
 
 
 def run_reference(args):
@@ -390,16 +429,18 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--cpu-tokens", type=int, default=8192)
+    ap.add_argument("--cpu-tokens", type=int, default=CTX)
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-compress", action="store_true")
-    ap.add_argument("--traffic", type=float, default=None,
-                    help="ncu dram bytes per decode launch (from profiles/), reported in the roofline")
+    ap.add_argument("--compress-only", action="store_true",
+                    help="run only the compress benchmark and print its JSON object")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.compress_only:
+        run_compress_only(args)
     else:
         run_ours(args)
 
