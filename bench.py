@@ -210,9 +210,10 @@ def run_ours(args):
 
     if world > 1:
         import torch.distributed as dist
-        gm = torch.empty((world, B, HQ, nspl), dtype=torch.float32, device=dev)
-        gl = torch.empty_like(gm)
-        go = torch.empty((world, B, HQ, nspl, D), dtype=torch.float32, device=dev)
+        # two-level combine: each rank merges its splits into one record
+        # {m, l, o[128]} per (b, q head); one all-gather of the records
+        rec = torch.empty((B, HQ, ops.RECORD_FLOATS), dtype=torch.float32, device=dev)
+        grec = torch.empty((world, B, HQ, ops.RECORD_FLOATS), dtype=torch.float32, device=dev)
 
     def step(i, seq_len, events=None):
         # append the new token (sharded run: the last rank owns the newest chunk)
@@ -227,16 +228,14 @@ def run_ours(args):
             if events is not None:
                 events[1].record(stream)
         else:
-            pm, pl, po = ops.decode_partials(qs[i], kpool, vpool, seq_len=seq_len, num_splits=nspl, rotate_q=True)
+            # ranks before the last hold a full, fixed chunk; the last rank's grows
+            local_len = seq_len if rank == world - 1 else CTX
+            pm, pl, po = ops.decode_partials(qs[i], kpool, vpool, seq_len=local_len, num_splits=nspl, rotate_q=True)
             if events is not None:
                 events[1].record(stream)
-            dist.all_gather_into_tensor(gm, pm, group=pg)
-            dist.all_gather_into_tensor(gl, pl, group=pg)
-            dist.all_gather_into_tensor(go, po, group=pg)
-            ops.lse_merge(gm.permute(1, 2, 0, 3).reshape(B, HQ, world * nspl).contiguous(),
-                          gl.permute(1, 2, 0, 3).reshape(B, HQ, world * nspl).contiguous(),
-                          go.permute(1, 2, 0, 3, 4).reshape(B, HQ, world * nspl, D).contiguous(),
-                          unrotate_out=True, out=out)
+            ops.lse_merge_to_record(pm, pl, po, out=rec)
+            dist.all_gather_into_tensor(grec, rec, group=pg)
+            ops.lse_merge_records(grec, unrotate_out=True, out=out)
 
     def barrier():
         if world > 1:
@@ -274,8 +273,11 @@ def run_ours(args):
         total_ms = t.item()
 
     mean_ctx = seq0 + (K + 1) / 2.0
-    bytes_per_step = B * HKV * mean_ctx * 2 * BLOCK          # K + V blocks read, per rank
-    value = bytes_per_step * world * K / (total_ms / 1e3) / 1e9
+    # K + V blocks read per step: the last rank's chunk grows, the others' are CTX
+    rank_ctx = mean_ctx if (world == 1 or rank == world - 1) else float(CTX)
+    bytes_per_step = B * HKV * rank_ctx * 2 * BLOCK
+    job_bytes_per_step = B * HKV * ((world - 1) * CTX + mean_ctx) * 2 * BLOCK
+    value = job_bytes_per_step * K / (total_ms / 1e3) / 1e9
     tok_s = B * K / (total_ms / 1e3)
     dec_avg_ms = sum(dec_ms) / len(dec_ms)
     achieved = bytes_per_step / (dec_avg_ms / 1e3) / 1e9
@@ -342,11 +344,11 @@ def run_ours(args):
                        "l2": "inputs 1.07 GB/rank > L2 (no flush needed)"},
             "decode_tok_s": tok_s, "pct_peak": value / world / peak,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": DECODE_DRAM_BYTES_PER_UNIT * B * HKV * mean_ctx,
+                         "frac": achieved / peak, "traffic": DECODE_DRAM_BYTES_PER_UNIT * B * HKV * rank_ctx,
                          "note": f"decode (split partials + merge) per step: 256 B per (token, kv head), "
-                                 f"{B * HKV} (b, kv head) rows x mean {mean_ctx:.0f} tokens; traffic from ncu "
+                                 f"{B * HKV} (b, kv head) rows x mean {rank_ctx:.0f} tokens; traffic from ncu "
                                  f"(per launch of the decode kernel); peak {peak_kind}"},
-            "gpu_launches": K * (4 if (world == 1 or rank == world - 1) else 2),
+            "gpu_launches": K * (4 if world == 1 else (5 if rank == world - 1 else 3)),
             "clocks": clocks, "e2e": e2e, "compress": comp, "cpu_baseline": cpu,
         }
         if comp:

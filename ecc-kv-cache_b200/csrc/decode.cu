@@ -180,27 +180,47 @@ decode_v1_kernel(const __half *__restrict__ q, const uint8_t *__restrict__ kb, c
     }
 }
 
-// Merge n partials per row; 128 threads = 128 dims.
-__global__ void __launch_bounds__(kD)
-lse_merge_kernel(const float *__restrict__ pm, const float *__restrict__ pl, const float *__restrict__ po,
-                 int n, __half *__restrict__ out, int flags) {
-    __shared__ float sh[kD];
-    const int64_t row = blockIdx.x;
-    const int d = threadIdx.x;
-    const float *m = pm + row * n;
-    const float *l = pl + row * n;
-    float M = -INFINITY;
+// LSE combine of n partials (m natural-log units, l, unnormalised o) of one
+// row, dim d: returns M = max over non-empty partials (-inf if none), L and
+// O relative to M.  Partial i is read through src(i) = {m, l, o[d]}.
+template <class Src>
+__device__ __forceinline__ void lse_combine(int n, int d, const Src &src, float &M, float &L, float &O) {
+    M = -INFINITY;
     for (int i = 0; i < n; ++i)
-        if (l[i] > 0.0f) M = fmaxf(M, m[i]);
-    float L = 0.0f, O = 0.0f;
+        if (src.l(i) > 0.0f) M = fmaxf(M, src.m(i));
+    L = 0.0f;
+    O = 0.0f;
     if (M != -INFINITY) {
         for (int i = 0; i < n; ++i) {
-            if (!(l[i] > 0.0f)) continue;
-            const float e = __expf(m[i] - M);
-            L = fmaf(l[i], e, L);
-            O = fmaf(po[(row * n + i) * kD + d], e, O);
+            if (!(src.l(i) > 0.0f)) continue;
+            const float e = __expf(src.m(i) - M);
+            L = fmaf(src.l(i), e, L);
+            O = fmaf(src.o(i, d), e, O);
         }
     }
+}
+
+// Split partials of one row: m, l [row][n], o [row][n][128].
+struct SplitSrc {
+    const float *pm, *pl, *po;
+    int64_t row;
+    int n;
+    __device__ float m(int i) const { return pm[row * n + i]; }
+    __device__ float l(int i) const { return pl[row * n + i]; }
+    __device__ float o(int i, int d) const { return po[(row * n + i) * kD + d]; }
+};
+// Records {m, l, o[128]} of one row, record i at rec + i * stride + row * kRec.
+constexpr int kRec = 2 + kD;
+struct RecordSrc {
+    const float *rec;
+    int64_t row, stride;
+    __device__ const float *at(int i) const { return rec + i * stride + row * kRec; }
+    __device__ float m(int i) const { return at(i)[0]; }
+    __device__ float l(int i) const { return at(i)[1]; }
+    __device__ float o(int i, int d) const { return at(i)[2 + d]; }
+};
+
+__device__ __forceinline__ void write_out(float L, float O, __half *out, int64_t row, int d, int flags, float *sh) {
     float val = (L > 0.0f) ? O / L : 0.0f;
     if (flags & ECC_DECODE_UNROTATE_OUT) {
         sh[d] = val;
@@ -208,6 +228,40 @@ lse_merge_kernel(const float *__restrict__ pm, const float *__restrict__ pl, con
         val = sh[d];
     }
     out[row * kD + d] = __float2half_rn(val);
+}
+
+// Merge n partials per row; 128 threads = 128 dims.
+__global__ void __launch_bounds__(kD)
+lse_merge_kernel(const float *__restrict__ pm, const float *__restrict__ pl, const float *__restrict__ po,
+                 int n, __half *__restrict__ out, int flags) {
+    __shared__ float sh[kD];
+    float M, L, O;
+    lse_combine(n, threadIdx.x, SplitSrc{pm, pl, po, (int64_t)blockIdx.x, n}, M, L, O);
+    write_out(L, O, out, blockIdx.x, threadIdx.x, flags, sh);
+}
+
+// Merge n partials per row into one record {M, L, O[128]} (still a partial).
+__global__ void __launch_bounds__(kD)
+lse_merge_record_kernel(const float *__restrict__ pm, const float *__restrict__ pl, const float *__restrict__ po,
+                        int n, float *__restrict__ rec) {
+    float M, L, O;
+    const int64_t row = blockIdx.x;
+    lse_combine(n, threadIdx.x, SplitSrc{pm, pl, po, row, n}, M, L, O);
+    float *r = rec + row * kRec;
+    if (threadIdx.x == 0) {
+        r[0] = M;
+        r[1] = L;
+    }
+    r[2 + threadIdx.x] = O;
+}
+
+// Merge n records per row (record i of row r at rec + i * stride + r * kRec).
+__global__ void __launch_bounds__(kD)
+lse_merge_records_kernel(const float *__restrict__ rec, int n, int64_t stride, __half *__restrict__ out, int flags) {
+    __shared__ float sh[kD];
+    float M, L, O;
+    lse_combine(n, threadIdx.x, RecordSrc{rec, (int64_t)blockIdx.x, stride}, M, L, O);
+    write_out(L, O, out, blockIdx.x, threadIdx.x, flags, sh);
 }
 
 }  // namespace ecc
@@ -326,6 +380,29 @@ extern "C" int ecc_lse_merge(const float *part_m, const float *part_l, const flo
     if (rows > 0x7fffffff) return ECC_ERR_SHAPE;
     lse_merge_kernel<<<(unsigned)rows, kD, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
         part_m, part_l, part_o, n, reinterpret_cast<__half *>(out_f16), flags);
+    return launch_status();
+}
+
+extern "C" int ecc_lse_merge_to_record(const float *part_m, const float *part_l, const float *part_o, int64_t rows,
+                                       int n, float *records, ecc_stream_t stream) {
+    if (rows < 0 || n <= 0) return ECC_ERR_SHAPE;
+    if (rows == 0) return ECC_OK;
+    if (!part_m || !part_l || !part_o || !records) return ECC_ERR_NULL;
+    if (rows > 0x7fffffff) return ECC_ERR_SHAPE;
+    lse_merge_record_kernel<<<(unsigned)rows, kD, 0, reinterpret_cast<cudaStream_t>(stream)>>>(part_m, part_l,
+                                                                                              part_o, n, records);
+    return launch_status();
+}
+
+extern "C" int ecc_lse_merge_records(const float *records, int64_t rows, int n, int64_t record_stride, void *out_f16,
+                                     int flags, ecc_stream_t stream) {
+    if (rows < 0 || n <= 0 || record_stride < 0) return ECC_ERR_SHAPE;
+    if (rows == 0) return ECC_OK;
+    if (!records || !out_f16) return ECC_ERR_NULL;
+    if (rows > 0x7fffffff) return ECC_ERR_SHAPE;
+    if (n > 1 && record_stride < rows * kRec) return ECC_ERR_SHAPE;  // record sets may not overlap
+    lse_merge_records_kernel<<<(unsigned)rows, kD, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        records, n, record_stride, reinterpret_cast<__half *>(out_f16), flags);
     return launch_status();
 }
 

@@ -68,6 +68,8 @@ def _load():
         "ecc_decode_default_splits": ([i32, i32, i64], i32),
         "ecc_decode_partials": ([p, p, p, i64, i64, p, p, p, i32, i32, i32, i64, f32, i32, i32, p], i32),
         "ecc_lse_merge": ([p, p, p, i64, i32, p, i32, p], i32),
+        "ecc_lse_merge_to_record": ([p, p, p, i64, i32, p, p], i32),
+        "ecc_lse_merge_records": ([p, i64, i32, i64, p, i32, p], i32),
         "ecc_device_status": ([i32], i32),
     }
     for name, (args, res) in sig.items():
@@ -397,6 +399,50 @@ def lse_merge(pm: torch.Tensor, pl: torch.Tensor, po: torch.Tensor, unrotate_out
         rc = _lib.ecc_lse_merge(_ptr(pm), _ptr(pl), _ptr(po), rows, n, _ptr(out),
                                 UNROTATE_OUT if unrotate_out else 0, _stream(pm))
     _check(rc, "lse_merge")
+    return out
+
+
+RECORD_FLOATS = 2 + D
+
+
+def lse_merge_to_record(pm: torch.Tensor, pl: torch.Tensor, po: torch.Tensor,
+                        out: torch.Tensor | None = None) -> torch.Tensor:
+    """Merge partials along their split axis into one partial record per row:
+    pm/pl [..., n], po [..., n, 128] -> [..., 130] fp32 {m, l, o[128]} (o
+    unnormalised).  Records of several devices merge with lse_merge_records."""
+    for t, nme in ((pm, "pm"), (pl, "pl"), (po, "po")):
+        _require_input(t, nme)
+        if t.dtype != torch.float32:
+            raise RuntimeError(f"{nme} must be float32")
+    n = pm.shape[-1]
+    rows = pm.numel() // max(n, 1)
+    if pl.shape != pm.shape or po.shape != pm.shape + (D,):
+        raise RuntimeError("partial shapes disagree")
+    if out is None:
+        out = torch.empty(pm.shape[:-1] + (RECORD_FLOATS,), dtype=torch.float32, device=pm.device)
+    elif not out.is_contiguous() or out.dtype != torch.float32 or out.numel() != rows * RECORD_FLOATS:
+        raise RuntimeError("out must be a contiguous float32 tensor of rows*130 elements")
+    with torch.cuda.device(pm.device):
+        rc = _lib.ecc_lse_merge_to_record(_ptr(pm), _ptr(pl), _ptr(po), rows, n, _ptr(out), _stream(pm))
+    _check(rc, "lse_merge_to_record")
+    return out
+
+
+def lse_merge_records(records: torch.Tensor, unrotate_out: bool = False,
+                      out: torch.Tensor | None = None) -> torch.Tensor:
+    """Merge n partial records per row: records [n, ..., 130] (e.g. the
+    all-gather of every device's lse_merge_to_record result) -> [..., 128] fp16."""
+    _require_input(records, "records")
+    if records.dtype != torch.float32 or records.shape[-1] != RECORD_FLOATS or records.dim() < 2:
+        raise RuntimeError("records must be float32 [n, ..., 130]")
+    n = records.shape[0]
+    rows = records[0].numel() // RECORD_FLOATS
+    if out is None:
+        out = torch.empty(records.shape[1:-1] + (D,), dtype=torch.float16, device=records.device)
+    with torch.cuda.device(records.device):
+        rc = _lib.ecc_lse_merge_records(_ptr(records), rows, n, rows * RECORD_FLOATS, _ptr(out),
+                                        UNROTATE_OUT if unrotate_out else 0, _stream(records))
+    _check(rc, "lse_merge_records")
     return out
 
 

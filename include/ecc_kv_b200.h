@@ -145,6 +145,23 @@ int ecc_decode_partials(const void *q_f16, const void *k_blocks, const void *v_b
 int ecc_lse_merge(const float *part_m, const float *part_l, const float *part_o, int64_t rows, int n,
                   void *out_f16, int flags, ecc_stream_t stream);
 
+/* Two-level combine for sequences sharded over devices (no counterpart in
+ * the reference, which runs on one GPU).  A partial record is 130 floats
+ * {m, l, o[128]} (m in natural-log units, o unnormalised), i.e. one merged
+ * split.
+ *   ecc_lse_merge_to_record: merges the n split partials of each row (layout
+ *     of ecc_lse_merge) into one record per row, records [rows, 130].
+ *   ecc_lse_merge_records: merges n records per row, record i of row r at
+ *     records + i * record_stride + r * 130 (floats) -- e.g. the [n, rows,
+ *     130] result of an all-gather of every device's records, with
+ *     record_stride = rows * 130 -- into out [rows, 128] fp16; flags may hold
+ *     ECC_DECODE_UNROTATE_OUT.  Record sets may not overlap. */
+#define ECC_RECORD_FLOATS 130
+int ecc_lse_merge_to_record(const float *part_m, const float *part_l, const float *part_o, int64_t rows, int n,
+                            float *records, ecc_stream_t stream);
+int ecc_lse_merge_records(const float *records, int64_t rows, int n, int64_t record_stride, void *out_f16,
+                          int flags, ecc_stream_t stream);
+
 /* Bytes of the library-owned device array ecc_decode_static uses for its
  * split partials (4 MiB on every GPU that loads the library, kept until the
  * process exits). */

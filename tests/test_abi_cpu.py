@@ -64,6 +64,13 @@ def test_argument_validation_before_any_device_call(lib):
     assert lib.ecc_decode(p(16), p(128), p(128), 0, 0, p(16), None, 0, 1, 4, 2, 8, 0.0, 0, 0, None) == -5
     lib.ecc_lse_merge.argtypes = [p, p, p, i64, i32, p, i32, p]
     assert lib.ecc_lse_merge(p(16), p(16), p(16), 4, 0, p(16), 0, None) == -2
+    lib.ecc_lse_merge_to_record.argtypes = [p, p, p, i64, i32, p, p]
+    assert lib.ecc_lse_merge_to_record(p(16), p(16), p(16), 4, 0, p(16), None) == -2
+    assert lib.ecc_lse_merge_to_record(p(16), p(16), p(16), 4, 3, None, None) == -1
+    lib.ecc_lse_merge_records.argtypes = [p, i64, i32, i64, p, i32, p]
+    assert lib.ecc_lse_merge_records(p(16), 4, 0, 520, p(16), 0, None) == -2
+    assert lib.ecc_lse_merge_records(None, 4, 2, 520, p(16), 0, None) == -1
+    assert lib.ecc_lse_merge_records(p(16), 4, 2, 100, p(16), 0, None) == -2  # overlapping record sets
 
 
 @pytest.mark.skipif(torch.cuda.is_available(), reason="only meaningful on a host without a GPU")

@@ -158,6 +158,18 @@ def test_partials_and_merge_equal_decode(ops, oracle, cuda_device, kern):
     cat = [torch.cat([x, y], dim=2).contiguous() for x, y in zip(a, b)]
     merged2 = ops.lse_merge(*cat, unrotate_out=True)
     assert close(merged2, full)
+    # two-level combine: each "device" merges its splits into one record per
+    # row, the records are stacked as an all-gather would, then merged
+    recs = torch.stack([ops.lse_merge_to_record(*a), ops.lse_merge_to_record(*b)])
+    assert recs.shape == (2, 2, 8, 130)
+    merged3 = ops.lse_merge_records(recs, unrotate_out=True)
+    assert close(merged3, full)
+    # a device with an empty chunk contributes an empty record
+    e = ops.decode_partials(q, K, V, seq_len=0, num_splits=2, rotate_q=True, kernel=kern)
+    rec_e = ops.lse_merge_to_record(*e)
+    assert (rec_e[..., 1] == 0).all()
+    merged4 = ops.lse_merge_records(torch.stack([recs[0], rec_e, recs[1]]), unrotate_out=True)
+    assert close(merged4, full)
 
 
 def test_empty_context_and_empty_splits(ops, cuda_device):
