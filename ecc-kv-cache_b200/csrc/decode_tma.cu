@@ -42,10 +42,11 @@ __device__ int g_device_error;  // raised by a bounded wait that ran out
 namespace tmak {
 
 constexpr int kWarps = 12;          // warps per CTA (384 threads)
-constexpr int kStages = 3;          // ring stages per warp
-constexpr int kTile = 16;
-constexpr int kStageBytes = 3072;
-constexpr int kOffKC = 0, kOffKS = 1024, kOffVC = 1536, kOffVS = 2560;
+constexpr int kStages = 2;          // ring stages per warp
+constexpr int kTile = 32;           // tokens per stage (two 16-token MMA sub-tiles)
+constexpr int kStageBytes = 6144;
+constexpr int kOffKC = 0, kOffKS = 2048, kOffVC = 3072, kOffVS = 5120;  // 32 x 64 B, 32 x 32 B, ...
+constexpr int kSubC = 1024, kSubS = 512;  // offset of sub-tile 1 in the code / syndrome boxes
 constexpr int kThreads = kWarps * 32;
 constexpr int kLutBytes = 65536;
 constexpr float kLn2f = 0.6931471805599453f;
@@ -53,7 +54,7 @@ constexpr long long kWaitCycles = 4000000000ll;
 
 constexpr int kSmemReserve = 1024;  // shared-window offset of dynamic shared memory
 constexpr int kSmLut = 0;
-constexpr int kSmRing = kSmLut + kLutBytes;                        // [kWarps][kStages][3072]
+constexpr int kSmRing = kSmLut + kLutBytes;                        // [kWarps][kStages][kStageBytes]
 constexpr int kSmCent = kSmRing + kWarps * kStages * kStageBytes;  // [16] u32
 constexpr int kSmBar = kSmCent + 16 * 4;                           // [kWarps][kStages] u64
 constexpr int kSmBytes = kSmBar + kWarps * kStages * 8;
@@ -191,33 +192,44 @@ struct Lane {
     int g, c;
     float scale_log2;
 
-    // One 16-token tile from shared stage `st`; tokens >= nvalid are masked.
-    __device__ __forceinline__ void tile(uint32_t st, int nvalid) {
-        const uint4 kca = lds128(st + kOffKC + 64 * g + 16 * c);
-        const uint4 kcb = lds128(st + kOffKC + 64 * (g + 8) + 16 * c);
-        const uint32_t ksa = lds32(st + kOffKS + 32 * g + 4 * c);
-        const uint32_t ksb = lds32(st + kOffKS + 32 * (g + 8) + 4 * c);
-        const uint2 kma = lds64(st + kOffKS + 32 * g + 16);
-        const uint2 kmb = lds64(st + kOffKS + 32 * (g + 8) + 16);
-        const bool va = g < nvalid, vb8 = g + 8 < nvalid;
-        // V tokens 2c, 2c+1, 2c+8, 2c+9: code bytes 8g..8g+7, syndrome word g/2
+    // Raw V data of one 16-token sub-tile: tokens 2c, 2c+1, 2c+8, 2c+9 (code
+    // bytes 8g..8g+7, syndrome word g/2) and the metadata of tokens g, g+8.
+    struct VRaw {
         uint2 vc[4];
         uint32_t vs[4];
+        uint2 vma, vmb;
+    };
+    __device__ __forceinline__ VRaw load_v(uint32_t vcb, uint32_t vsb) const {
+        VRaw v;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const int tok = 2 * c + (u & 1) + 8 * (u >> 1);
-            vc[u] = lds64(st + kOffVC + 64 * tok + 8 * g);
-            vs[u] = lds32(st + kOffVS + 32 * tok + 4 * (g >> 1));
+            v.vc[u] = lds64(vcb + 64 * tok + 8 * g);
+            v.vs[u] = lds32(vsb + 32 * tok + 4 * (g >> 1));
         }
-        const uint2 vma = lds64(st + kOffVS + 32 * g + 16);
-        const uint2 vmb = lds64(st + kOffVS + 32 * (g + 8) + 16);
+        v.vma = lds64(vsb + 32 * g + 16);
+        v.vmb = lds64(vsb + 32 * (g + 8) + 16);
+        return v;
+    }
+
+    // log2-scaled scores of one 16-token sub-tile (K codes at kcb, syndrome +
+    // metadata at ksb): s2[e] token g, s2[2+e] token g+8, head 2c+e; tokens
+    // >= nvalid are -inf.
+    __device__ __forceinline__ void qk(uint32_t kcb, uint32_t ksb, int nvalid, float (&s2)[4]) const {
+        const uint4 kca = lds128(kcb + 64 * g + 16 * c);
+        const uint4 kcb8 = lds128(kcb + 64 * (g + 8) + 16 * c);
+        const uint32_t ksa = lds32(ksb + 32 * g + 4 * c);
+        const uint32_t ksb8 = lds32(ksb + 32 * (g + 8) + 4 * c);
+        const uint2 kma = lds64(ksb + 32 * g + 16);
+        const uint2 kmb = lds64(ksb + 32 * (g + 8) + 16);
+        const bool va = g < nvalid, vb8 = g + 8 < nvalid;
 
         // Centroid products: rows g / g+8 of the A operand carry the fp16 hi /
         // lo parts of one token's centroids, so each table entry (hi, lo)
         // lands in the operand registers as loaded; one product per 8 tokens.
         float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f}, ss[4] = {0.f, 0.f, 0.f, 0.f};
         const uint32_t kwa[4] = {kca.x, kca.y, kca.z, kca.w};
-        const uint32_t kwb[4] = {kcb.x, kcb.y, kcb.z, kcb.w};
+        const uint32_t kwb[4] = {kcb8.x, kcb8.y, kcb8.z, kcb8.w};
 #pragma unroll
         for (int m = 0; m < 8; ++m) {
             const int w = m >> 1, by = 2 * (m & 1);
@@ -227,101 +239,95 @@ struct Lane {
             const uint2 yb = lut(kwb[w], by + 1, lane8);
             mma16816(sa, xa.x, xa.y, ya.x, ya.y, qc[m][0], qc[m][1]);
             mma16816(sb, xb.x, xb.y, yb.x, yb.y, qc[m][0], qc[m][1]);
-            mma16816(ss, sign_pair(ksa, 2 * m), sign_pair(ksb, 2 * m), sign_pair(ksa, 2 * m + 1),
-                     sign_pair(ksb, 2 * m + 1), qs[m][0], qs[m][1]);
+            mma16816(ss, sign_pair(ksa, 2 * m), sign_pair(ksb8, 2 * m), sign_pair(ksa, 2 * m + 1),
+                     sign_pair(ksb8, 2 * m + 1), qs[m][0], qs[m][1]);
         }
         // q.C of token g (head 2c+e) = hi row + lo row
         const float sc[4] = {sa[0] + sa[2], sa[1] + sa[3], sb[0] + sb[2], sb[1] + sb[3]};
-        float s2[4];
-        {
-            const float k_sa = h_lo(kma.x), k_za = h_hi(kma.x), k_aa = h_lo(kma.y);
-            const float k_sb = h_lo(kmb.x), k_zb = h_hi(kmb.x), k_ab = h_lo(kmb.y);
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const float xa = fmaf(k_sa, sc[e], fmaf(k_aa, ss[e], k_za * qsum[e]));
-                const float xb = fmaf(k_sb, sc[2 + e], fmaf(k_ab, ss[2 + e], k_zb * qsum[e]));
-                s2[e] = va ? xa * scale_log2 : -INFINITY;
-                s2[2 + e] = vb8 ? xb * scale_log2 : -INFINITY;
-            }
-        }
-        float corr[2];
+        const float k_sa = h_lo(kma.x), k_za = h_hi(kma.x), k_aa = h_lo(kma.y);
+        const float k_sb = h_lo(kmb.x), k_zb = h_hi(kmb.x), k_ab = h_lo(kmb.y);
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-            float mx = fmaxf(s2[e], s2[2 + e]);
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-            const float mnew = fmaxf(mrun[e], mx);
-            corr[e] = ex2(mrun[e] - mnew);
-            mrun[e] = mnew;
+            const float xa = fmaf(k_sa, sc[e], fmaf(k_aa, ss[e], k_za * qsum[e]));
+            const float xb = fmaf(k_sb, sc[2 + e], fmaf(k_ab, ss[2 + e], k_zb * qsum[e]));
+            s2[e] = va ? xa * scale_log2 : -INFINITY;
+            s2[2 + e] = vb8 ? xb * scale_log2 : -INFINITY;
         }
-        float p[4];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-            p[e] = ex2(s2[e] - mrun[e]);
-            p[2 + e] = ex2(s2[2 + e] - mrun[e]);
-        }
-        if (corr[0] != 1.0f || corr[1] != 1.0f) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                o[i][0] *= corr[0];
-                o[i][1] *= corr[1];
-                o[i][2] *= corr[0];
-                o[i][3] *= corr[1];
-            }
-        }
-        const float v_sa = h_lo(vma.x), v_za = h_hi(vma.x), v_aa = h_lo(vma.y);
-        const float v_sb = h_lo(vmb.x), v_zb = h_hi(vmb.x), v_ab = h_lo(vmb.y);
-        uint32_t pk[4];
+    }
+
+    // PV products of one 16-token sub-tile with probabilities p (same layout
+    // as the scores).
+    __device__ __forceinline__ void pv(const VRaw &v, const float (&p)[4]) {
+        const float v_sa = h_lo(v.vma.x), v_aa = h_lo(v.vma.y);
+        const float v_sb = h_lo(v.vmb.x), v_ab = h_lo(v.vmb.y);
         constexpr bool kSplitCols = G <= 4;
+        // P operand words per (token, head): pk = fp16 (p*scale_v, p*alpha_v
+        // (x2 with the split columns)), pr = fp16 residual of p*scale_v, so
+        // that the centroid products carry p*scale_v to ~2^-22 (a single
+        // fp16 rounding of it is 2^-11 relative, close to the 2e-3 output
+        // tolerance when a few large values dominate)
+        uint32_t pk[4], pr[4];
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-            lrun[e] = fmaf(lrun[e], corr[e], p[e] + p[2 + e]);
-            if constexpr (kSplitCols) {
-                // sign s = 2b - 1: the -valpha part joins the zero point
-                zrun[e] = fmaf(zrun[e], corr[e], fmaf(p[e], v_za - v_aa, p[2 + e] * (v_zb - v_ab)));
-                pk[e] = pack_h2(p[e] * v_sa, 2.0f * (p[e] * v_aa));
-                pk[2 + e] = pack_h2(p[2 + e] * v_sb, 2.0f * (p[2 + e] * v_ab));
-            } else {
-                zrun[e] = fmaf(zrun[e], corr[e], fmaf(p[e], v_za, p[2 + e] * v_zb));
-                pk[e] = pack_h2(p[e] * v_sa, p[e] * v_aa);
-                pk[2 + e] = pack_h2(p[2 + e] * v_sb, p[2 + e] * v_ab);
-            }
+        for (int j = 0; j < 4; ++j) {
+            const float pj = p[j];
+            const float ws = pj * (j < 2 ? v_sa : v_sb);
+            const float wa = (kSplitCols ? 2.0f : 1.0f) * (pj * (j < 2 ? v_aa : v_ab));
+            pk[j] = pack_h2(ws, wa);
+            pr[j] = pack_h2(ws - h_lo(pk[j]), 0.0f);
         }
-        uint32_t bt[4];
+        uint32_t bt[4], br[4];
         {
             const int srcA = 8 * c + ((kSplitCols ? (g & 3) : g) >> 1), srcB = srcA + 4;
             const bool odd = g & 1;
-            const uint32_t x0e = __shfl_sync(0xffffffffu, pk[0], srcA), x0o = __shfl_sync(0xffffffffu, pk[1], srcA);
-            const uint32_t x1e = __shfl_sync(0xffffffffu, pk[0], srcB), x1o = __shfl_sync(0xffffffffu, pk[1], srcB);
-            const uint32_t x2e = __shfl_sync(0xffffffffu, pk[2], srcA), x2o = __shfl_sync(0xffffffffu, pk[3], srcA);
-            const uint32_t x3e = __shfl_sync(0xffffffffu, pk[2], srcB), x3o = __shfl_sync(0xffffffffu, pk[3], srcB);
-            bt[0] = odd ? x0o : x0e;
-            bt[1] = odd ? x1o : x1e;
-            bt[2] = odd ? x2o : x2e;
-            bt[3] = odd ? x3o : x3e;
+            // lane srcA holds the P words of tokens 2c (slots 0, 1) and 2c+8
+            // (slots 2, 3), lane srcB those of tokens 2c+1 and 2c+9
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const int src = (t & 1) ? srcB : srcA;
+                const int j = (t >> 1) * 2;  // slot pair: tokens g (j = 0) or g+8 (j = 2)
+                const uint32_t xe = __shfl_sync(0xffffffffu, pk[j], src), xo = __shfl_sync(0xffffffffu, pk[j + 1], src);
+                const uint32_t re = __shfl_sync(0xffffffffu, pr[j], src), ro = __shfl_sync(0xffffffffu, pr[j + 1], src);
+                bt[t] = odd ? xo : xe;
+                br[t] = odd ? ro : re;
+            }
         }
-        uint32_t b1_0, b1_1, b2_0, b2_1;
+        // b1: p*scale_v, b2: sign weights, b3: p*scale_v residual, bo: the
+        // operand of the odd dims' centroid products
+        uint32_t b1_0, b1_1, b2_0, b2_1, b3_0, b3_1, bo_0, bo_1;
         if constexpr (kSplitCols) {
+            // columns 0..3 (lanes g < 4): p*scale_v of head g, and its
+            // residual for an extra product into the even dims' accumulators;
+            // columns 4..7 (lanes g >= 4) of head g-4: the sign weights in the
+            // even dims' accumulators, the residual in the odd dims' (their
+            // columns 4..7 are otherwise unused)
             const bool cent = g < 4;
             const uint32_t sel = cent ? 0x5410u : 0x7632u;
             const uint32_t y0 = __byte_perm(bt[0], bt[1], sel), y1 = __byte_perm(bt[2], bt[3], sel);
+            const uint32_t r0 = __byte_perm(br[0], br[1], 0x5410), r1 = __byte_perm(br[2], br[3], 0x5410);
             b1_0 = cent ? y0 : 0u;
             b1_1 = cent ? y1 : 0u;
             b2_0 = cent ? 0u : y0;
             b2_1 = cent ? 0u : y1;
+            b3_0 = cent ? r0 : 0u;
+            b3_1 = cent ? r1 : 0u;
+            bo_0 = cent ? y0 : r0;
+            bo_1 = cent ? y1 : r1;
         } else {
             b1_0 = __byte_perm(bt[0], bt[1], 0x5410);
             b1_1 = __byte_perm(bt[2], bt[3], 0x5410);
             b2_0 = __byte_perm(bt[0], bt[1], 0x7632);
             b2_1 = __byte_perm(bt[2], bt[3], 0x7632);
+            b3_0 = __byte_perm(br[0], br[1], 0x5410);
+            b3_1 = __byte_perm(br[2], br[3], 0x5410);
+            bo_0 = b1_0;
+            bo_1 = b1_1;
         }
 
-        const uint32_t sA = __byte_perm(vs[0], vs[1], sel_half), sB = __byte_perm(vs[2], vs[3], sel_half);
+        const uint32_t sA = __byte_perm(v.vs[0], v.vs[1], sel_half), sB = __byte_perm(v.vs[2], v.vs[3], sel_half);
 #pragma unroll
         for (int w = 0; w < 2; ++w) {
-            const uint32_t xa0 = w ? vc[0].y : vc[0].x, xa1 = w ? vc[1].y : vc[1].x;
-            const uint32_t xb0 = w ? vc[2].y : vc[2].x, xb1 = w ? vc[3].y : vc[3].x;
+            const uint32_t xa0 = w ? v.vc[0].y : v.vc[0].x, xa1 = w ? v.vc[1].y : v.vc[1].x;
+            const uint32_t xb0 = w ? v.vc[2].y : v.vc[2].x, xb1 = w ? v.vc[3].y : v.vc[3].x;
             constexpr uint32_t kLo = 0x0F0F0F0Fu, kHi = 0xF0F0F0F0u;
             const uint32_t ia_e = (xa0 & kLo) | ((xa1 << 4) & kHi), ia_o = ((xa0 >> 4) & kLo) | (xa1 & kHi);
             const uint32_t ib_e = (xb0 & kLo) | ((xb1 << 4) & kHi), ib_o = ((xb0 >> 4) & kLo) | (xb1 & kHi);
@@ -336,7 +342,9 @@ struct Lane {
                 const uint2 r1 = lut(ia_o, k, lane8);  // odd dim
                 const uint2 r3 = lut(ib_o, k, lane8);
                 mma16816(o[2 * i], r0.x, r0.y, r2.x, r2.y, b1_0, b1_1);
-                mma16816(o[2 * i + 1], r1.x, r1.y, r3.x, r3.y, b1_0, b1_1);
+                mma16816(o[2 * i], r0.x, r0.y, r2.x, r2.y, b3_0, b3_1);
+                mma16816(o[2 * i + 1], r1.x, r1.y, r3.x, r3.y, bo_0, bo_1);
+                if constexpr (!kSplitCols) mma16816(o[2 * i + 1], r1.x, r1.y, r3.x, r3.y, b3_0, b3_1);
                 if constexpr (kSplitCols) {
                     // columns 4..7 of accumulator 2i: rows g the even dim's
                     // sign term, rows g+8 the odd dim's
@@ -349,6 +357,62 @@ struct Lane {
                 }
             }
         }
+    }
+
+    // One 32-token stage at `st` (two sub-tiles sharing one softmax update);
+    // tokens >= nvalid are masked.
+    __device__ __forceinline__ void tile(uint32_t st, int nvalid) {
+        const VRaw v0 = load_v(st + kOffVC, st + kOffVS);
+        float s0[4], s1[4];
+        qk(st + kOffKC, st + kOffKS, nvalid, s0);
+        qk(st + kOffKC + kSubC, st + kOffKS + kSubS, nvalid - 16, s1);
+
+        float corr[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            float mx = fmaxf(fmaxf(s0[e], s0[2 + e]), fmaxf(s1[e], s1[2 + e]));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            const float mnew = fmaxf(mrun[e], mx);
+            corr[e] = ex2(mrun[e] - mnew);
+            mrun[e] = mnew;
+        }
+        float p0[4], p1[4];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            p0[e] = ex2(s0[e] - mrun[e]);
+            p0[2 + e] = ex2(s0[2 + e] - mrun[e]);
+            p1[e] = ex2(s1[e] - mrun[e]);
+            p1[2 + e] = ex2(s1[2 + e] - mrun[e]);
+        }
+        if (corr[0] != 1.0f || corr[1] != 1.0f) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                o[i][0] *= corr[0];
+                o[i][1] *= corr[1];
+                o[i][2] *= corr[0];
+                o[i][3] *= corr[1];
+            }
+        }
+        const VRaw v1 = load_v(st + kOffVC + kSubC, st + kOffVS + kSubS);
+        {
+            // running sum and zero-point sum (with the split columns the sign
+            // s = 2b - 1 moves -valpha into the zero point)
+            constexpr bool kSplitCols = G <= 4;
+            const float za0 = h_hi(v0.vma.x) - (kSplitCols ? h_lo(v0.vma.y) : 0.0f);
+            const float zb0 = h_hi(v0.vmb.x) - (kSplitCols ? h_lo(v0.vmb.y) : 0.0f);
+            const float za1 = h_hi(v1.vma.x) - (kSplitCols ? h_lo(v1.vma.y) : 0.0f);
+            const float zb1 = h_hi(v1.vmb.x) - (kSplitCols ? h_lo(v1.vmb.y) : 0.0f);
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                lrun[e] = fmaf(lrun[e], corr[e], (p0[e] + p0[2 + e]) + (p1[e] + p1[2 + e]));
+                zrun[e] = fmaf(zrun[e], corr[e],
+                               fmaf(p0[e], za0, fmaf(p0[2 + e], zb0, fmaf(p1[e], za1, p1[2 + e] * zb1))));
+            }
+        }
+        pv(v0, p0);
+        pv(v1, p1);
     }
 };
 
@@ -572,6 +636,10 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap mkc, const __grid_constant
 #pragma unroll
                 for (int k = 0; k < 4; ++k)
                     sg[k] = __shfl_down_sync(0xffffffffu, L.o[2 * i][k], 2) * sign_unweight(k < 2 ? 2 * i : 2 * i + 1);
+                // the odd dim's residual products (columns 4..7, rows g and g+8)
+#pragma unroll
+                for (int e = 0; e < 2; ++e)
+                    sg[2 + e] += __shfl_down_sync(0xffffffffu, L.o[2 * i + 1][e] + L.o[2 * i + 1][2 + e], 2);
             }
             const int d0 = 16 * L.g + 2 * i;
 #pragma unroll
@@ -720,7 +788,7 @@ int launch_decode_tma(const void *q, const void *kb, const void *vb, int64_t bs_
     if (G < 1 || G > 8 || seq_len < 1 || seq_len > (1ll << 30)) return 1;
     if (((uintptr_t)kb % 16) || ((uintptr_t)vb % 16) || ((uintptr_t)q % 16)) return 1;
     const Plan plan = make_plan(B, Hkv, seq_len);
-    if (plan.nslots != ns) return 1;  // the caller asked for another split count
+    if (ns < plan.nslots) return 1;  // fewer partial slots than the partition writes
     if (!reserve_matches()) return 1;
     if (get_encode() != ECC_OK) return 1;
     CUtensorMap kc, ks, vc, vs;
