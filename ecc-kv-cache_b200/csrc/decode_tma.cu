@@ -266,16 +266,20 @@ struct Lane {
         // that the centroid products carry p*scale_v to ~2^-22 (a single
         // fp16 rounding of it is 2^-11 relative, close to the 2e-3 output
         // tolerance when a few large values dominate)
-        uint32_t pk[4], pr[4];
+        // pr[j/2] packs the residuals of the lane's two heads (slots j, j+1)
+        uint32_t pk[4], pr[2];
+        float res[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const float pj = p[j];
             const float ws = pj * (j < 2 ? v_sa : v_sb);
             const float wa = (kSplitCols ? 2.0f : 1.0f) * (pj * (j < 2 ? v_aa : v_ab));
             pk[j] = pack_h2(ws, wa);
-            pr[j] = pack_h2(ws - h_lo(pk[j]), 0.0f);
+            res[j] = ws - h_lo(pk[j]);
         }
-        uint32_t bt[4], br[4];
+        pr[0] = pack_h2(res[0], res[1]);
+        pr[1] = pack_h2(res[2], res[3]);
+        uint32_t bt[4], rp0, rp1;
         {
             const int srcA = 8 * c + ((kSplitCols ? (g & 3) : g) >> 1), srcB = srcA + 4;
             const bool odd = g & 1;
@@ -286,10 +290,12 @@ struct Lane {
                 const int src = (t & 1) ? srcB : srcA;
                 const int j = (t >> 1) * 2;  // slot pair: tokens g (j = 0) or g+8 (j = 2)
                 const uint32_t xe = __shfl_sync(0xffffffffu, pk[j], src), xo = __shfl_sync(0xffffffffu, pk[j + 1], src);
-                const uint32_t re = __shfl_sync(0xffffffffu, pr[j], src), ro = __shfl_sync(0xffffffffu, pr[j + 1], src);
                 bt[t] = odd ? xo : xe;
-                br[t] = odd ? ro : re;
             }
+            // residual pairs (token 2c, 2c+1) and (2c+8, 2c+9) of the lane's head
+            const uint32_t sel = odd ? 0x7632u : 0x5410u;
+            rp0 = __byte_perm(__shfl_sync(0xffffffffu, pr[0], srcA), __shfl_sync(0xffffffffu, pr[0], srcB), sel);
+            rp1 = __byte_perm(__shfl_sync(0xffffffffu, pr[1], srcA), __shfl_sync(0xffffffffu, pr[1], srcB), sel);
         }
         // b1: p*scale_v, b2: sign weights, b3: p*scale_v residual, bo: the
         // operand of the odd dims' centroid products
@@ -303,22 +309,21 @@ struct Lane {
             const bool cent = g < 4;
             const uint32_t sel = cent ? 0x5410u : 0x7632u;
             const uint32_t y0 = __byte_perm(bt[0], bt[1], sel), y1 = __byte_perm(bt[2], bt[3], sel);
-            const uint32_t r0 = __byte_perm(br[0], br[1], 0x5410), r1 = __byte_perm(br[2], br[3], 0x5410);
             b1_0 = cent ? y0 : 0u;
             b1_1 = cent ? y1 : 0u;
             b2_0 = cent ? 0u : y0;
             b2_1 = cent ? 0u : y1;
-            b3_0 = cent ? r0 : 0u;
-            b3_1 = cent ? r1 : 0u;
-            bo_0 = cent ? y0 : r0;
-            bo_1 = cent ? y1 : r1;
+            b3_0 = cent ? rp0 : 0u;
+            b3_1 = cent ? rp1 : 0u;
+            bo_0 = cent ? y0 : rp0;
+            bo_1 = cent ? y1 : rp1;
         } else {
             b1_0 = __byte_perm(bt[0], bt[1], 0x5410);
             b1_1 = __byte_perm(bt[2], bt[3], 0x5410);
             b2_0 = __byte_perm(bt[0], bt[1], 0x7632);
             b2_1 = __byte_perm(bt[2], bt[3], 0x7632);
-            b3_0 = __byte_perm(br[0], br[1], 0x5410);
-            b3_1 = __byte_perm(br[2], br[3], 0x5410);
+            b3_0 = rp0;
+            b3_1 = rp1;
             bo_0 = b1_0;
             bo_1 = b1_1;
         }

@@ -135,6 +135,26 @@ def test_decode_custom_scale_and_prefix(ops, oracle, cuda_device):
 
 
 @pytest.mark.parametrize("kern", ["tma", "register", "cuda_cores"])
+@pytest.mark.parametrize("hq,hkv", [(4, 1), (8, 1)])
+def test_sharp_softmax_heavy_values(ops, oracle, cuda_device, kern, hq, hkv):
+    """A few tokens dominate (large sm_scale) and the values are heavy-tailed
+    with both signs: the output is a near-cancelling mix of large values,
+    where a single fp16 rounding of the softmax weights would exceed the
+    tolerance."""
+    L = 700
+    k16 = workloads.make_heavy(seed=11, n=hkv * L)
+    v16 = workloads.make_heavy(seed=12, n=hkv * L) * 4
+    kp = oracle.compress(k16.numpy()).reshape(1, hkv, L, 128)
+    vp = oracle.compress(v16.numpy()).reshape(1, hkv, L, 128)
+    for seed in range(4):
+        q = (torch.randn(1, hq, 1, 128, generator=torch.Generator().manual_seed(seed)) * 2).half()
+        out = ops.decode_attention(q.to(cuda_device), _dev(kp, cuda_device), _dev(vp, cuda_device), seq_len=L,
+                                   sm_scale=0.35, rotate_q=True, unrotate_out=True, kernel=kern)
+        ref = oracle.decode(q.numpy(), kp, vp, hkv=hkv, seq_len=L, sm_scale=0.35, rotate_q=True, unrotate_out=True)
+        assert _err(out, ref) <= TOL, seed
+
+
+@pytest.mark.parametrize("kern", ["tma", "register", "cuda_cores"])
 def test_partials_and_merge_equal_decode(ops, oracle, cuda_device, kern):
     """decode_partials + lse_merge (the cross-device combine) equals decode,
     including partials gathered from two token chunks (sequence sharding)."""
