@@ -181,22 +181,58 @@ decode_v1_kernel(const __half *__restrict__ q, const uint8_t *__restrict__ kb, c
 }
 
 // LSE combine of n partials (m natural-log units, l, unnormalised o) of one
-// row, dim d: returns M = max over non-empty partials (-inf if none), L and
-// O relative to M.  Partial i is read through src(i) = {m, l, o[d]}.
+// row by a 128-thread block, thread d = dim d: M = max over the non-empty
+// partials (l > 0; -inf if none), L and O relative to M.  Partial i is read through src(i) =
+// {m, l, o[d]}.  The sums run in partial order; the partials' (m, l) are
+// staged in shared memory a chunk at a time and the o loads are issued eight
+// at a time, so the loop is not bound by one load latency per partial.
 template <class Src>
 __device__ __forceinline__ void lse_combine(int n, int d, const Src &src, float &M, float &L, float &O) {
-    M = -INFINITY;
-    for (int i = 0; i < n; ++i)
-        if (src.l(i) > 0.0f) M = fmaxf(M, src.m(i));
+    __shared__ float s_l[kD], s_e[kD], s_red[kD / 32];
+    float mx = -INFINITY;
+    for (int i = d; i < n; i += kD)
+        if (src.l(i) > 0.0f) mx = fmaxf(mx, src.m(i));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if ((d & 31) == 0) s_red[d >> 5] = mx;
+    __syncthreads();
+    M = s_red[0];
+#pragma unroll
+    for (int w = 1; w < kD / 32; ++w) M = fmaxf(M, s_red[w]);
     L = 0.0f;
     O = 0.0f;
-    if (M != -INFINITY) {
-        for (int i = 0; i < n; ++i) {
-            if (!(src.l(i) > 0.0f)) continue;
-            const float e = __expf(src.m(i) - M);
-            L = fmaf(src.l(i), e, L);
-            O = fmaf(src.o(i, d), e, O);
+    if (M == -INFINITY) return;  // block-uniform
+    for (int c0 = 0; c0 < n; c0 += kD) {
+        {
+            const int i = c0 + d;
+            float l = 0.0f, e = 0.0f;
+            if (i < n) {
+                l = src.l(i);
+                if (l > 0.0f) e = __expf(src.m(i) - M);
+            }
+            s_l[d] = l;
+            s_e[d] = e;
         }
+        __syncthreads();
+        const int cn = min(kD, n - c0);
+        int k = 0;
+        for (; k + 8 <= cn; k += 8) {
+            float ov[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ov[j] = (s_l[k + j] > 0.0f) ? src.o(c0 + k + j, d) : 0.0f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (s_l[k + j] > 0.0f) {
+                    L = fmaf(s_l[k + j], s_e[k + j], L);
+                    O = fmaf(ov[j], s_e[k + j], O);
+                }
+        }
+        for (; k < cn; ++k)
+            if (s_l[k] > 0.0f) {
+                L = fmaf(s_l[k], s_e[k], L);
+                O = fmaf(src.o(c0 + k, d), s_e[k], O);
+            }
+        __syncthreads();
     }
 }
 
