@@ -62,7 +62,10 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every 200 ms while running."""
+    """nvidia-smi clocks/throttle reasons sampled every 20 ms with host
+    timestamps; summary() reports the samples inside the window mark_start()
+    .. mark_stop() (the timed region), or the nearest ones if the window was
+    shorter than the sampling interval."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -71,22 +74,33 @@ class ClockSampler:
     def __init__(self, gpu_id: str):
         self.gpu = gpu_id
         self.proc = None
-        self.lines = []
+        self.samples = []  # (host time, line)
+        self.t0 = self.t1 = None
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            deadline = time.time() + 10.0  # let nvidia-smi come up before the timed region
+            while not self.samples and time.time() < deadline and self.proc.poll() is None:
+                time.sleep(0.01)
         except Exception:
             self.proc = None
         return self
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.samples.append((time.time(), line.strip()))
+
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_stop(self):
+        self.t1 = time.time()
+        time.sleep(0.06)  # the sample that covers the end of the window
 
     def __exit__(self, *a):
         if self.proc is not None:
@@ -97,9 +111,15 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
+        picked = [ln for t, ln in self.samples if self.t0 is not None and self.t0 <= t <= (self.t1 or t)]
+        window = "timed region"
+        if not picked and self.samples and self.t0 is not None:
+            mid = 0.5 * (self.t0 + (self.t1 or self.t0))
+            picked = [min(self.samples, key=lambda s: abs(s[0] - mid))[1]]
+            window = "nearest sample"
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in picked:
             parts = [x.strip() for x in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -112,7 +132,7 @@ class ClockSampler:
                 if v.lower() == "active":
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "window": window}
 
 
 def dist_env():
@@ -218,8 +238,7 @@ def run_ours(args):
     def step(i, seq_len, events=None):
         # append the new token (sharded run: the last rank owns the newest chunk)
         if world == 1 or rank == world - 1:
-            ops.compress_into(new_k[i], kpool, pos=seq_len - 1, rotate=True)
-            ops.compress_into(new_v[i], vpool, pos=seq_len - 1, rotate=True)
+            ops.compress_pair_into(new_k[i], new_v[i], kpool, vpool, pos=seq_len - 1, rotate=True)
         if events is not None:
             events[0].record(stream)
         if world == 1:
@@ -243,6 +262,12 @@ def run_ours(args):
             dist.barrier()
         torch.cuda.synchronize()
 
+    try:
+        gpu_id = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        gpu_id = str(local)
+    clk = ClockSampler(gpu_id).__enter__()  # up and sampling before the warm-up steps
+
     seq = CTX
     for i in range(W):
         seq += 1
@@ -253,18 +278,16 @@ def run_ours(args):
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     seq0 = seq
-    try:
-        gpu_id = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
-    except Exception:
-        gpu_id = str(local)
-    with ClockSampler(gpu_id) as clk:
-        barrier()
-        start.record(stream)
-        for i in range(K):
-            seq += 1
-            step(W + i, seq, ev[i])
-        stop.record(stream)
-        barrier()
+    barrier()
+    clk.mark_start()
+    start.record(stream)
+    for i in range(K):
+        seq += 1
+        step(W + i, seq, ev[i])
+    stop.record(stream)
+    barrier()
+    clk.mark_stop()
+    clk.__exit__(None, None, None)
     total_ms = start.elapsed_time(stop)
     dec_ms = [a.elapsed_time(b) for a, b in ev]
     if world > 1:
@@ -306,8 +329,7 @@ def run_ours(args):
             dq.copy_(hq[i], non_blocking=True)
             dk.copy_(hk[i], non_blocking=True)
             dv.copy_(hv[i], non_blocking=True)
-            ops.compress_into(dk, kpool, pos=seq_e - 1, rotate=True)
-            ops.compress_into(dv, vpool, pos=seq_e - 1, rotate=True)
+            ops.compress_pair_into(dk, dv, kpool, vpool, pos=seq_e - 1, rotate=True)
             ops.decode_attention(dq, kpool, vpool, seq_len=seq_e, rotate_q=True, unrotate_out=True,
                                  num_splits=splits, out=out)
             hout[i].copy_(out, non_blocking=True)
@@ -348,7 +370,7 @@ def run_ours(args):
                          "note": f"decode (split partials + merge) per step: 256 B per (token, kv head), "
                                  f"{B * HKV} (b, kv head) rows x mean {rank_ctx:.0f} tokens; traffic from ncu "
                                  f"(per launch of the decode kernel); peak {peak_kind}"},
-            "gpu_launches": K * (4 if world == 1 else (5 if rank == world - 1 else 3)),
+            "gpu_launches": K * (3 if world == 1 else (4 if rank == world - 1 else 3)),
             "clocks": clocks, "e2e": e2e, "compress": comp, "cpu_baseline": cpu,
         }
         if comp:

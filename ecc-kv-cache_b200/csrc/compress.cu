@@ -216,6 +216,23 @@ __device__ __noinline__ int exact_code(float d, float scale) {
     return best;
 }
 
+// One compress job: vectors (b, h, l) of a strided fp16 [B, H, L, 128] view
+// into blocks (b, h, l) of a pool.
+struct CompressJob {
+    const __half *x;
+    int64_t xs_b, xs_h, xs_l;
+    uint8_t *blocks;
+    int64_t bs_b, bs_h;
+    FastDiv div_h, div_l;
+    uint32_t n_vec, n_tiles;
+};
+// Up to two jobs in one launch (K and V of one append): tiles [0, n_tiles of
+// job 0) belong to job 0, the rest to job 1.
+struct CompressJobs {
+    CompressJob j[2];
+    int njobs;
+};
+
 // One warp's kVecPerWarp vectors of tile `tile`.  The fast pass (kExact =
 // false) gives up and returns false, before writing anything, when any of the
 // warp's elements needs the exact treatment (a quotient within kBand of a
@@ -369,10 +386,7 @@ __device__ __noinline__ void compress_warp_exact(const __half *__restrict__ x, i
 }
 
 template <bool kRotate>
-__global__ void __launch_bounds__(kCompressWarps * 32, 3)
-compress_kernel(const __half *__restrict__ x, int64_t xs_b, int64_t xs_h, int64_t xs_l,
-                uint8_t *__restrict__ blocks, int64_t bs_b, int64_t bs_h, FastDiv div_h, FastDiv div_l,
-                uint32_t n_vec) {
+__global__ void __launch_bounds__(kCompressWarps * 32, 3) compress_kernel(const __grid_constant__ CompressJobs jobs) {
     __shared__ QEntry tab[kCells * kReplicas];
     __shared__ __align__(16) uint32_t stage[kCompressWarps][kVecPerWarp][20];
     build_qtable(tab);
@@ -380,12 +394,16 @@ compress_kernel(const __half *__restrict__ x, int64_t xs_b, int64_t xs_h, int64_
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     uint32_t *st = stage[warp][lane >> 2];
-    const uint32_t n_tiles = (n_vec + kVecPerTile - 1) / kVecPerTile;
+    const uint32_t t0 = jobs.j[0].n_tiles;
+    const uint32_t n_tiles = t0 + (jobs.njobs > 1 ? jobs.j[1].n_tiles : 0u);
     for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-        if (!compress_warp<kRotate, false>(x, xs_b, xs_h, xs_l, blocks, bs_b, bs_h, div_h, div_l, n_vec, tile, tab,
-                                           st))
-            compress_warp_exact<kRotate>(x, xs_b, xs_h, xs_l, blocks, bs_b, bs_h, div_h, div_l, n_vec, tile, tab,
-                                         st);
+        const bool second = tile >= t0;  // block-uniform
+        const CompressJob &jb = second ? jobs.j[1] : jobs.j[0];
+        const uint32_t t = second ? tile - t0 : tile;
+        if (!compress_warp<kRotate, false>(jb.x, jb.xs_b, jb.xs_h, jb.xs_l, jb.blocks, jb.bs_b, jb.bs_h, jb.div_h,
+                                           jb.div_l, jb.n_vec, t, tab, st))
+            compress_warp_exact<kRotate>(jb.x, jb.xs_b, jb.xs_h, jb.xs_l, jb.blocks, jb.bs_b, jb.bs_h, jb.div_h,
+                                         jb.div_l, jb.n_vec, t, tab, st);
     }
 }
 
@@ -540,31 +558,77 @@ using namespace ecc;
 
 static inline bool aligned(const void *p, size_t a) { return ((uintptr_t)p % a) == 0; }
 
-extern "C" int ecc_compress_strided(const void *x_f16, int64_t xs_b, int64_t xs_h, int64_t xs_l, void *blocks,
-                                    int64_t bs_b, int64_t bs_h, int B, int H, int64_t L, int rotate,
-                                    ecc_stream_t stream) {
+// Validates one strided compress request and fills its job; *n_out = vectors.
+static int make_job(const void *x_f16, int64_t xs_b, int64_t xs_h, int64_t xs_l, void *blocks, int64_t bs_b,
+                    int64_t bs_h, int B, int H, int64_t L, CompressJob *jb, int64_t *n_out) {
     if (B < 0 || H < 0 || L < 0) return ECC_ERR_SHAPE;
     const int64_t n = (int64_t)B * H * L;
+    *n_out = n;
     if (n == 0) return ECC_OK;
     if (n >= (int64_t)0xffffff00ll) return ECC_ERR_SHAPE;  // 32-bit vector index
     if (!x_f16 || !blocks) return ECC_ERR_NULL;
     if (!aligned(x_f16, 16) || !aligned(blocks, 128)) return ECC_ERR_ALIGN;
     if ((xs_b % 8) || (xs_h % 8) || (xs_l % 8)) return ECC_ERR_ALIGN;
+    jb->x = reinterpret_cast<const __half *>(x_f16);
+    jb->xs_b = xs_b;
+    jb->xs_h = xs_h;
+    jb->xs_l = xs_l;
+    jb->blocks = reinterpret_cast<uint8_t *>(blocks);
+    jb->bs_b = bs_b;
+    jb->bs_h = bs_h;
+    jb->div_h = make_fastdiv((uint32_t)std::max(H, 1));
+    jb->div_l = make_fastdiv((uint32_t)std::max<int64_t>(L, 1));
+    jb->n_vec = (uint32_t)n;
+    jb->n_tiles = (uint32_t)((n + kVecPerTile - 1) / kVecPerTile);
+    return ECC_OK;
+}
+
+static int launch_jobs(CompressJobs &jobs, int rotate, ecc_stream_t stream) {
+    // drop empty jobs
+    if (jobs.njobs > 1 && jobs.j[1].n_vec == 0) jobs.njobs = 1;
+    if (jobs.njobs > 0 && jobs.j[0].n_vec == 0) {
+        jobs.j[0] = jobs.j[1];
+        jobs.njobs -= 1;
+    }
+    if (jobs.njobs == 0) return ECC_OK;
     DevInfo *di = nullptr;
     int rc = dev_info(&di);
     if (rc != ECC_OK) return rc;
-    const int64_t tiles = (n + kVecPerTile - 1) / kVecPerTile;
+    const int64_t tiles = (int64_t)jobs.j[0].n_tiles + (jobs.njobs > 1 ? jobs.j[1].n_tiles : 0);
+    if (tiles >= (int64_t)0xffffff00ll) return ECC_ERR_SHAPE;
     const int64_t grid = std::min<int64_t>(tiles, (int64_t)di->sms * di->compress_ctas_per_sm[rotate ? 1 : 0]);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     if (rotate)
-        compress_kernel<true><<<(unsigned)grid, kCompressWarps * 32, 0, s>>>(
-            reinterpret_cast<const __half *>(x_f16), xs_b, xs_h, xs_l, reinterpret_cast<uint8_t *>(blocks),
-            bs_b, bs_h, make_fastdiv((uint32_t)H), make_fastdiv((uint32_t)L), (uint32_t)n);
+        compress_kernel<true><<<(unsigned)grid, kCompressWarps * 32, 0, s>>>(jobs);
     else
-        compress_kernel<false><<<(unsigned)grid, kCompressWarps * 32, 0, s>>>(
-            reinterpret_cast<const __half *>(x_f16), xs_b, xs_h, xs_l, reinterpret_cast<uint8_t *>(blocks),
-            bs_b, bs_h, make_fastdiv((uint32_t)H), make_fastdiv((uint32_t)L), (uint32_t)n);
+        compress_kernel<false><<<(unsigned)grid, kCompressWarps * 32, 0, s>>>(jobs);
     return launch_status();
+}
+
+extern "C" int ecc_compress_strided(const void *x_f16, int64_t xs_b, int64_t xs_h, int64_t xs_l, void *blocks,
+                                    int64_t bs_b, int64_t bs_h, int B, int H, int64_t L, int rotate,
+                                    ecc_stream_t stream) {
+    CompressJobs jobs{};
+    int64_t n = 0;
+    const int rc = make_job(x_f16, xs_b, xs_h, xs_l, blocks, bs_b, bs_h, B, H, L, &jobs.j[0], &n);
+    if (rc != ECC_OK || n == 0) return rc;
+    jobs.njobs = 1;
+    return launch_jobs(jobs, rotate, stream);
+}
+
+extern "C" int ecc_compress_strided_pair(const void *x0_f16, int64_t x0s_b, int64_t x0s_h, int64_t x0s_l,
+                                         void *blocks0, int64_t b0s_b, int64_t b0s_h, const void *x1_f16,
+                                         int64_t x1s_b, int64_t x1s_h, int64_t x1s_l, void *blocks1, int64_t b1s_b,
+                                         int64_t b1s_h, int B, int H, int64_t L, int rotate, ecc_stream_t stream) {
+    CompressJobs jobs{};
+    int64_t n0 = 0, n1 = 0;
+    int rc = make_job(x0_f16, x0s_b, x0s_h, x0s_l, blocks0, b0s_b, b0s_h, B, H, L, &jobs.j[0], &n0);
+    if (rc != ECC_OK) return rc;
+    rc = make_job(x1_f16, x1s_b, x1s_h, x1s_l, blocks1, b1s_b, b1s_h, B, H, L, &jobs.j[1], &n1);
+    if (rc != ECC_OK) return rc;
+    if (n0 == 0) return ECC_OK;
+    jobs.njobs = 2;
+    return launch_jobs(jobs, rotate, stream);
 }
 
 extern "C" int ecc_compress(const void *x_f16, void *blocks, int64_t n, int rotate, ecc_stream_t stream) {

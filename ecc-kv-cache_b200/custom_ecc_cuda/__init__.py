@@ -60,6 +60,8 @@ def _load():
         "ecc_hadamard_f32": ([p, i64, i32, p], i32),
         "ecc_compress": ([p, p, i64, i32, p], i32),
         "ecc_compress_strided": ([p, i64, i64, i64, p, i64, i64, i32, i32, i64, i32, p], i32),
+        "ecc_compress_strided_pair": ([p, i64, i64, i64, p, i64, i64, p, i64, i64, i64, p, i64, i64, i32, i32, i64,
+                                       i32, p], i32),
         "ecc_get_block_metadata": ([p, i64, i64, p, p], i32),
         "ecc_dequantize": ([p, p, i64, p], i32),
         "ecc_pack_soa": ([p, i64, p, i64, p, i64, p, i64, p], i32),
@@ -215,6 +217,41 @@ def compress_into(x: torch.Tensor, pool: torch.Tensor, pos: int = 0, rotate: boo
         rc = _lib.ecc_compress_strided(_ptr(x), x.stride(0), x.stride(1), x.stride(2), _ptr(dst), bs_b, bs_h,
                                        B, H, L, int(bool(rotate)), _stream(x))
     _check(rc, "compress_into")
+
+
+def _compress_dst(x: torch.Tensor, pool: torch.Tensor, pos: int, name: str):
+    _require_cuda(x, name)
+    if x.dtype != torch.float16:
+        raise RuntimeError(f"{name} must be float16")
+    if x.dim() != 4 or x.shape[-1] != D:
+        raise RuntimeError("Only D=128 supported (hardcoded kernel)")
+    if x.stride(-1) != 1:
+        raise RuntimeError(f"{name} must have a contiguous last dimension")
+    bs = _pool_strides(pool, "pool")
+    B, H, L, _ = x.shape
+    if pool.shape[-4] != B or pool.shape[-3] != H:
+        raise RuntimeError("pool batch/head dims do not match x")
+    if pos < 0 or pos + L > pool.shape[-2]:
+        raise RuntimeError(f"positions {pos}..{pos + L} exceed the pool capacity {pool.shape[-2]}")
+    if x.device != pool.device:
+        raise RuntimeError("x and pool must be on the same device")
+    return (pool[..., pos:, :] if pos else pool), bs
+
+
+def compress_pair_into(k: torch.Tensor, v: torch.Tensor, kpool: torch.Tensor, vpool: torch.Tensor, pos: int = 0,
+                       rotate: bool = True) -> None:
+    """compress_into of ``k`` into ``kpool`` and ``v`` into ``vpool`` (same
+    [B, H, L, 128] shape, same positions) in one launch."""
+    if k.shape != v.shape:
+        raise RuntimeError("k and v must have the same shape")
+    kdst, kbs = _compress_dst(k, kpool, pos, "k")
+    vdst, vbs = _compress_dst(v, vpool, pos, "v")
+    B, H, L, _ = k.shape
+    with torch.cuda.device(k.device):
+        rc = _lib.ecc_compress_strided_pair(_ptr(k), k.stride(0), k.stride(1), k.stride(2), _ptr(kdst), kbs[0],
+                                            kbs[1], _ptr(v), v.stride(0), v.stride(1), v.stride(2), _ptr(vdst),
+                                            vbs[0], vbs[1], B, H, L, int(bool(rotate)), _stream(k))
+    _check(rc, "compress_pair_into")
 
 
 def rotate_and_compress(x: torch.Tensor, blocks: torch.Tensor | None = None) -> torch.Tensor:

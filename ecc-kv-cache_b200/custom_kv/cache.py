@@ -158,8 +158,11 @@ class ErrorCorrectedCache(_HFCache):
         k16 = key_states if key_states.dtype == torch.float16 else key_states.to(torch.float16)
         v16 = value_states if value_states.dtype == torch.float16 else value_states.to(torch.float16)
         kp, vp = self.layer_pools(layer_idx)
-        ops.compress_into(k16, kp, pos=pos, rotate=True)
-        ops.compress_into(v16, vp, pos=pos, rotate=self.rotate_values)
+        if self.rotate_values:
+            ops.compress_pair_into(k16, v16, kp, vp, pos=pos, rotate=True)
+        else:
+            ops.compress_into(k16, kp, pos=pos, rotate=True)
+            ops.compress_into(v16, vp, pos=pos, rotate=False)
 
         self._layer_fill[layer_idx] = pos + L_new
         self._last_layer = layer_idx

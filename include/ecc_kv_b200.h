@@ -85,6 +85,17 @@ int ecc_compress_strided(const void *x_f16, int64_t xs_b, int64_t xs_h, int64_t 
                          void *blocks, int64_t bs_b, int64_t bs_h,
                          int B, int H, int64_t L, int rotate, ecc_stream_t stream);
 
+/* Two ecc_compress_strided requests of the same [B, H, L] shape in one launch
+ * -- the K and V writes of one cache update, which the reference issues as
+ * two compress_and_store calls (custom_kv/cache.py:103-126).  The two
+ * requests are validated like ecc_compress_strided and run concurrently; for
+ * an append of a few tokens that halves the latency of the pair. */
+int ecc_compress_strided_pair(const void *x0_f16, int64_t x0s_b, int64_t x0s_h, int64_t x0s_l,
+                              void *blocks0, int64_t b0s_b, int64_t b0s_h,
+                              const void *x1_f16, int64_t x1s_b, int64_t x1s_h, int64_t x1s_l,
+                              void *blocks1, int64_t b1s_b, int64_t b1s_h,
+                              int B, int H, int64_t L, int rotate, ecc_stream_t stream);
+
 /* Copy the fp16 (scale, zero, alpha) of block block_idx to host memory as
  * fp32.  Synchronous on `stream`.  Replaces custom_ecc_cuda.get_block_metadata
  * (csrc/ecc_ops.cpp:98). */

@@ -72,6 +72,23 @@ def test_large_heavy_tail_equals_oracle(ops, oracle, cuda_device, rotate):
     assert bad.size == 0, f"{bad.size} blocks differ ({ties} tie elements among them)"
 
 
+@pytest.mark.parametrize("B,H,L,pos", [(8, 8, 1, 4095), (2, 4, 37, 5), (1, 8, 2048, 0)])
+def test_pair_equals_two_single_compresses(ops, cuda_device, B, H, L, pos):
+    """compress_pair_into (K and V of one append in one launch) writes exactly
+    what two compress_into calls write, also for strided (transposed) inputs."""
+    g = torch.Generator(device=cuda_device).manual_seed(L)
+    k = torch.randn((B, L, H, 128), generator=g, device=cuda_device).half().transpose(1, 2)  # strided view
+    v = (torch.randn((B, H, L, 128), generator=g, device=cuda_device) * 3).half()
+    cap = pos + L + 3
+    kp1 = torch.zeros((B, H, cap, 128), dtype=torch.uint8, device=cuda_device)
+    vp1, kp2, vp2 = torch.zeros_like(kp1), torch.zeros_like(kp1), torch.zeros_like(kp1)
+    ops.compress_into(k, kp1, pos=pos, rotate=True)
+    ops.compress_into(v, vp1, pos=pos, rotate=True)
+    ops.compress_pair_into(k, v, kp2, vp2, pos=pos, rotate=True)
+    assert torch.equal(kp1, kp2) and torch.equal(vp1, vp2)
+    assert torch.count_nonzero(kp2[:, :, :pos]) == 0 and torch.count_nonzero(kp2[:, :, pos + L:]) == 0
+
+
 def test_strided_input_into_pool_positions(ops, oracle, cuda_device):
     """HF key_states are a transposed view [B, H, L, D]; write at pos > 0."""
     B, H, L, cap, pos = 2, 3, 37, 64, 11
