@@ -176,6 +176,20 @@ __host__ __device__ constexpr float sign_unweight(int p) {
                    : (float)(1u << (24 - p));  // subnormal 2^(p-24)
 }
 
+// K sign bits kept as 0/1 in the exponent field: bit pair (p, p+16) of the
+// syndrome word w lands at bit positions (q, q+16), q = kpos(p) in 10..14,
+// each half then being 0 or the fp16 2^kexp(p).  x5 = w << 5, x10 = w << 10,
+// x1 = w >> 1 are shared by the 16 pairs of a word (3 shifts + 16 masks
+// instead of 2 operations per pair).
+__host__ __device__ constexpr int kpos(int p) { return p == 15 ? 14 : p >= 10 ? p : p >= 5 ? p + 5 : p + 10; }
+__host__ __device__ constexpr int kexp(int p) {
+    return kpos(p) == 10 ? -14 : kpos(p) == 11 ? -13 : kpos(p) == 12 ? -11 : kpos(p) == 13 ? -7 : 1;
+}
+__device__ __forceinline__ uint32_t kbits(uint32_t w, uint32_t x5, uint32_t x10, uint32_t x1, int p) {
+    const uint32_t src = p == 15 ? x1 : p >= 10 ? w : p >= 5 ? x5 : x10;
+    return src & (0x00010001u << kpos(p));
+}
+
 // Consumer lane state for one work item.  For groups of at most 4 query heads
 // the PV products use the idle columns 4..7 of the n8 operand for the V sign
 // term: lanes g < 4 of the P operand carry p * vscale of head g (columns
@@ -184,7 +198,9 @@ __host__ __device__ constexpr float sign_unweight(int p) {
 // accumulator row has one power-of-two weight, removed at the end).
 template <int G>
 struct Lane {
-    uint32_t qc[8][2], qs[8][2];
+    uint32_t qc[8][2];
+    uint32_t qs[8][2];  // q of the sign products, k slot of bit p scaled by 2^-(ssh + kexp(p))
+    float sgn2;         // 2^(ssh + 1): q.s = sgn2 * (sign product) - sum(q)
     float qsum[2];
     float o[16][4];  // PV accumulators, one per dim of the lane's 16 (rows g: hi + sign, g+8: lo)
     float mrun[2], lrun[2], zrun[2];
@@ -220,6 +236,8 @@ struct Lane {
         const uint4 kcb8 = lds128(kcb + 64 * (g + 8) + 16 * c);
         const uint32_t ksa = lds32(ksb + 32 * g + 4 * c);
         const uint32_t ksb8 = lds32(ksb + 32 * (g + 8) + 4 * c);
+        const uint32_t ka5 = ksa << 5, ka10 = ksa << 10, ka1 = ksa >> 1;
+        const uint32_t kb5 = ksb8 << 5, kb10 = ksb8 << 10, kb1 = ksb8 >> 1;
         const uint2 kma = lds64(ksb + 32 * g + 16);
         const uint2 kmb = lds64(ksb + 32 * (g + 8) + 16);
         const bool va = g < nvalid, vb8 = g + 8 < nvalid;
@@ -239,17 +257,20 @@ struct Lane {
             const uint2 yb = lut(kwb[w], by + 1, lane8);
             mma16816(sa, xa.x, xa.y, ya.x, ya.y, qc[m][0], qc[m][1]);
             mma16816(sb, xb.x, xb.y, yb.x, yb.y, qc[m][0], qc[m][1]);
-            mma16816(ss, sign_pair(ksa, 2 * m), sign_pair(ksb8, 2 * m), sign_pair(ksa, 2 * m + 1),
-                     sign_pair(ksb8, 2 * m + 1), qs[m][0], qs[m][1]);
+            mma16816(ss, kbits(ksa, ka5, ka10, ka1, 2 * m), kbits(ksb8, kb5, kb10, kb1, 2 * m),
+                     kbits(ksa, ka5, ka10, ka1, 2 * m + 1), kbits(ksb8, kb5, kb10, kb1, 2 * m + 1), qs[m][0],
+                     qs[m][1]);
         }
         // q.C of token g (head 2c+e) = hi row + lo row
         const float sc[4] = {sa[0] + sa[2], sa[1] + sa[3], sb[0] + sb[2], sb[1] + sb[3]};
+        // score = scale q.C + alpha (2 q.b - sum q) + zero sum q  (s = 2b - 1)
         const float k_sa = h_lo(kma.x), k_za = h_hi(kma.x), k_aa = h_lo(kma.y);
         const float k_sb = h_lo(kmb.x), k_zb = h_hi(kmb.x), k_ab = h_lo(kmb.y);
+        const float k_ga = k_aa * sgn2, k_gb = k_ab * sgn2, k_da = k_za - k_aa, k_db = k_zb - k_ab;
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-            const float xa = fmaf(k_sa, sc[e], fmaf(k_aa, ss[e], k_za * qsum[e]));
-            const float xb = fmaf(k_sb, sc[2 + e], fmaf(k_ab, ss[2 + e], k_zb * qsum[e]));
+            const float xa = fmaf(k_sa, sc[e], fmaf(k_ga, ss[e], k_da * qsum[e]));
+            const float xb = fmaf(k_sb, sc[2 + e], fmaf(k_gb, ss[2 + e], k_db * qsum[e]));
             s2[e] = va ? xa * scale_log2 : -INFINITY;
             s2[2 + e] = vb8 ? xb * scale_log2 : -INFINITY;
         }
@@ -581,8 +602,26 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap mkc, const __grid_constant
             for (int m = 0; m < 8; ++m) {
                 L.qc[m][0] = pack_h2(x[4 * m], x[4 * m + 1]);
                 L.qc[m][1] = pack_h2(x[4 * m + 2], x[4 * m + 3]);
-                L.qs[m][0] = pack_h2(x[2 * m], x[2 * m + 16]);
-                L.qs[m][1] = pack_h2(x[2 * m + 1], x[2 * m + 17]);
+            }
+            // sign-product operand: scale 2^-ssh keeps q * 2^(14 - ssh) < 2^15
+            // for the largest |q| of the group (q is fp16, the scalings are
+            // exact powers of two)
+            {
+                float qmax = 0.0f;
+#pragma unroll
+                for (int k = 0; k < 32; ++k) qmax = fmaxf(qmax, fabsf(x[k]));
+#pragma unroll
+                for (int off = 1; off < 32; off <<= 1) qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, off));
+                const int e2 = (qmax > 0.0f) ? ((__float_as_int(qmax) >> 23) & 0xff) - 127 : 0;
+                const int ssh = max(0, e2);
+                L.sgn2 = __int_as_float((ssh + 1 + 127) << 23);
+#pragma unroll
+                for (int m = 0; m < 8; ++m) {
+                    const float f0 = __int_as_float((127 - ssh - kexp(2 * m)) << 23);
+                    const float f1 = __int_as_float((127 - ssh - kexp(2 * m + 1)) << 23);
+                    L.qs[m][0] = pack_h2(x[2 * m] * f0, x[2 * m + 16] * f0);
+                    L.qs[m][1] = pack_h2(x[2 * m + 1] * f1, x[2 * m + 17] * f1);
+                }
             }
             float sum = 0.0f;
 #pragma unroll
