@@ -391,6 +391,8 @@ __global__ void __launch_bounds__(kCompressWarps * 32, 3) compress_kernel(const 
     __shared__ __align__(16) uint32_t stage[kCompressWarps][kVecPerWarp][20];
     build_qtable(tab);
     __syncthreads();
+    pdl_trigger();
+    pdl_wait();  // the table set-up above touched shared memory only
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     uint32_t *st = stage[warp][lane >> 2];
@@ -598,10 +600,11 @@ static int launch_jobs(CompressJobs &jobs, int rotate, ecc_stream_t stream) {
     if (tiles >= (int64_t)0xffffff00ll) return ECC_ERR_SHAPE;
     const int64_t grid = std::min<int64_t>(tiles, (int64_t)di->sms * di->compress_ctas_per_sm[rotate ? 1 : 0]);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    if (rotate)
-        compress_kernel<true><<<(unsigned)grid, kCompressWarps * 32, 0, s>>>(jobs);
-    else
-        compress_kernel<false><<<(unsigned)grid, kCompressWarps * 32, 0, s>>>(jobs);
+    const cudaError_t e = rotate ? launch_pdl(compress_kernel<true>, dim3((unsigned)grid), dim3(kCompressWarps * 32),
+                                              0, s, jobs)
+                                 : launch_pdl(compress_kernel<false>, dim3((unsigned)grid),
+                                              dim3(kCompressWarps * 32), 0, s, jobs);
+    if (e != cudaSuccess) return ECC_ERR_LAUNCH;
     return launch_status();
 }
 

@@ -271,6 +271,8 @@ __global__ void __launch_bounds__(kD)
 lse_merge_kernel(const float *__restrict__ pm, const float *__restrict__ pl, const float *__restrict__ po,
                  int n, __half *__restrict__ out, int flags) {
     __shared__ float sh[kD];
+    pdl_trigger();
+    pdl_wait();
     float M, L, O;
     lse_combine(n, threadIdx.x, SplitSrc{pm, pl, po, (int64_t)blockIdx.x, n}, M, L, O);
     write_out(L, O, out, blockIdx.x, threadIdx.x, flags, sh);
@@ -414,8 +416,9 @@ extern "C" int ecc_lse_merge(const float *part_m, const float *part_l, const flo
     if (rows == 0) return ECC_OK;
     if (!part_m || !part_l || !part_o || !out_f16) return ECC_ERR_NULL;
     if (rows > 0x7fffffff) return ECC_ERR_SHAPE;
-    lse_merge_kernel<<<(unsigned)rows, kD, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-        part_m, part_l, part_o, n, reinterpret_cast<__half *>(out_f16), flags);
+    if (launch_pdl(lse_merge_kernel, dim3((unsigned)rows), dim3(kD), 0, reinterpret_cast<cudaStream_t>(stream),
+                   part_m, part_l, part_o, n, reinterpret_cast<__half *>(out_f16), flags) != cudaSuccess)
+        return ECC_ERR_LAUNCH;
     return launch_status();
 }
 

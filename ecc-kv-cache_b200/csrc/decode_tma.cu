@@ -488,6 +488,8 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap mkc, const __grid_constant
         reinterpret_cast<uint2 *>(sm + kSmLut + v * 256)[lane] = e;
     }
     __syncthreads();
+    pdl_trigger();
+    pdl_wait();  // everything above touched shared memory only
 
     // at most one warp per tile, so that every range is non-empty and the
     // partial slots of a row have no holes
@@ -774,8 +776,10 @@ static int launch_g(const CUtensorMap &kc, const CUtensorMap &ks, const CUtensor
             return ECC_ERR_CUDA;
         configured[dev] = true;
     }
-    decode_tma_kernel<G><<<grid, kThreads, kSmBytes, s>>>(kc, ks, vc, vs, reinterpret_cast<const __half *>(q), pm,
-                                                         pl, po, Hq, Hkv, seq_len, tpr, T, ns, scale_log2, flags);
+    if (launch_pdl(decode_tma_kernel<G>, dim3(grid), dim3(kThreads), kSmBytes, s, kc, ks, vc, vs,
+                   reinterpret_cast<const __half *>(q), pm, pl, po, Hq, Hkv, seq_len, tpr, T, ns, scale_log2,
+                   flags) != cudaSuccess)
+        return ECC_ERR_LAUNCH;
     return launch_status();
 }
 

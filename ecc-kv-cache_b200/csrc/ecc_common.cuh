@@ -48,4 +48,28 @@ constexpr float kInvSqrt128 = 0x1.6a09e6p-4f;
 
 __device__ __forceinline__ unsigned lane_id() { return threadIdx.x & 31u; }
 
+// Programmatic dependent launch: the hot kernels are launched as dependents
+// of the kernel before them on the stream.  Each calls pdl_wait() before it
+// reads or writes memory that earlier work may touch (so its set-up overlaps
+// the previous kernel's tail) and pdl_trigger() early so that the next kernel
+// can be launched while it runs.  Both are no-ops for a normal launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+static inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                     Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 }  // namespace ecc
