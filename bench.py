@@ -185,6 +185,69 @@ def run_compress_only(args):
     print(json.dumps({"compress": comp}), flush=True)
 
 
+def run_model_e2e(args):
+    """Model-level run: a Llama-3.1-8B-shaped model (32 layers, 32 q / 8 kv
+    heads, hidden 4096, MLP 14336, vocab 128256, rope theta 5e5) with seeded
+    random fp16 weights (no checkpoint is available offline), a 32768-token
+    seeded random prompt, 200 greedy tokens through transformers generate():
+    once with the ECC cache (prefill on fp16 K/V with every layer compressed
+    into the block pools, every decode step through the fused kernel) and once
+    with transformers' own fp16 cache.  Prints one JSON object."""
+    import torch
+    from transformers import LlamaConfig, LlamaForCausalLM
+    from custom_kv import ecc_cache
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    prompt_len, new_tokens = 32768, 200
+    cfg = LlamaConfig(hidden_size=4096, intermediate_size=14336, num_hidden_layers=32, num_attention_heads=32,
+                      num_key_value_heads=8, head_dim=128, vocab_size=128256, rope_theta=500000.0,
+                      max_position_embeddings=131072)
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = LlamaForCausalLM(cfg).half().eval()  # torch's default init, seeded, on the GPU
+    prompt = torch.randint(0, cfg.vocab_size, (1, prompt_len), generator=torch.Generator().manual_seed(0)).to(dev)
+    mask = torch.ones_like(prompt)
+
+    def timed_generate(n, cache_ctx):
+        # time generate() only: the cache context's set-up and exit (pool
+        # allocation, allocator cache release) are outside the timed region
+        with torch.no_grad(), cache_ctx() as cache:
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            out = model.generate(prompt, attention_mask=mask, past_key_values=cache, max_new_tokens=n,
+                                 min_new_tokens=n, do_sample=False)
+            torch.cuda.synchronize()
+            dt = time.perf_counter() - t0
+            extra = cache.memory_bytes() if hasattr(cache, "memory_bytes") else None
+        return dt, out, extra
+
+    class _NoCache:  # transformers' default (fp16 DynamicCache)
+        def __enter__(self):
+            return None
+
+        def __exit__(self, *a):
+            return False
+
+    def ecc_ctx():
+        return ecc_cache(model, batch_size=1, max_cache_len=prompt_len + new_tokens + 8, device=str(dev))
+
+    res = {}
+    for name, ctx in (("ecc_cache", ecc_ctx), ("fp16_cache", _NoCache)):
+        timed_generate(2, ctx)  # warm-up: kernels, allocator, tensor maps
+        t_pre, _, _ = timed_generate(1, ctx)
+        t_all, out, mem = timed_generate(new_tokens + 1, ctx)
+        dec = t_all - t_pre
+        res[name] = {"prefill_s": t_pre, "decode_tok_s": new_tokens / dec, "decode_ms_per_token": 1e3 * dec / new_tokens,
+                     "tokens": out[0, prompt_len:].tolist()[:8]}
+        if mem:
+            res[name]["cache_memory"] = mem
+        torch.cuda.empty_cache()
+    same_first = res["ecc_cache"]["tokens"][0] == res["fp16_cache"]["tokens"][0]
+    print(json.dumps({"workload": f"Llama-3.1-8B shape, random fp16 weights, {prompt_len}-token prompt, "
+                                  f"{new_tokens} greedy tokens, batch 1, transformers generate()",
+                      "data": "synthetic", **res, "first_token_equal": same_first}), flush=True)
+
+
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
@@ -458,6 +521,8 @@ def main():
     ap.add_argument("--skip-compress", action="store_true")
     ap.add_argument("--compress-only", action="store_true",
                     help="run only the compress benchmark and print its JSON object")
+    ap.add_argument("--model-e2e", action="store_true",
+                    help="run the Llama-3.1-8B-shaped 32k-prompt generate() comparison and print its JSON object")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
@@ -465,6 +530,8 @@ def main():
         run_reference(args)
     elif args.compress_only:
         run_compress_only(args)
+    elif args.model_e2e:
+        run_model_e2e(args)
     else:
         run_ours(args)
 
