@@ -83,11 +83,11 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 // Bounded wait by one lane; false when it ran out (the device flag is raised).
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, long long limit = kWaitCycles) {
     if (mbar_try(bar, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try(bar, parity)) {
-        if (clock64() - t0 > kWaitCycles) {
+        if (clock64() - t0 > limit) {
             atomicExch(&g_device_error, 1);
             return false;
         }
@@ -857,6 +857,43 @@ int launch_decode_tma(const void *q, const void *kb, const void *vb, int64_t bs_
 }
 
 }  // namespace ecc
+
+namespace ecc {
+namespace tmak {
+// Self-test of the bounded wait: one warp arms an mbarrier for bytes that no
+// copy will deliver and waits on it with mbar_wait (the decode's wait) and a
+// short limit.  The wait runs out, raises the device flag and the kernel
+// returns; *out = 1 when the warp saw the wait give up.
+__global__ void wait_timeout_selftest_kernel(long long limit, int *out) {
+    __shared__ __align__(8) uint64_t bar;
+    const uint32_t b = smem_u32(&bar);
+    if (threadIdx.x == 0) {
+        mbar_init(b, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        mbar_expect_tx(b, 16);  // 16 bytes that never arrive: the phase never completes
+    }
+    __syncwarp();
+    bool ok = true;
+    if (threadIdx.x == 0) ok = mbar_wait(b, 0, limit);
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (threadIdx.x == 0) *out = ok ? 0 : 1;
+}
+}  // namespace tmak
+}  // namespace ecc
+
+extern "C" int ecc_selftest_wait_timeout(long long limit_cycles, int *host_gave_up) {
+    if (!host_gave_up || limit_cycles <= 0 || limit_cycles > (4ll << 30)) return ECC_ERR_SHAPE;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return ECC_ERR_DEVICE;
+    int *d = nullptr;
+    if (cudaMalloc(&d, sizeof(int)) != cudaSuccess) return ECC_ERR_CUDA;
+    ecc::tmak::wait_timeout_selftest_kernel<<<1, 32>>>(limit_cycles, d);
+    int rc = ecc::launch_status();
+    if (rc == ECC_OK && cudaMemcpy(host_gave_up, d, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+        rc = ECC_ERR_CUDA;
+    cudaFree(d);
+    return rc;
+}
 
 extern "C" int ecc_device_status(int reset) {
     int v = 0;

@@ -58,6 +58,14 @@ int ecc_version(void);
  * reset != 0 clears the flag.  Synchronous. */
 int ecc_device_status(int reset);
 
+/* Self-test of the bounded device waits (no counterpart in the reference):
+ * launches one warp that waits on an mbarrier nothing will complete, with the
+ * decode kernel's wait routine and a limit of limit_cycles clocks (at most
+ * 2^32).  The wait gives up, raises the flag ecc_device_status reports, and
+ * the kernel returns; *host_gave_up = 1 then.  Synchronous; allocates 4 bytes
+ * of device memory for the result.  Faults and hangs nothing. */
+int ecc_selftest_wait_timeout(long long limit_cycles, int *host_gave_up);
+
 /* ---- WHT ------------------------------------------------------------------
  * In-place normalised Walsh-Hadamard transform of n rows of length d (power
  * of two, 1 <= d <= 1024), contiguous [n, d], fp16 or fp32.  Butterfly with

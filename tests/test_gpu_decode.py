@@ -241,3 +241,22 @@ def test_kernels_agree_at_benchmark_shape(ops, cuda_device):
     assert (a.float() - b.float()).abs().max().item() <= 1e-3
     assert (a.float() - c.float()).abs().max().item() <= 1e-3
     assert ops.device_status() == 0
+
+
+def test_bounded_wait_gives_up_and_reports(ops, cuda_device):
+    """A device wait that can never complete (an armed mbarrier without a
+    copy) runs out after its limit, raises the device flag and returns: the
+    context stays usable and the flag clears."""
+    import ctypes
+    lib = ctypes.CDLL(ops.library_path)
+    lib.ecc_selftest_wait_timeout.argtypes = [ctypes.c_longlong, ctypes.POINTER(ctypes.c_int)]
+    lib.ecc_selftest_wait_timeout.restype = ctypes.c_int
+    assert ops.device_status(reset=True) == 0
+    gave_up = ctypes.c_int(-1)
+    assert lib.ecc_selftest_wait_timeout(2_000_000, ctypes.byref(gave_up)) == 0  # ~1 ms at 2 GHz
+    assert gave_up.value == 1
+    assert ops.device_status(reset=True) == 1
+    assert ops.device_status() == 0
+    # the device still computes
+    x = torch.ones(4, 128, device=cuda_device, dtype=torch.float16)
+    assert torch.isfinite(ops.hadamard_rotate(x)).all()
