@@ -385,10 +385,296 @@ __device__ __noinline__ void compress_warp_exact(const __half *__restrict__ x, i
     compress_warp<kRotate, true>(x, xs_b, xs_h, xs_l, blocks, bs_b, bs_h, div_h, div_l, n_vec, tile, tab, st);
 }
 
+// ---- packed fast pass -------------------------------------------------------
+// The same arithmetic as compress_warp, with the element pairs (i, i+1) of a
+// lane held in float2 registers so that every butterfly, quotient and
+// quantiser step is one packed fp32x2 instruction (add/mul/fma .rn on two
+// lanes, each rounded exactly like its scalar form; no packed product is ever
+// followed by a packed add of it, which ptxas would fuse).  Torch's
+// accumulator lanes are reduced through shared memory (each lane adds two of
+// the eight slots, see tsum_finish) instead of by 32 shuffles per sum.
+
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+// a - b, rounded once (fma with multiplier -1 is exact before its rounding)
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) { return __ffma2_rn(b, make_float2(-1.0f, -1.0f), a); }
+
+__device__ __forceinline__ float4 lds_f4(uint32_t a) {
+    float4 r;
+    // the table is constant after the kernel's set-up barrier: not volatile
+    asm("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w) : "r"(a));
+    return r;
+}
+
+// Finishes a torch-order sum whose lane g holds accumulator g's eight slots
+// (A[j] = slots 2j, 2j+1): slot i of the four accumulators is combined as
+// ((acc0 + acc1) + acc2) + acc3 by lane i/2, then the eight slot totals are
+// added in order.  `red` is the vector's 40-float area (32 accumulator slots,
+// then 8 slot totals); every lane of the vector gets the sum.
+__device__ __forceinline__ float tsum_finish(const float2 (&A)[4], float *red, int g) {
+    __syncwarp();  // earlier readers of the area are done
+    float4 *r4 = reinterpret_cast<float4 *>(red + 8 * g);
+    r4[0] = make_float4(A[0].x, A[0].y, A[1].x, A[1].y);
+    r4[1] = make_float4(A[2].x, A[2].y, A[3].x, A[3].y);
+    __syncwarp();
+    float2 t = *reinterpret_cast<const float2 *>(red + 2 * g);
+    t = add2(t, *reinterpret_cast<const float2 *>(red + 8 + 2 * g));
+    t = add2(t, *reinterpret_cast<const float2 *>(red + 16 + 2 * g));
+    t = add2(t, *reinterpret_cast<const float2 *>(red + 24 + 2 * g));
+    *reinterpret_cast<float2 *>(red + 32 + 2 * g) = t;
+    __syncwarp();
+    const float4 u0 = reinterpret_cast<const float4 *>(red + 32)[0];
+    const float4 u1 = reinterpret_cast<const float4 *>(red + 32)[1];
+    float s = __fadd_rn(u0.x, u0.y);
+    s = __fadd_rn(s, u0.z);
+    s = __fadd_rn(s, u0.w);
+    s = __fadd_rn(s, u1.x);
+    s = __fadd_rn(s, u1.y);
+    s = __fadd_rn(s, u1.z);
+    return __fadd_rn(s, u1.w);
+}
+
+// Where a lane's vector of the current tile lives.
+struct VecRef {
+    uint8_t *dst;  // its block
+    bool valid;
+};
+
+__device__ __forceinline__ void load_vec(const CompressJob &jb, uint32_t tile, uint4 (&raw)[4], VecRef &ref) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane & 3, vsub = lane >> 2;
+    const uint32_t vi = tile * kVecPerTile + warp * kVecPerWarp + vsub;
+    ref.valid = vi < jb.n_vec;
+    const uint32_t v = ref.valid ? vi : 0u;
+    const uint32_t row = fdiv(v, jb.div_l);
+    const int64_t l = v - row * jb.div_l.d;
+    const uint32_t bq = fdiv(row, jb.div_h);
+    const int64_t b = bq, h = row - bq * jb.div_h.d;
+    const __half *src = jb.x + b * jb.xs_b + h * jb.xs_h + l * jb.xs_l + 8 * g;
+    ref.dst = jb.blocks + (b * jb.bs_b + h * jb.bs_h + l) * kBlockBytes;
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+        raw[c] = ref.valid ? __ldcs(reinterpret_cast<const uint4 *>(src + 32 * c)) : make_uint4(0, 0, 0, 0);
+}
+
+// Fast pass over the warp's eight vectors (lane layout as compress_warp).
+// Returns false, having written nothing, when any vector of the warp needs
+// the exact pass: a quotient within kBand of a decision threshold, a std
+// near an fp32 rounding midpoint, or a non-finite scale or zero point.
+// `tabq` is the shared-window address of this lane's replica of entry 0,
+// `red` the vector's reduction area, `st` its staging row.
+template <bool kRotate>
+__device__ __forceinline__ bool compress_fast(const uint4 (&raw)[4], const VecRef &ref, uint32_t tabq, float *red,
+                                              uint32_t *st) {
+    const int g = threadIdx.x & 3;
+    float2 P[4][4];  // P[c][j] = elements 32c + 8g + 2j, +1
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const uint32_t w[4] = {raw[c].x, raw[c].y, raw[c].z, raw[c].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 f = h2_to_f2(w[j]);
+            P[c][j] = kRotate ? make_float2(__fadd_rn(f.x, f.y), __fsub_rn(f.x, f.y)) : f;  // stride 1
+        }
+    }
+    if (kRotate) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+#pragma unroll
+            for (int j = 0; j < 4; j += 2) {  // stride 2
+                const float2 a = P[c][j], b = P[c][j + 1];
+                P[c][j] = add2(a, b);
+                P[c][j + 1] = sub2(a, b);
+            }
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {  // stride 4
+                const float2 a = P[c][j], b = P[c][j + 2];
+                P[c][j] = add2(a, b);
+                P[c][j + 2] = sub2(a, b);
+            }
+        }
+#pragma unroll
+        for (int s = 1; s <= 2; s <<= 1) {  // strides 8, 16: partner lane g ^ s
+            const float sg = (g & s) ? -1.0f : 1.0f;
+            const float2 sg2 = make_float2(sg, sg);
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float2 p = make_float2(__shfl_xor_sync(kFull, P[c][j].x, s),
+                                                 __shfl_xor_sync(kFull, P[c][j].y, s));
+                    P[c][j] = fma2(sg2, P[c][j], p);
+                }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {  // stride 32, then 64
+            float2 a = P[0][j], b = P[1][j];
+            P[0][j] = add2(a, b);
+            P[1][j] = sub2(a, b);
+            a = P[2][j];
+            b = P[3][j];
+            P[2][j] = add2(a, b);
+            P[3][j] = sub2(a, b);
+            a = P[0][j];
+            b = P[2][j];
+            P[0][j] = add2(a, b);
+            P[2][j] = sub2(a, b);
+            a = P[1][j];
+            b = P[3][j];
+            P[1][j] = add2(a, b);
+            P[3][j] = sub2(a, b);
+        }
+        const float2 r2 = make_float2(kInvSqrt128, kInvSqrt128), nc2 = make_float2(-kSqrt128, -kSqrt128);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float2 q0 = mul2(P[c][j], r2);
+                const float2 rem = fma2(q0, nc2, P[c][j]);
+                P[c][j] = fma2(rem, r2, q0);
+            }
+    }
+
+    // mean (zero point), ops_cpu.py:72: torch accumulator g, slots in c order
+    float2 A[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        A[j] = add2(make_float2(0.0f, 0.0f), P[0][j]);
+        A[j] = add2(A[j], P[1][j]);
+        A[j] = add2(A[j], P[2][j]);
+        A[j] = add2(A[j], P[3][j]);
+    }
+    const float zero = __fmul_rn(tsum_finish(A, red, g), 0.0078125f);
+
+    // unbiased std, ops_cpu.py:73 (fp64 sum of squares against the fp32 mean)
+    const double md = (double)zero;
+    double acc0 = 0.0, acc1 = 0.0;
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const double d0 = (double)P[c][j].x - md, d1 = (double)P[c][j].y - md;
+            acc0 = fma(d0, d0, acc0);
+            acc1 = fma(d1, d1, acc1);
+        }
+    double acc = acc0 + acc1;
+    acc += __shfl_xor_sync(kFull, acc, 1);
+    acc += __shfl_xor_sync(kFull, acc, 2);
+    // the quotient by 127 and the square root are each within an ulp of
+    // double; the midpoint test below is 1e-12 wide, far above that
+    const double sd = sqrt(acc * (1.0 / 127.0));
+    const float s32 = __double2float_rn(sd);
+    bool fallback;
+    {
+        const double lo = (double)s32;
+        const double nb = (double)(lo <= sd ? nextafterf(s32, INFINITY) : nextafterf(s32, 0.0f));
+        const double mid = 0.5 * (lo + nb);
+        fallback = fabs(sd - mid) <= 1e-12 * sd;
+    }
+    const float scale = __double2float_rn(__dadd_rn((double)s32, 1e-8));
+    // non-finite inputs: the exact pass clamps the table index
+    fallback = fallback || !(fabsf(scale) < INFINITY) || !(fabsf(zero) < INFINITY);
+    if (__any_sync(kFull, fallback)) return false;
+    const float rs = __frcp_rn(scale);
+
+    // quantise, residual, syndrome.  |u| <= sqrt(127) (1 + 2^-20) for finite
+    // inputs (every |x - zero| is at most sqrt(127) times the std against
+    // that zero point), so the cell 8u + 96 lies in [6, 187) and the table
+    // address needs no clamp.
+    //   * The cell comes from the unrounded product (fma of d with 8/scale):
+    //     it differs from the cell of u = RN(d/scale) only next to a cell
+    //     boundary, where both cells give the same code because every
+    //     threshold is >= 0.09 cells from a boundary.
+    //   * w = RN(d * rs - thr) decides the side of the cell's threshold;
+    //     |w| < kBand sends the warp to the exact pass.  m = sign mask of w
+    //     picks code and centroid with integer ops (m = -1: below).
+    //   * Codes are shifted into their word and sign bits of eps into
+    //     `negs` (funnel shift) in descending element order, so nibble i
+    //     and, after a byte reversal, bit 8c + i come out in place.  eps is
+    //     never -0 here: a rotated element is never -0 (the quotient returns
+    //     +0 for +-0), and eps = -0 needs x = -0; unrotated inputs use the
+    //     comparison instead.
+    const float2 nz2 = make_float2(-zero, -zero);
+    const float rs8 = __fmul_rn(rs, 8.0f);  // exact
+    const float2 rs82 = make_float2(rs8, rs8), mg2 = make_float2(kMagic + 96.0f, kMagic + 96.0f);
+    const uint32_t tbase = tabq - (uint32_t)__float_as_int(kMagic) * (uint32_t)(kReplicas * sizeof(QEntry));
+    uint32_t codes[4];
+    uint32_t negs = 0u, bits = 0u;
+    bool band = false;
+    float2 AL[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) AL[j] = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        uint32_t cw = 0u;
+#pragma unroll
+        for (int j = 3; j >= 0; --j) {
+            const float2 X = P[c][j];
+            const float2 D = add2(X, nz2);
+            const float2 T = fma2(D, rs82, mg2);
+            const float4 e1 = lds_f4(tbase + (uint32_t)__float_as_int(T.y) * (uint32_t)(kReplicas * sizeof(QEntry)));
+            const float4 e0 = lds_f4(tbase + (uint32_t)__float_as_int(T.x) * (uint32_t)(kReplicas * sizeof(QEntry)));
+            const float w1 = __fmaf_rn(D.y, rs, -e1.x), w0 = __fmaf_rn(D.x, rs, -e0.x);
+            band = band || (fabsf(w1) < kBand) || (fabsf(w0) < kBand);
+            const uint32_t m1 = (uint32_t)(__float_as_int(w1) >> 31), m0 = (uint32_t)(__float_as_int(w0) >> 31);
+            const float cq1 = __uint_as_float((__float_as_uint(e1.y) & m1) | (__float_as_uint(e1.z) & ~m1));
+            const float cq0 = __uint_as_float((__float_as_uint(e0.y) & m0) | (__float_as_uint(e0.z) & ~m0));
+            cw = (cw << 4) + ((uint32_t)__float_as_int(e1.w) + 1u + m1);
+            cw = (cw << 4) + ((uint32_t)__float_as_int(e0.w) + 1u + m0);
+            // k_tilde stays scalar: ptxas fuses a packed multiply followed by
+            // a packed add into one fma2 (single rounding) even when both are
+            // written as mul.rn/add.rn f32x2 PTX, and the reference rounds twice
+            const float2 KT = make_float2(__fadd_rn(__fmul_rn(cq0, scale), zero),
+                                          __fadd_rn(__fmul_rn(cq1, scale), zero));
+            const float2 E = sub2(X, KT);
+            if (kRotate) {
+                negs = __funnelshift_l(__float_as_uint(E.y), negs, 1);
+                negs = __funnelshift_l(__float_as_uint(E.x), negs, 1);
+            } else {
+                bits |= (E.x >= 0.0f ? 1u : 0u) << (8 * c + 2 * j);
+                bits |= (E.y >= 0.0f ? 1u : 0u) << (8 * c + 2 * j + 1);
+            }
+            AL[j] = add2(AL[j], make_float2(fabsf(E.x), fabsf(E.y)));
+        }
+        codes[c] = cw;
+    }
+    if (kRotate) bits = ~__byte_perm(negs, 0u, 0x0123u);
+    if (__any_sync(kFull, band)) return false;
+    const float alpha = __fmul_rn(tsum_finish(AL, red, g), 0.0078125f);
+
+    // stage: code word 4c+g and syndrome byte 4c+g of this vector
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        st[4 * c + g] = codes[c];
+        reinterpret_cast<uint8_t *>(st + 16)[4 * c + g] = (uint8_t)(bits >> (8 * c));
+    }
+    __syncwarp();
+    if (ref.valid) {
+        const uint4 w0 = *reinterpret_cast<const uint4 *>(st + 4 * g);
+        uint4 w1;
+        if (g == 0) {
+            w1 = *reinterpret_cast<const uint4 *>(st + 16);
+        } else if (g == 1) {
+            const uint32_t hs = __half_as_ushort(__float2half_rn(scale));
+            const uint32_t hz = __half_as_ushort(__float2half_rn(zero));
+            const uint32_t ha = __half_as_ushort(__float2half_rn(alpha));
+            w1 = make_uint4(hs | (hz << 16), ha, 0u, 0u);
+        } else {
+            w1 = make_uint4(0u, 0u, 0u, 0u);
+        }
+        __stcs(reinterpret_cast<uint4 *>(ref.dst + 16 * g), w0);
+        __stcs(reinterpret_cast<uint4 *>(ref.dst + 64 + 16 * g), w1);
+    }
+    __syncwarp();
+    return true;
+}
+
 template <bool kRotate>
 __global__ void __launch_bounds__(kCompressWarps * 32, 3) compress_kernel(const __grid_constant__ CompressJobs jobs) {
     __shared__ QEntry tab[kCells * kReplicas];
     __shared__ __align__(16) uint32_t stage[kCompressWarps][kVecPerWarp][20];
+    __shared__ __align__(16) float reduce[kCompressWarps][kVecPerWarp][40];
     build_qtable(tab);
     __syncthreads();
     pdl_trigger();
@@ -396,16 +682,31 @@ __global__ void __launch_bounds__(kCompressWarps * 32, 3) compress_kernel(const 
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     uint32_t *st = stage[warp][lane >> 2];
+    float *red = reduce[warp][lane >> 2];
+    const uint32_t tabq = (uint32_t)__cvta_generic_to_shared(tab + (lane & (kReplicas - 1)));
     const uint32_t t0 = jobs.j[0].n_tiles;
     const uint32_t n_tiles = t0 + (jobs.njobs > 1 ? jobs.j[1].n_tiles : 0u);
-    for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-        const bool second = tile >= t0;  // block-uniform
-        const CompressJob &jb = second ? jobs.j[1] : jobs.j[0];
-        const uint32_t t = second ? tile - t0 : tile;
-        if (!compress_warp<kRotate, false>(jb.x, jb.xs_b, jb.xs_h, jb.xs_l, jb.blocks, jb.bs_b, jb.bs_h, jb.div_h,
-                                           jb.div_l, jb.n_vec, t, tab, st))
+    // the next tile's inputs are loaded before the current tile is processed
+    uint32_t tile = blockIdx.x;
+    uint4 raw[4];
+    VecRef ref;
+    if (tile < n_tiles) load_vec(tile >= t0 ? jobs.j[1] : jobs.j[0], tile >= t0 ? tile - t0 : tile, raw, ref);
+    while (tile < n_tiles) {
+        const uint32_t next = tile + gridDim.x;
+        uint4 nraw[4];
+        VecRef nref;
+        if (next < n_tiles) load_vec(next >= t0 ? jobs.j[1] : jobs.j[0], next >= t0 ? next - t0 : next, nraw, nref);
+        if (!compress_fast<kRotate>(raw, ref, tabq, red, st)) {
+            const bool second = tile >= t0;  // block-uniform
+            const CompressJob &jb = second ? jobs.j[1] : jobs.j[0];
+            const uint32_t t = second ? tile - t0 : tile;
             compress_warp_exact<kRotate>(jb.x, jb.xs_b, jb.xs_h, jb.xs_l, jb.blocks, jb.bs_b, jb.bs_h, jb.div_h,
                                          jb.div_l, jb.n_vec, t, tab, st);
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) raw[c] = nraw[c];
+        ref = nref;
+        tile = next;
     }
 }
 
