@@ -400,6 +400,17 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __
 // a - b, rounded once (fma with multiplier -1 is exact before its rounding)
 __device__ __forceinline__ float2 sub2(float2 a, float2 b) { return __ffma2_rn(b, make_float2(-1.0f, -1.0f), a); }
 
+// Stride-1 butterfly of an fp16 pair (a, b): (RN(a + b), RN(a - b)) in fp32,
+// with the mixed-precision add/sub that widens a exactly before adding.
+__device__ __forceinline__ float2 bfly_h2(uint32_t w) {
+    float2 r;
+    asm("{\n .reg .b16 lo, hi;\n .reg .f32 fh;\n mov.b32 {lo, hi}, %2;\n cvt.f32.f16 fh, hi;\n"
+        " add.rn.f32.f16 %0, lo, fh;\n sub.rn.f32.f16 %1, lo, fh;\n}"
+        : "=f"(r.x), "=f"(r.y)
+        : "r"(w));
+    return r;
+}
+
 __device__ __forceinline__ float4 lds_f4(uint32_t a) {
     float4 r;
     // the table is constant after the kernel's set-up barrier: not volatile
@@ -446,7 +457,7 @@ __device__ __forceinline__ void load_vec(const CompressJob &jb, uint32_t tile, u
     const int g = lane & 3, vsub = lane >> 2;
     const uint32_t vi = tile * kVecPerTile + warp * kVecPerWarp + vsub;
     ref.valid = vi < jb.n_vec;
-    const uint32_t v = ref.valid ? vi : 0u;
+    const uint32_t v = min(vi, jb.n_vec - 1u);  // lanes past the end re-read the last vector, store nothing
     const uint32_t row = fdiv(v, jb.div_l);
     const int64_t l = v - row * jb.div_l.d;
     const uint32_t bq = fdiv(row, jb.div_h);
@@ -455,7 +466,7 @@ __device__ __forceinline__ void load_vec(const CompressJob &jb, uint32_t tile, u
     ref.dst = jb.blocks + (b * jb.bs_b + h * jb.bs_h + l) * kBlockBytes;
 #pragma unroll
     for (int c = 0; c < 4; ++c)
-        raw[c] = ref.valid ? __ldcs(reinterpret_cast<const uint4 *>(src + 32 * c)) : make_uint4(0, 0, 0, 0);
+        raw[c] = __ldcs(reinterpret_cast<const uint4 *>(src + 32 * c));
 }
 
 // Fast pass over the warp's eight vectors (lane layout as compress_warp).
@@ -473,10 +484,7 @@ __device__ __forceinline__ bool compress_fast(const uint4 (&raw)[4], const VecRe
     for (int c = 0; c < 4; ++c) {
         const uint32_t w[4] = {raw[c].x, raw[c].y, raw[c].z, raw[c].w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float2 f = h2_to_f2(w[j]);
-            P[c][j] = kRotate ? make_float2(__fadd_rn(f.x, f.y), __fsub_rn(f.x, f.y)) : f;  // stride 1
-        }
+        for (int j = 0; j < 4; ++j) P[c][j] = kRotate ? bfly_h2(w[j]) : h2_to_f2(w[j]);  // stride 1
     }
     if (kRotate) {
 #pragma unroll

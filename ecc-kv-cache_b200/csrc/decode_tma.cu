@@ -645,10 +645,16 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap mkc, const __grid_constant
         }
         // ---------------- tiles of the segment ----------------
         for (int u = 0; u < seg_tiles; ++u) {
-            bool ready = true;
-            if (lane == 0) ready = ok && mbar_wait(bars + 8 * stage, phase);
-            ready = __shfl_sync(0xffffffffu, ready, 0);
-            __syncwarp();  // orders the warp's reads of the stage after lane 0's wait
+            // every lane polls the stage's mbarrier once (one warp-wide
+            // try_wait, no divergence); a warp that does not find the phase
+            // complete in every lane takes the bounded wait in lane 0
+            bool ready = ok;
+            if (ok && !__all_sync(0xffffffffu, mbar_try(bars + 8 * stage, phase))) {
+                bool r = true;
+                if (lane == 0) r = mbar_wait(bars + 8 * stage, phase);
+                ready = __shfl_sync(0xffffffffu, r, 0);
+            }
+            __syncwarp();  // orders the warp's reads of the stage after the wait
             if (ok && !ready) jfail = j;
             ok = ok && ready;
             if (ok) L.tile(ring + stage * kStageBytes, (int)min((int64_t)kTile, seq_len - tok0));
