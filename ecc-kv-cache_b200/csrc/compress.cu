@@ -41,7 +41,14 @@ namespace ecc {
 constexpr unsigned kFull = 0xffffffffu;
 constexpr int kCells = 192;       // u cells of width 1/8: cell = rint(8u + 96)
 constexpr int kReplicas = 8;      // one table copy per (lane % 8): conflict-free LDS.128
-constexpr float kBand = 4e-6f;    // exact-recompute band around each threshold
+constexpr float kBand = 4e-6f;    // exact-recompute band around each threshold (u = RN(d * rs))
+// Band of the packed fast pass, whose side test is w = RN(d * rs - thr) with
+// one rounding.  Near a threshold |d * rs - d / scale| <= 1.7e-7, the
+// reference's RN(d / scale) adds <= 1.2e-7, its flip point lies within 1e-7
+// of the exact midpoint and thr within 1.2e-7 of it: a decision with
+// |w| >= 5.2e-7 is the reference's.  A CPU stress of 4 M near-threshold
+// quotients sees wrong decisions only for |w| < 2.8e-7.
+constexpr float kBandFast = 1.5e-6f;
 constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: fma(u, 8, kMagic + 96) rounds 8u+96 to an integer
 constexpr int kCompressWarps = 8;
 constexpr int kVecPerWarp = 8;
@@ -471,7 +478,7 @@ __device__ __forceinline__ void load_vec(const CompressJob &jb, uint32_t tile, u
 
 // Fast pass over the warp's eight vectors (lane layout as compress_warp).
 // Returns false, having written nothing, when any vector of the warp needs
-// the exact pass: a quotient within kBand of a decision threshold, a std
+// the exact pass: a quotient within kBandFast of a decision threshold, a std
 // near an fp32 rounding midpoint, or a non-finite scale or zero point.
 // `tabq` is the shared-window address of this lane's replica of entry 0,
 // `red` the vector's reduction area, `st` its staging row.
@@ -595,7 +602,7 @@ __device__ __forceinline__ bool compress_fast(const uint4 (&raw)[4], const VecRe
     //     boundary, where both cells give the same code because every
     //     threshold is >= 0.09 cells from a boundary.
     //   * w = RN(d * rs - thr) decides the side of the cell's threshold;
-    //     |w| < kBand sends the warp to the exact pass.  m = sign mask of w
+    //     |w| < kBandFast sends the warp to the exact pass.  m = sign mask of w
     //     picks code and centroid with integer ops (m = -1: below).
     //   * Codes are shifted into their word and sign bits of eps into
     //     `negs` (funnel shift) in descending element order, so nibble i
@@ -624,7 +631,7 @@ __device__ __forceinline__ bool compress_fast(const uint4 (&raw)[4], const VecRe
             const float4 e1 = lds_f4(tbase + (uint32_t)__float_as_int(T.y) * (uint32_t)(kReplicas * sizeof(QEntry)));
             const float4 e0 = lds_f4(tbase + (uint32_t)__float_as_int(T.x) * (uint32_t)(kReplicas * sizeof(QEntry)));
             const float w1 = __fmaf_rn(D.y, rs, -e1.x), w0 = __fmaf_rn(D.x, rs, -e0.x);
-            band = band || (fabsf(w1) < kBand) || (fabsf(w0) < kBand);
+            band = band || (fabsf(w1) < kBandFast) || (fabsf(w0) < kBandFast);
             const uint32_t m1 = (uint32_t)(__float_as_int(w1) >> 31), m0 = (uint32_t)(__float_as_int(w0) >> 31);
             const float cq1 = __uint_as_float((__float_as_uint(e1.y) & m1) | (__float_as_uint(e1.z) & ~m1));
             const float cq0 = __uint_as_float((__float_as_uint(e0.y) & m0) | (__float_as_uint(e0.z) & ~m0));

@@ -9,6 +9,7 @@ import pytest
 import workloads
 
 CELLS, MAGIC, BAND = 192, np.float32(12582912.0), np.float32(4e-6)
+BAND_FAST = np.float32(1.5e-6)  # the packed fast pass's band (compress.cu kBandFast)
 
 
 def test_division_by_sqrt128_sampled(oracle):
@@ -78,3 +79,54 @@ def test_table_quantiser_equals_argmin(oracle):
     q = np.where(band, exact, q)
     assert np.array_equal(q, q_ref)
     assert band.sum() < 0.001 * band.size
+
+
+def _fast_pass_codes(d, scale, C, tab):
+    """The packed fast pass's quantiser: cell from fma(d, 8 rs, magic + 96),
+    side from w = fma(d, rs, -thr), band |w| < BAND_FAST.  float64 holds the
+    exact products d*rs (48-bit), so one rounding to float32 emulates each fma."""
+    thr = np.array([t[0] for t in tab], np.float32)
+    qlo = np.array([t[3] for t in tab], np.int64)
+    rs = (np.float64(1.0) / scale.astype(np.float64)).astype(np.float32)
+    rs8 = (rs * np.float32(8.0)).astype(np.float32)
+    t = (d.astype(np.float64) * rs8.astype(np.float64)[..., None] + np.float64(MAGIC + np.float32(96.0))).astype(np.float32)
+    cell = t.view(np.int32) - np.array([MAGIC], np.float32).view(np.int32)[0]
+    assert cell.min() >= 0 and cell.max() < CELLS  # no clamp in the kernel
+    w = (d.astype(np.float64) * rs.astype(np.float64)[..., None] - thr[cell].astype(np.float64)).astype(np.float32)
+    return qlo[cell] + (w >= 0), np.abs(w) < BAND_FAST
+
+
+def test_fast_pass_quantiser_equals_argmin(oracle):
+    """The packed fast pass's decision rule on real compress inputs: outside
+    its band the codes are the oracle's first-index argmin."""
+    C = oracle.LM_CENTROIDS
+    tab, _, _ = _table(C)
+    x16 = np.concatenate([workloads.make_heavy(seed=32, n=2048).numpy(),
+                          workloads.make_c1(seed=5, L=64)[0].reshape(-1, 128).numpy(),
+                          workloads.make_edge().numpy()])
+    r = oracle.compress_np(x16, rotate=True)
+    d = (r["x_rot"] - r["zero"][:, None]).astype(np.float32)
+    q, band = _fast_pass_codes(d, r["scale"], C, tab)
+    assert np.array_equal(q[~band], r["q"][~band])
+    assert band.sum() < 0.001 * band.size
+
+
+def test_fast_pass_band_near_thresholds(oracle):
+    """Quotients placed within 3e-6 of every decision threshold over scales
+    1e-3..1e3: no fast-pass decision outside the band differs from the
+    reference's RN(d / scale) argmin, and the closest wrong decision of an
+    unbanded rule stays far inside the band."""
+    C = oracle.LM_CENTROIDS.astype(np.float32)
+    tab, m, _ = _table(C)
+    rng = np.random.default_rng(5)
+    n = 1_000_000
+    j = rng.integers(0, 15, n)
+    scale = np.exp(rng.uniform(np.log(1e-3), np.log(1e3), n)).astype(np.float32)
+    d = ((m[j].astype(np.float64) + rng.uniform(-3e-6, 3e-6, n)) * scale.astype(np.float64)).astype(np.float32)
+    xn = (d.astype(np.float64) / scale.astype(np.float64)).astype(np.float32)
+    q_ref = np.abs((xn[:, None] - C[None, :]).astype(np.float32)).argmin(1)
+    rs = (np.float64(1.0) / scale.astype(np.float64)).astype(np.float32)
+    w = (d.astype(np.float64) * rs.astype(np.float64) - m[j].astype(np.float64)).astype(np.float32)
+    wrong = (j + (w >= 0)) != q_ref
+    assert not np.any(wrong & (np.abs(w) >= BAND_FAST))
+    assert np.abs(w[wrong]).max() < BAND_FAST / 4
