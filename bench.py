@@ -49,7 +49,7 @@ COMPRESS_TOKENS = 131072
 # algorithmic 384 B; the output blocks of a launch partly stay in the 126 MB L2
 # when the launch ends, so DRAM writes are counted below 128 B per vector.
 DECODE_DRAM_BYTES_PER_UNIT = (1.074092e9 + 4.958208e6) / (B * HKV * 65542)
-COMPRESS_DRAM_BYTES_PER_VECTOR = (268.526080e6 + 97.954304e6) / (HKV * COMPRESS_TOKENS)
+COMPRESS_DRAM_BYTES_PER_VECTOR = (268.652032e6 + 97.288704e6) / (HKV * COMPRESS_TOKENS)
 
 
 def peaks():
@@ -445,6 +445,153 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+LONG_B, LONG_CTX = 16, 131072
+
+
+def run_long(args):
+    """Long-context decode at the Llama-3.1-8B long-context shapes: batch 16,
+    32 query heads over 8 kv heads, 131072-token compressed context per
+    sequence; a step is one layer's decode attention (append the new K/V
+    token, fused decode).  The work is split over the ranks (strong scaling,
+    the total work is fixed as N grows):
+
+    * ``--long kv``: rank r holds kv heads [8r/N, 8(r+1)/N) of every sequence
+      and their query heads; attention needs no exchange, and one all-gather
+      of the ranks' fp16 outputs assembles the layer's attention output.
+    * ``--long seq``: rank r holds tokens [rL/N, (r+1)L/N) of every (b, kv head)
+      row (the last rank also the appended ones); each rank merges its split
+      partials into one record per (b, q head), the records are all-gathered
+      and merged (LSE combine).
+    """
+    import torch
+    import custom_ecc_cuda as ops
+    import workloads
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    mode = args.long
+    if HKV % world:
+        raise SystemExit(f"--long: {world} ranks do not divide {HKV} kv heads")
+    K, W = args.steps, args.warmup
+    Bl = LONG_B
+    hkv_l = HKV // world if mode == "kv" else HKV
+    hq_l = HQ // world if mode == "kv" else HQ
+    chunk_ctx = LONG_CTX if mode == "kv" else LONG_CTX // world
+    last = rank == world - 1
+    grows = mode == "kv" or last  # this rank appends the new tokens
+    cap = chunk_ctx + W + K + 8
+    gen = torch.Generator(device=dev).manual_seed(4321 + rank)
+    kpool = torch.empty((Bl, hkv_l, cap, BLOCK), dtype=torch.uint8, device=dev)
+    vpool = torch.empty_like(kpool)
+    fill = 4096
+    for t0 in range(0, chunk_ctx, fill):
+        for pool in (kpool, vpool):
+            x = torch.randn((Bl, hkv_l, fill, D), generator=gen, device=dev).half()
+            ops.compress_into(x, pool, pos=t0, rotate=True)
+            del x
+    torch.cuda.synchronize()
+    n = W + K
+    new_k = torch.randn((n, Bl, hkv_l, 1, D), generator=gen, device=dev).half()
+    new_v = torch.randn((n, Bl, hkv_l, 1, D), generator=gen, device=dev).half()
+    # every rank draws the full query set of a step and keeps its heads
+    qs = torch.stack([workloads.make_queries(i, Bl, HQ, device=dev) for i in range(n)])
+    if mode == "kv":
+        qs = qs[:, :, rank * hq_l:(rank + 1) * hq_l].contiguous()
+    out = torch.empty((Bl, hq_l, 1, D), dtype=torch.float16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    if world > 1:
+        import torch.distributed as dist
+        if mode == "kv":
+            gout = torch.empty((world, Bl, hq_l, 1, D), dtype=torch.float16, device=dev)
+        else:
+            nspl = max(ops.default_splits(Bl, HKV, s) for s in (chunk_ctx, cap)) + 1
+            rec = torch.empty((Bl, HQ, ops.RECORD_FLOATS), dtype=torch.float32, device=dev)
+            grec = torch.empty((world, Bl, HQ, ops.RECORD_FLOATS), dtype=torch.float32, device=dev)
+
+    def step(i, local_len, events=None):
+        if grows:
+            ops.compress_pair_into(new_k[i], new_v[i], kpool, vpool, pos=local_len - 1, rotate=True)
+        if events is not None:
+            events[0].record(stream)
+        if world == 1 or mode == "kv":
+            ops.decode_attention(qs[i], kpool, vpool, seq_len=local_len, rotate_q=True, unrotate_out=True, out=out)
+            if events is not None:
+                events[1].record(stream)
+            if world > 1:
+                dist.all_gather_into_tensor(gout, out, group=dist.group.WORLD)
+        else:
+            pm, pl, po = ops.decode_partials(qs[i], kpool, vpool, seq_len=local_len, num_splits=nspl, rotate_q=True)
+            if events is not None:
+                events[1].record(stream)
+            ops.lse_merge_to_record(pm, pl, po, out=rec)
+            dist.all_gather_into_tensor(grec, rec, group=dist.group.WORLD)
+            ops.lse_merge_records(grec, unrotate_out=True, out=out)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    try:
+        gpu_id = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        gpu_id = str(local)
+    clk = ClockSampler(gpu_id).__enter__()
+    ln = chunk_ctx
+    for i in range(W):
+        ln += 1 if grows else 0
+        step(i, ln)
+    barrier()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ln0 = ln
+    clk.mark_start()
+    start.record(stream)
+    for i in range(K):
+        ln += 1 if grows else 0
+        step(W + i, ln, ev[i])
+    stop.record(stream)
+    barrier()
+    clk.mark_stop()
+    clk.__exit__(None, None, None)
+    total_ms = start.elapsed_time(stop)
+    dec_ms = sum(a.elapsed_time(b) for a, b in ev) / K
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = t.item()
+    # K + V blocks the whole job reads per step (mean over the timed steps)
+    job_ctx = LONG_CTX + W + (K + 1) / 2.0
+    job_bytes = Bl * HKV * job_ctx * 2 * BLOCK
+    rank_ctx = (ln0 + (K + 1) / 2.0) if grows else float(chunk_ctx)
+    rank_bytes = Bl * hkv_l * rank_ctx * 2 * BLOCK
+    peak, peak_kind = peaks()
+    if rank == 0:
+        line = {
+            "metric": "long-context ECC-INT4 decode attention: job HBM GB/s; decode tok/s", "value":
+                job_bytes * K / (total_ms / 1e3) / 1e9, "unit": "GB/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "strong", "dtype": "fp32",
+            "data": "synthetic",
+            "config": {"workload": f"long-context decode step: B{Bl} Hq{HQ}/Hkv{HKV} D{D}, {LONG_CTX}-token "
+                                   f"compressed context per sequence, one layer, append + fused decode",
+                       "batch": Bl, "context": LONG_CTX,
+                       "parallelism": {"kv": "kv-head", "seq": "seq-chunk"}[mode] if world > 1 else "single",
+                       "per_rank": f"{hkv_l} kv heads x {chunk_ctx} tokens"},
+            "decode_tok_s": Bl * K / (total_ms / 1e3),
+            "rank0_decode_gbs": rank_bytes / (dec_ms / 1e3) / 1e9, "peak": peak, "peak_kind": peak_kind,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 # ---------------------------------------------------------------------------
 # CPU baseline / reference arm: the oracle port of the reference's CPU path
 # ---------------------------------------------------------------------------
@@ -523,6 +670,8 @@ def main():
                     help="run only the compress benchmark and print its JSON object")
     ap.add_argument("--model-e2e", action="store_true",
                     help="run the Llama-3.1-8B-shaped 32k-prompt generate() comparison and print its JSON object")
+    ap.add_argument("--long", choices=["kv", "seq"], default=None,
+                    help="long-context decode (B16, 131072 tokens) sharded by kv head or by sequence chunk")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
@@ -532,6 +681,8 @@ def main():
         run_compress_only(args)
     elif args.model_e2e:
         run_model_e2e(args)
+    elif args.long:
+        run_long(args)
     else:
         run_ours(args)
 
