@@ -293,10 +293,10 @@ def run_ours(args):
 
     if world > 1:
         import torch.distributed as dist
+        from custom_kv.sharding import ShardedDecode
         # two-level combine: each rank merges its splits into one record
         # {m, l, o[128]} per (b, q head); one all-gather of the records
-        rec = torch.empty((B, HQ, ops.RECORD_FLOATS), dtype=torch.float32, device=dev)
-        grec = torch.empty((world, B, HQ, ops.RECORD_FLOATS), dtype=torch.float32, device=dev)
+        shard = ShardedDecode("seq", pg)
 
     def step(i, seq_len, events=None):
         # append the new token (sharded run: the last rank owns the newest chunk)
@@ -312,12 +312,8 @@ def run_ours(args):
         else:
             # ranks before the last hold a full, fixed chunk; the last rank's grows
             local_len = seq_len if rank == world - 1 else CTX
-            pm, pl, po = ops.decode_partials(qs[i], kpool, vpool, seq_len=local_len, num_splits=nspl, rotate_q=True)
-            if events is not None:
-                events[1].record(stream)
-            ops.lse_merge_to_record(pm, pl, po, out=rec)
-            dist.all_gather_into_tensor(grec, rec, group=pg)
-            ops.lse_merge_records(grec, unrotate_out=True, out=out)
+            shard.step(qs[i], kpool, vpool, local_len, num_splits=nspl, out=out,
+                       mark=events[1] if events is not None else None)
 
     def barrier():
         if world > 1:
@@ -536,31 +532,23 @@ def run_long(args):
     stream = torch.cuda.current_stream(dev)
     if world > 1:
         import torch.distributed as dist
-        if mode == "kv":
-            gout = torch.empty((world, Bl, hq_l, 1, D), dtype=torch.float16, device=dev)
-        else:
-            nspl = max(ops.default_splits(Bl, HKV, s) for s in (chunk_ctx, cap)) + 1
-            rec = torch.empty((Bl, HQ, ops.RECORD_FLOATS), dtype=torch.float32, device=dev)
-            grec = torch.empty((world, Bl, HQ, ops.RECORD_FLOATS), dtype=torch.float32, device=dev)
+        from custom_kv.sharding import ShardedDecode
+        shard = ShardedDecode(mode)
+        nspl = max(ops.default_splits(Bl, HKV, s) for s in (chunk_ctx, cap)) + 1
+        full = torch.empty((Bl, HQ, 1, D), dtype=torch.float16, device=dev)  # the layer's whole output
 
     def step(i, local_len, events=None):
         if grows:
             ops.compress_pair_into(new_k[i], new_v[i], kpool, vpool, pos=local_len - 1, rotate=True)
         if events is not None:
             events[0].record(stream)
-        if world == 1 or mode == "kv":
+        if world == 1:
             ops.decode_attention(qs[i], kpool, vpool, seq_len=local_len, rotate_q=True, unrotate_out=True, out=out)
             if events is not None:
                 events[1].record(stream)
-            if world > 1:
-                dist.all_gather_into_tensor(gout, out, group=dist.group.WORLD)
         else:
-            pm, pl, po = ops.decode_partials(qs[i], kpool, vpool, seq_len=local_len, num_splits=nspl, rotate_q=True)
-            if events is not None:
-                events[1].record(stream)
-            ops.lse_merge_to_record(pm, pl, po, out=rec)
-            dist.all_gather_into_tensor(grec, rec, group=dist.group.WORLD)
-            ops.lse_merge_records(grec, unrotate_out=True, out=out)
+            shard.step(qs[i], kpool, vpool, local_len, num_splits=nspl, out=full,
+                       mark=events[1] if events is not None else None)
 
     def barrier():
         if world > 1:

@@ -1,0 +1,143 @@
+"""Multi-GPU decode over a layer's compressed cache: one process per GPU
+(torch.distributed, NCCL over NVLink), two layouts of the cache.
+
+* **kv-head sharding** (``mode="kv"``): rank r holds kv heads
+  [r*Hkv/N, (r+1)*Hkv/N) of every sequence and serves their query heads.
+  Attention needs no exchange; one all-gather of the ranks' fp16 outputs
+  assembles the layer's attention output [B, Hq, 1, 128].
+* **sequence-chunk sharding** (``mode="seq"``): rank r holds tokens
+  [r*L/N, (r+1)*L/N) of every (sequence, kv head) row; new tokens are
+  appended on the last rank.  Each rank computes split partials (m, l, o) of
+  its chunk, merges them into one 130-float record {m, l, o[128]} per
+  (sequence, query head), the records are all-gathered and merged (the
+  log-sum-exp combine of flash-decoding).
+
+The reference keeps everything on one device (custom_kv/cache.py:79-84); this
+module is the multi-GPU layer around the same fused decode.  Every rank takes
+the same collective steps in the same order.
+"""
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+D = 128
+
+
+def kv_head_range(rank: int, world: int, hkv: int) -> Tuple[int, int]:
+    """kv heads [lo, hi) of `rank` under kv-head sharding (world must divide hkv)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("rank out of range")
+    if hkv % world:
+        raise ValueError(f"{world} ranks do not divide {hkv} kv heads")
+    per = hkv // world
+    return rank * per, (rank + 1) * per
+
+
+def q_head_range(rank: int, world: int, hkv: int, hq: int) -> Tuple[int, int]:
+    """Query heads [lo, hi) served by `rank` under kv-head sharding (the GQA
+    groups of its kv heads, HF repeat_kv order: kv head = q head // (hq/hkv))."""
+    if hq % hkv:
+        raise ValueError("query heads must be a multiple of kv heads")
+    lo, hi = kv_head_range(rank, world, hkv)
+    g = hq // hkv
+    return lo * g, hi * g
+
+
+def seq_chunk_range(rank: int, world: int, seq_len: int) -> Tuple[int, int]:
+    """Tokens [start, stop) of `rank` under sequence-chunk sharding of a
+    context of seq_len tokens: contiguous chunks, the first seq_len % world
+    ranks one token longer."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("rank out of range")
+    if seq_len < 0:
+        raise ValueError("seq_len must be >= 0")
+    base, extra = divmod(seq_len, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def _all_gather(out: torch.Tensor, inp: torch.Tensor, group) -> None:
+    """out[r] = rank r's inp (out [world, *inp.shape])."""
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, inp, group=group)
+    else:
+        dist.all_gather(list(out.unbind(0)), inp, group=group)
+
+
+class ShardedDecode:
+    """One decode step of a sharded layer on this rank.
+
+    ``ops`` provides the per-rank compute (default: the CUDA ops of
+    custom_ecc_cuda: decode_attention, decode_partials, lse_merge_to_record,
+    lse_merge_records, RECORD_FLOATS).  Buffers for the exchange are made on
+    first use and reused, so a steady decode loop allocates nothing.
+    """
+
+    def __init__(self, mode: str, group=None, ops=None):
+        if mode not in ("kv", "seq"):
+            raise ValueError("mode must be 'kv' or 'seq'")
+        if ops is None:
+            import custom_ecc_cuda as ops  # noqa: F811
+        self.mode = mode
+        self.ops = ops
+        self.group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        self._bufs: dict = {}
+
+    def _buf(self, key, shape, dtype, device):
+        b = self._bufs.get(key)
+        if b is None or b.shape != shape or b.dtype != dtype or b.device != device:
+            b = torch.empty(shape, dtype=dtype, device=device)
+            self._bufs[key] = b
+        return b
+
+    def step(self, query: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, local_len: int,
+             num_splits: int = 0, rotate_q: bool = True, unrotate_out: bool = True,
+             out: Optional[torch.Tensor] = None, mark: Optional[torch.cuda.Event] = None) -> torch.Tensor:
+        """Attention output of this step for every query head, [B, Hq, 1, 128] fp16.
+
+        kv mode: ``query`` holds this rank's query heads [B, Hq/N, 1, 128] and
+        the pools its kv heads; seq mode: ``query`` holds every head and the
+        pools this rank's token chunk, of which the first ``local_len`` tokens
+        are valid.  ``num_splits`` (seq mode) is the split count of the local
+        partials; give one that covers every local length of the run so that
+        the exchange shapes stay fixed.  ``mark``, if given, is recorded on
+        the current stream after this rank's own attention work and before the
+        exchange (to time the two apart)."""
+        ops, W = self.ops, self.world
+        B, hq_l = query.shape[0], query.shape[1]
+        if self.mode == "kv":
+            loc = self._buf("loc", (B, hq_l, 1, D), torch.float16, query.device)
+            ops.decode_attention(query, k_pool, v_pool, seq_len=local_len, rotate_q=rotate_q,
+                                 unrotate_out=unrotate_out, out=loc)
+            if mark is not None:
+                mark.record()
+            if W == 1:
+                res = loc
+            else:
+                g = self._buf("gather", (W, B, hq_l, 1, D), torch.float16, query.device)
+                _all_gather(g, loc, self.group)
+                res = g.permute(1, 0, 2, 3, 4).reshape(B, W * hq_l, 1, D)
+            if out is None:
+                return res.clone() if res is loc else res
+            out.copy_(res)
+            return out
+        # sequence chunks
+        if num_splits <= 0:
+            raise ValueError("seq mode needs a fixed num_splits")
+        pm, pl, po = ops.decode_partials(query, k_pool, v_pool, seq_len=local_len, num_splits=num_splits,
+                                         rotate_q=rotate_q)
+        rec = self._buf("rec", (B, hq_l, ops.RECORD_FLOATS), torch.float32, query.device)
+        ops.lse_merge_to_record(pm, pl, po, out=rec)
+        if mark is not None:
+            mark.record()
+        grec = self._buf("grec", (W, B, hq_l, ops.RECORD_FLOATS), torch.float32, query.device)
+        if W == 1:
+            grec[0].copy_(rec)
+        else:
+            _all_gather(grec, rec, self.group)
+        return ops.lse_merge_records(grec, unrotate_out=unrotate_out, out=out)
