@@ -198,7 +198,8 @@ __device__ __forceinline__ void wht_group(float (&v)[4][8], int g) {
             const float x = v[c][i];
             const float q0 = __fmul_rn(x, kInvSqrt128);
             const float rem = __fmaf_rn(-q0, kSqrt128, x);
-            v[c][i] = __fmaf_rn(rem, kInvSqrt128, q0);
+            // x = +-inf: the remainder is inf - inf = NaN, the quotient is +-inf
+            v[c][i] = fabsf(q0) == INFINITY ? q0 : __fmaf_rn(rem, kInvSqrt128, q0);
         }
 }
 
@@ -725,6 +726,102 @@ __global__ void __launch_bounds__(kCompressWarps * 32, 3) compress_kernel(const 
     }
 }
 
+// ---- calibrated compress ---------------------------------------------------
+// Fixed quantiser parameters instead of per-vector statistics: the per-layer
+// scale, zero point and alpha of a calibration config (custom_kv/calibration.py
+// :232-237 computes them; the quantiser is ops_cpu.lloyd_max_quantize_cpu,
+// ops_cpu.py:78-109, called with those scalars).  Per element:
+// d = RN(x - zero), q = first-index argmin_k |RN(d / scale) - C[k]|,
+// k~ = RN(RN(C[q] * scale) + zero), bit = (x - k~ >= 0); every block stores
+// fp16 of the fp32 scale, zero and alpha.  |d / scale| is unbounded here, so
+// the table cell is clamped (the end cells hold no threshold); an element
+// within kBand of a threshold, or non-finite, takes the IEEE quotient and the
+// full argmin.  Scalar code: this path is an option, not the hot path.
+struct CalParams {
+    float scale, zero, alpha, rs;  // rs = RN(1 / scale)
+};
+
+template <bool kRotate>
+__global__ void __launch_bounds__(kCompressWarps * 32, 3)
+    compress_cal_kernel(const __grid_constant__ CompressJob jb, const CalParams cp) {
+    __shared__ QEntry tab[kCells * kReplicas];
+    __shared__ __align__(16) uint32_t stage[kCompressWarps][kVecPerWarp][20];
+    build_qtable(tab);
+    __syncthreads();
+    pdl_trigger();
+    pdl_wait();
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane & 3;
+    uint32_t *st = stage[warp][lane >> 2];
+    const QEntry *mytab = tab + (lane & (kReplicas - 1));
+    for (uint32_t tile = blockIdx.x; tile < jb.n_tiles; tile += gridDim.x) {
+        uint4 raw[4];
+        VecRef ref;
+        load_vec(jb, tile, raw, ref);
+        float v[4][8];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint32_t w[4] = {raw[c].x, raw[c].y, raw[c].z, raw[c].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float2 f = h2_to_f2(w[j]);
+                v[c][2 * j] = f.x;
+                v[c][2 * j + 1] = f.y;
+            }
+        }
+        if (kRotate) wht_group(v, g);
+        uint32_t codes[4] = {0u, 0u, 0u, 0u};
+        uint32_t bits = 0u;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float xv = v[c][i];
+                const float d = __fsub_rn(xv, cp.zero);
+                const float u = __fmul_rn(d, cp.rs);
+                // nearest cell, clamped; NaN lands in cell 0 (no threshold, NaN test below)
+                const int cell = (int)fminf(fmaxf(rintf(__fmaf_rn(u, 8.0f, 96.0f)), 0.0f), (float)(kCells - 1));
+                const QEntry e = mytab[cell * kReplicas];
+                int q;
+                float cq;
+                if (!(fabsf(__fsub_rn(u, e.thr)) >= kBand)) {  // near a threshold, or u not finite
+                    q = exact_code(d, cp.scale);
+                    cq = lm(0);
+#pragma unroll
+                    for (int k = 1; k < 16; ++k) cq = (q == k) ? lm(k) : cq;
+                } else {
+                    const bool hi = u > e.thr;
+                    q = e.q_lo + (hi ? 1 : 0);
+                    cq = hi ? e.c_hi : e.c_lo;
+                }
+                const float kt = __fadd_rn(__fmul_rn(cq, cp.scale), cp.zero);
+                bits |= (__fsub_rn(xv, kt) >= 0.0f ? 1u : 0u) << (8 * c + i);
+                codes[c] |= (uint32_t)q << (4 * i);
+            }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            st[4 * c + g] = codes[c];
+            reinterpret_cast<uint8_t *>(st + 16)[4 * c + g] = (uint8_t)(bits >> (8 * c));
+        }
+        __syncwarp();
+        if (ref.valid) {
+            const uint4 w0 = *reinterpret_cast<const uint4 *>(st + 4 * g);
+            uint4 w1 = make_uint4(0u, 0u, 0u, 0u);
+            if (g == 0) {
+                w1 = *reinterpret_cast<const uint4 *>(st + 16);
+            } else if (g == 1) {
+                const uint32_t hs = __half_as_ushort(__float2half_rn(cp.scale));
+                const uint32_t hz = __half_as_ushort(__float2half_rn(cp.zero));
+                const uint32_t ha = __half_as_ushort(__float2half_rn(cp.alpha));
+                w1 = make_uint4(hs | (hz << 16), ha, 0u, 0u);
+            }
+            __stcs(reinterpret_cast<uint4 *>(ref.dst + 16 * g), w0);
+            __stcs(reinterpret_cast<uint4 *>(ref.dst + 64 + 16 * g), w1);
+        }
+        __syncwarp();
+    }
+}
+
 // ---- generic WHT (any power of two d <= 1024), one CTA per row ------------
 template <typename T>
 __device__ __forceinline__ float to_f(T v);
@@ -950,6 +1047,31 @@ extern "C" int ecc_compress_strided_pair(const void *x0_f16, int64_t x0s_b, int6
     return launch_jobs(jobs, rotate, stream);
 }
 
+extern "C" int ecc_compress_strided_calibrated(const void *x_f16, int64_t xs_b, int64_t xs_h, int64_t xs_l,
+                                               void *blocks, int64_t bs_b, int64_t bs_h, int B, int H, int64_t L,
+                                               int rotate, float scale, float zero, float alpha,
+                                               ecc_stream_t stream) {
+    if (!(scale > 0.0f) || !std::isfinite(scale) || !std::isfinite(zero) || !std::isfinite(alpha))
+        return ECC_ERR_PARAM;
+    CompressJob jb{};
+    int64_t n = 0;
+    int rc = make_job(x_f16, xs_b, xs_h, xs_l, blocks, bs_b, bs_h, B, H, L, &jb, &n);
+    if (rc != ECC_OK || n == 0) return rc;
+    DevInfo *di = nullptr;
+    rc = dev_info(&di);
+    if (rc != ECC_OK) return rc;
+    const float rs = 1.0f / scale;  // IEEE single division: RN(1 / scale)
+    if (!std::isfinite(rs)) return ECC_ERR_PARAM;
+    const CalParams cp{scale, zero, alpha, rs};
+    const int64_t grid = std::min<int64_t>(jb.n_tiles, (int64_t)di->sms * 3);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const cudaError_t e =
+        rotate ? launch_pdl(compress_cal_kernel<true>, dim3((unsigned)grid), dim3(kCompressWarps * 32), 0, s, jb, cp)
+               : launch_pdl(compress_cal_kernel<false>, dim3((unsigned)grid), dim3(kCompressWarps * 32), 0, s, jb, cp);
+    if (e != cudaSuccess) return ECC_ERR_LAUNCH;
+    return launch_status();
+}
+
 extern "C" int ecc_compress(const void *x_f16, void *blocks, int64_t n, int rotate, ecc_stream_t stream) {
     if (n < 0) return ECC_ERR_SHAPE;
     return ecc_compress_strided(x_f16, 0, 0, kD, blocks, 0, 0, 1, 1, n, rotate, stream);
@@ -1031,6 +1153,7 @@ extern "C" const char *ecc_strerror(int code) {
         case ECC_ERR_CUDA: return "CUDA runtime call failed";
         case ECC_ERR_DEVICE: return "no usable CUDA device";
         case ECC_ERR_SCRATCH_LIMIT: return "request exceeds the library's static decode scratch";
+        case ECC_ERR_PARAM: return "quantiser parameter not finite or scale not positive";
         default: return "unknown error";
     }
 }

@@ -26,7 +26,7 @@ import torch
 __all__ = [
     "hadamard_rotate", "compress_and_store", "get_block_metadata", "rotate_and_compress",
     "compress_into", "decode_attention", "decode_partials", "lse_merge", "dequantize", "pack_soa",
-    "decode_workspace_size", "default_splits", "library_path", "EccError",
+    "decode_workspace_size", "default_splits", "library_path", "EccError", "compress_calibrated_into",
 ]
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -62,6 +62,8 @@ def _load():
         "ecc_compress_strided": ([p, i64, i64, i64, p, i64, i64, i32, i32, i64, i32, p], i32),
         "ecc_compress_strided_pair": ([p, i64, i64, i64, p, i64, i64, p, i64, i64, i64, p, i64, i64, i32, i32, i64,
                                        i32, p], i32),
+        "ecc_compress_strided_calibrated": ([p, i64, i64, i64, p, i64, i64, i32, i32, i64, i32, f32, f32, f32, p],
+                                            i32),
         "ecc_get_block_metadata": ([p, i64, i64, p, p], i32),
         "ecc_dequantize": ([p, p, i64, p], i32),
         "ecc_pack_soa": ([p, i64, p, i64, p, i64, p, i64, p], i32),
@@ -236,6 +238,22 @@ def _compress_dst(x: torch.Tensor, pool: torch.Tensor, pos: int, name: str):
     if x.device != pool.device:
         raise RuntimeError("x and pool must be on the same device")
     return (pool[..., pos:, :] if pos else pool), bs
+
+
+def compress_calibrated_into(x: torch.Tensor, pool: torch.Tensor, scale: float, zero: float, alpha: float,
+                             pos: int = 0, rotate: bool = True) -> None:
+    """compress_into with fixed quantiser parameters -- a layer's (scale, zero,
+    alpha) from a calibration config (custom_kv/calibration.py:232-237) -- in
+    place of each vector's own statistics: the arithmetic of
+    ops_cpu.lloyd_max_quantize_cpu(x_rot, scale, zero) + compute_syndrome_cpu,
+    every block storing fp16 of the fp32 scale, zero and alpha."""
+    dst, bs = _compress_dst(x, pool, pos, "x")
+    B, H, L, _ = x.shape
+    with torch.cuda.device(x.device):
+        rc = _lib.ecc_compress_strided_calibrated(_ptr(x), x.stride(0), x.stride(1), x.stride(2), _ptr(dst), bs[0],
+                                                  bs[1], B, H, L, int(bool(rotate)), float(scale), float(zero),
+                                                  float(alpha), _stream(x))
+    _check(rc, "compress_calibrated_into")
 
 
 def compress_pair_into(k: torch.Tensor, v: torch.Tensor, kpool: torch.Tensor, vpool: torch.Tensor, pos: int = 0,

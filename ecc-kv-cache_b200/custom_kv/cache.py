@@ -74,6 +74,12 @@ class ErrorCorrectedCache(_HFCache):
 
         with ecc_cache(model, max_cache_len=32768) as cache:
             out = model.generate(**inputs, past_key_values=cache, max_new_tokens=200)
+
+    ``calibration`` (a config of custom_kv/calibration.py, e.g. from
+    load_calibration_config): the key blocks of every layer the config lists
+    are quantised with that layer's calibrated scale / zero point and store its
+    alpha, instead of each vector's own statistics; values keep per-vector
+    statistics (the config calibrates keys only).
     """
 
     def __init__(self, config, batch_size: int = 1, max_cache_len: int = 128_000, device: Optional[str] = None,
@@ -158,7 +164,11 @@ class ErrorCorrectedCache(_HFCache):
         k16 = key_states if key_states.dtype == torch.float16 else key_states.to(torch.float16)
         v16 = value_states if value_states.dtype == torch.float16 else value_states.to(torch.float16)
         kp, vp = self.layer_pools(layer_idx)
-        if self.rotate_values:
+        kcal = self._key_calibration(layer_idx)
+        if kcal is not None:
+            ops.compress_calibrated_into(k16, kp, kcal["scale"], kcal["zero"], kcal["alpha"], pos=pos, rotate=True)
+            ops.compress_into(v16, vp, pos=pos, rotate=self.rotate_values)
+        elif self.rotate_values:
             ops.compress_pair_into(k16, v16, kp, vp, pos=pos, rotate=True)
         else:
             ops.compress_into(k16, kp, pos=pos, rotate=True)
@@ -190,6 +200,15 @@ class ErrorCorrectedCache(_HFCache):
         y = x.to(torch.float32 if x.dtype not in (torch.float16, torch.float32) else x.dtype).contiguous().clone()
         ops.hadamard_rotate(y.view(-1, y.shape[-1]))
         return y.to(x.dtype)
+
+    def _key_calibration(self, layer_idx: int) -> Optional[Dict[str, float]]:
+        """The calibrated {scale, zero, alpha} of a layer's keys, or None."""
+        if not self.calibration:
+            return None
+        entry = self.calibration.get("layers", {}).get(str(layer_idx))
+        if entry is None:
+            return None
+        return {k: float(entry[k]) for k in ("scale", "zero", "alpha")}
 
     def _compress(self, x: torch.Tensor, int4_store: torch.Tensor, syn_store: torch.Tensor,
                   meta_store: torch.Tensor, pos: int, L_new: int) -> None:

@@ -36,7 +36,8 @@ enum {
     ECC_ERR_LAUNCH = -6,      /* the CUDA launch failed (cudaGetLastError) */
     ECC_ERR_CUDA = -7,        /* another CUDA runtime call failed */
     ECC_ERR_DEVICE = -8,      /* no usable sm_100 device */
-    ECC_ERR_SCRATCH_LIMIT = -9 /* request larger than ECC_DECODE_STATIC_SCRATCH_BYTES */
+    ECC_ERR_SCRATCH_LIMIT = -9, /* request larger than ECC_DECODE_STATIC_SCRATCH_BYTES */
+    ECC_ERR_PARAM = -10         /* a quantiser parameter is not finite, or scale <= 0 */
 };
 
 #define ECC_DECODE_ROTATE_Q 1    /* rotate the query (WHT) inside the kernel */
@@ -103,6 +104,18 @@ int ecc_compress_strided_pair(const void *x0_f16, int64_t x0s_b, int64_t x0s_h, 
                               const void *x1_f16, int64_t x1s_b, int64_t x1s_h, int64_t x1s_l,
                               void *blocks1, int64_t b1s_b, int64_t b1s_h,
                               int B, int H, int64_t L, int rotate, ecc_stream_t stream);
+
+/* ecc_compress_strided with the quantiser parameters of a calibration config
+ * (custom_kv/calibration.py:232-237: per-layer scale, zero, alpha) in place of
+ * each vector's own statistics: q = first-index argmin |(x - zero) / scale -
+ * C[k]| and k~ = C[q]*scale + zero in fp32 as ops_cpu.lloyd_max_quantize_cpu
+ * (ops_cpu.py:78-109) computes them with those scalars, syndrome bit =
+ * (x - k~ >= 0), and every block stores fp16(scale), fp16(zero), fp16(alpha).
+ * The block format and the decode are unchanged.  ECC_ERR_PARAM unless
+ * scale > 0 and all three are finite. */
+int ecc_compress_strided_calibrated(const void *x_f16, int64_t xs_b, int64_t xs_h, int64_t xs_l,
+                                    void *blocks, int64_t bs_b, int64_t bs_h, int B, int H, int64_t L,
+                                    int rotate, float scale, float zero, float alpha, ecc_stream_t stream);
 
 /* Copy the fp16 (scale, zero, alpha) of block block_idx to host memory as
  * fp32.  Synchronous on `stream`.  Replaces custom_ecc_cuda.get_block_metadata

@@ -218,6 +218,26 @@ def compress_np(x16, rotate: bool = True) -> dict:
             "blocks": blocks}
 
 
+def compress_calibrated_np(x16, scale: float, zero: float, alpha: float, rotate: bool = True) -> np.ndarray:
+    """Compress with fixed per-layer quantiser parameters (the values of a
+    calibration config, custom_kv/calibration.py:232-237):
+    ops_cpu.lloyd_max_quantize_cpu(x_rot, scale, zero) (ops_cpu.py:78-109)
+    and compute_syndrome_cpu (ops_cpu.py:114-126), every block storing
+    fp16(fp32(scale)), fp16(fp32(zero)), fp16(fp32(alpha)).  The Python
+    scalars enter torch's float32 arithmetic rounded to fp32."""
+    x = _as_f16_bits(x16).reshape(-1, D).view(np.float16).astype(np.float32)
+    xr = wht_np(x) if rotate else x
+    s32, z32 = np.float32(scale), np.float32(zero)
+    with np.errstate(invalid="ignore", over="ignore"):
+        xn = ((xr - z32).astype(np.float32) / s32).astype(np.float32)
+        dist = np.abs((xn[:, :, None] - LM_CENTROIDS[None, None, :]).astype(np.float32))
+        q = dist.argmin(-1).astype(np.uint8)
+        kt = ((LM_CENTROIDS[q] * s32).astype(np.float32) + z32).astype(np.float32)
+        syn = (xr - kt).astype(np.float32) >= 0
+    n = x.shape[0]
+    return pack_blocks(q, syn, np.full(n, s32), np.full(n, z32), np.full(n, np.float32(alpha)))
+
+
 def pack_blocks(q, syn, scale, zero, alpha) -> np.ndarray:
     """csrc/ecc_ops.h:22-64 layout: codes @0 (byte i = q[2i] | q[2i+1] << 4),
     syndrome @64 (bit j in byte j/8, position j%8), fp16 scale/zero/alpha at

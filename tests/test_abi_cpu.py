@@ -41,7 +41,7 @@ def test_strerror_and_version(lib):
     lib.ecc_strerror.restype = ctypes.c_char_p
     lib.ecc_strerror.argtypes = [ctypes.c_int]
     assert lib.ecc_strerror(0) == b"ok"
-    for code in range(-8, 0):
+    for code in range(-10, 0):
         assert lib.ecc_strerror(code) not in (b"ok", b"unknown error")
     assert lib.ecc_version() == 100
 
@@ -93,3 +93,17 @@ def test_workspace_size_is_host_only(lib):
     # explicit split count: (2 + 128) floats per (b, q head, split) + alignment slack
     assert lib.ecc_decode_workspace_size(2, 8, 2, 4096, 4) == 2 * 8 * 4 * 130 * 4 + 256
     assert lib.ecc_decode_workspace_size(0, 8, 2, 4096, 4) == 0
+
+
+def test_calibrated_compress_rejects_bad_parameters(lib):
+    p, i32, i64, f32 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
+    fn = lib.ecc_compress_strided_calibrated
+    fn.argtypes = [p, i64, i64, i64, p, i64, i64, i32, i32, i64, i32, f32, f32, f32, p]
+    fn.restype = i32
+    args = (p(16), 0, 0, 128, p(128), 0, 0, 1, 1, 4, 1)
+    assert fn(*args, 0.0, 0.0, 0.1, None) == -10            # scale <= 0
+    assert fn(*args, -1.0, 0.0, 0.1, None) == -10
+    assert fn(*args, float("nan"), 0.0, 0.1, None) == -10
+    assert fn(*args, 1.0, float("inf"), 0.1, None) == -10   # zero not finite
+    assert fn(*args, 1.0, 0.0, float("nan"), None) == -10   # alpha not finite
+    assert fn(None, 0, 0, 128, None, 0, 0, 1, 1, 4, 1, 1.0, 0.0, 0.1, None) == -1  # NULL, checked before the device

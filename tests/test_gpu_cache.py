@@ -206,3 +206,32 @@ def test_llama_generate_through_ecc_cache(cuda_device, monkeypatch):
     assert torch.equal(got.sequences[0, 300], ref.sequences[0, 300])
     cos = F.cosine_similarity(got.logits[1].float().flatten(), ref.logits[1].float().flatten(), dim=0)
     assert cos > 0.98
+
+
+def test_cache_consumes_calibration_for_keys(oracle, cuda_device):
+    """With a calibration config the cache's key blocks of the listed layers
+    carry that layer's scale / zero / alpha and the calibrated quantisation;
+    values and unlisted layers keep per-vector statistics; decode through the
+    pools still matches the oracle."""
+    import custom_ecc_cuda as ops
+    cal = {"layers": {"1": {"scale": 0.93, "zero": 0.011, "alpha": 0.18, "sigma": 0.93}}}
+    cache = _cache(L=128, calibration=cal)
+    k, v = _kv(100, seed=9)
+    for layer in (0, 1):
+        cache.update(k, v, layer_idx=layer)
+    kp1, vp1 = cache.layer_pools(1)
+    kp0, _ = cache.layer_pools(0)
+    k_blocks = kp1[:, :, :100].reshape(-1, 128).cpu().numpy()
+    ref_k = oracle.compress_calibrated_np(k.reshape(-1, 128).cpu().numpy(), 0.93, 0.011, 0.18, rotate=True)
+    assert np.array_equal(k_blocks, ref_k)
+    assert np.array_equal(vp1[:, :, :100].reshape(-1, 128).cpu().numpy(),
+                          oracle.compress(v.reshape(-1, 128).cpu().numpy(), rotate=True))
+    assert np.array_equal(kp0[:, :, :100].reshape(-1, 128).cpu().numpy(),
+                          oracle.compress(k.reshape(-1, 128).cpu().numpy(), rotate=True))
+    q = torch.randn(1, 4, 1, 128, device="cuda").half()
+    out = ops.decode_attention(q, kp1, vp1, seq_len=100, rotate_q=True, unrotate_out=True)
+    ref = oracle.decode(q.cpu().numpy(), kp1[:, :, :100].cpu().numpy(), vp1[:, :, :100].cpu().numpy(), hkv=2,
+                        seq_len=100, rotate_q=True, unrotate_out=True)
+    ref16 = ref.astype(np.float16).astype(np.float32)
+    err = np.abs(out.float().cpu().numpy().reshape(1, 4, 128) - ref16)
+    assert np.all(err <= 2e-3 + np.spacing(np.abs(ref16).astype(np.float16)).astype(np.float32) / 2)

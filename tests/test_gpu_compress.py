@@ -181,3 +181,69 @@ def test_pack_soa_roundtrip(ops, oracle, compress_golden, cuda_device):
     t = lambda a: torch.from_numpy(a).to(cuda_device)
     packed = ops.pack_soa(t(int4), t(syn), t(meta.view(np.int16)).view(torch.float16)).cpu().numpy()
     assert np.array_equal(packed, blk)
+
+
+def _calibrated_golden():
+    return dict(np.load(os.path.join(os.path.dirname(__file__), "golden", "calibrated_golden.npz")))
+
+
+@pytest.mark.parametrize("rotate", [True, False])
+def test_calibrated_compress_matches_reference_golden(ops, cuda_device, rotate):
+    """Fixed per-layer quantiser parameters (a calibration config's scale,
+    zero, alpha): blocks equal the reference's lloyd_max_quantize_cpu +
+    compute_syndrome_cpu fixtures bit for bit."""
+    g = _calibrated_golden()
+    x = _f16(g["x16"], cuda_device).reshape(1, 1, -1, 128)
+    for pi, (scale, zero, alpha) in enumerate(g["params"]):
+        pool = torch.empty((1, 1, x.shape[2], 128), dtype=torch.uint8, device=cuda_device)
+        ops.compress_calibrated_into(x, pool, scale, zero, alpha, rotate=rotate)
+        got = pool.reshape(-1, 128).cpu().numpy()
+        bad = np.nonzero((got != g[f"p{pi}_r{int(rotate)}_blocks"]).any(1))[0]
+        assert bad.size == 0, f"parameter set {pi}: rows {bad[:10]} differ"
+
+
+def test_calibrated_compress_large_and_non_finite(ops, oracle, cuda_device):
+    """65536 heavy-tailed vectors under narrow and wide layer parameters,
+    plus rows with inf and nan, against the oracle; strided input into a pool
+    position; bad parameters raise."""
+    x16 = workloads.make_heavy(seed=91, n=65536)
+    x16[7, 3] = float("inf")
+    x16[8, 100] = float("-inf")
+    x16[9, 0] = float("nan")
+    for scale, zero, alpha in ((0.05, -0.01, 0.02), (1.05, 0.02, 0.21), (9.0, 1.5, 2.0)):
+        # [B, L, H, D] memory seen as [B, H, L, D] (HF layout before its transpose)
+        xd = x16.to(cuda_device).reshape(4, 8192, 2, 128).transpose(1, 2)
+        pool = torch.zeros((4, 2, 8200, 128), dtype=torch.uint8, device=cuda_device)
+        ops.compress_calibrated_into(xd, pool, scale, zero, alpha, pos=5, rotate=True)
+        got = pool[:, :, 5:5 + 8192].reshape(-1, 128).cpu().numpy()
+        rows = x16.reshape(4, 8192, 2, 128).transpose(1, 2).reshape(-1, 128).numpy()
+        ref = oracle.compress_calibrated_np(rows, scale, zero, alpha, rotate=True)
+        bad = np.nonzero((got != ref).any(1))[0]
+        assert bad.size == 0, f"{bad.size} blocks differ, first {bad[:8]}"
+        assert not pool[:, :, :5].any() and not pool[:, :, 5 + 8192:].any()
+    x = x16[:4].to(cuda_device).reshape(1, 1, 4, 128)
+    pool = torch.empty((1, 1, 4, 128), dtype=torch.uint8, device=cuda_device)
+    for bad_args in ((0.0, 0.0, 0.1), (1.0, float("nan"), 0.1)):
+        with pytest.raises(RuntimeError):
+            ops.compress_calibrated_into(x, pool, *bad_args)
+
+
+def test_hadamard_rotate_keeps_infinities(ops, oracle, cuda_device):
+    """hadamard_rotate_cpu divides by fp32(sqrt(128)): +-inf elements stay
+    +-inf (inf - inf butterflies give NaN), like the oracle."""
+    x = torch.randn(4, 128)
+    x[0, 5] = float("inf")
+    x[1, 0] = float("-inf")
+    x[2, 7] = float("inf")
+    x[2, 9] = float("-inf")
+    x[3, 1] = float("nan")
+    ref = oracle.wht(x.numpy())
+    for dt in (torch.float32, torch.float16):
+        got = x.to(dt).to(cuda_device)
+        ops.hadamard_rotate(got)
+        r = oracle.wht(x.to(dt).float().numpy())
+        g = got.float().cpu().numpy()
+        if dt == torch.float16:
+            r = r.astype(np.float16).astype(np.float32)
+        assert np.array_equal(np.isnan(g), np.isnan(r)) and np.array_equal(g[~np.isnan(g)], r[~np.isnan(r)])
+    assert np.isinf(ref[0]).all()

@@ -168,3 +168,15 @@ def test_tie_counter(oracle):
     x16 = workloads.make_heavy(seed=9, n=512).numpy()
     assert oracle.count_ties(x16, tol=1e-6) >= 0
     assert oracle.count_ties(x16, tol=1.0) > 0
+
+
+def test_calibrated_oracle_matches_reference(oracle):
+    """Compress with fixed per-layer parameters: the oracle equals the
+    reference's lloyd_max_quantize_cpu + compute_syndrome_cpu fixtures
+    (tests/golden/make_calibrated_golden.py) for every parameter set, rotated
+    and unrotated, including fp16 extremes far outside the centroid range."""
+    g = dict(np.load(os.path.join(os.path.dirname(__file__), "golden", "calibrated_golden.npz")))
+    for pi, (scale, zero, alpha) in enumerate(g["params"]):
+        for rot in (1, 0):
+            got = oracle.compress_calibrated_np(g["x16"], scale, zero, alpha, rotate=bool(rot))
+            assert np.array_equal(got, g[f"p{pi}_r{rot}_blocks"]), (pi, rot)
