@@ -182,57 +182,50 @@ decode_v1_kernel(const __half *__restrict__ q, const uint8_t *__restrict__ kb, c
 
 // LSE combine of n partials (m natural-log units, l, unnormalised o) of one
 // row by a 128-thread block, thread d = dim d: M = max over the non-empty
-// partials (l > 0; -inf if none), L and O relative to M.  Partial i is read through src(i) =
-// {m, l, o[d]}.  The sums run in partial order; the partials' (m, l) are
-// staged in shared memory a chunk at a time and the o loads are issued eight
-// at a time, so the loop is not bound by one load latency per partial.
+// partials (l > 0; -inf if none), L and O relative to M.  Partial i is read
+// through src(i) = {m, l, o[d]}.  Partials go in batches of up to 32 and each
+// batch is one memory round trip: every thread issues its o loads of the
+// whole batch together with the batch's (m, l) loads (threads < 32), the
+// batch maximum comes from shared memory, and sums kept under an earlier
+// maximum are rescaled.  With n <= 32 (every split count of one device's
+// default partition up to 32 per row) M is the global maximum and the sums
+// run in partial order.
 template <class Src>
 __device__ __forceinline__ void lse_combine(int n, int d, const Src &src, float &M, float &L, float &O) {
-    __shared__ float s_l[kD], s_e[kD], s_red[kD / 32];
-    float mx = -INFINITY;
-    for (int i = d; i < n; i += kD)
-        if (src.l(i) > 0.0f) mx = fmaxf(mx, src.m(i));
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    if ((d & 31) == 0) s_red[d >> 5] = mx;
-    __syncthreads();
-    M = s_red[0];
-#pragma unroll
-    for (int w = 1; w < kD / 32; ++w) M = fmaxf(M, s_red[w]);
+    constexpr int kBatch = 32;
+    __shared__ float s_m[kBatch], s_l[kBatch];
+    M = -INFINITY;
     L = 0.0f;
     O = 0.0f;
-    if (M == -INFINITY) return;  // block-uniform
-    for (int c0 = 0; c0 < n; c0 += kD) {
-        {
-            const int i = c0 + d;
-            float l = 0.0f, e = 0.0f;
-            if (i < n) {
-                l = src.l(i);
-                if (l > 0.0f) e = __expf(src.m(i) - M);
-            }
-            s_l[d] = l;
-            s_e[d] = e;
+    for (int c0 = 0; c0 < n; c0 += kBatch) {
+        const int cn = min(kBatch, n - c0);
+        float ov[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) ov[j] = (j < cn) ? src.o(c0 + j, d) : 0.0f;
+        if (d < cn) {
+            s_m[d] = src.m(c0 + d);
+            s_l[d] = src.l(c0 + d);
         }
         __syncthreads();
-        const int cn = min(kD, n - c0);
-        int k = 0;
-        for (; k + 8 <= cn; k += 8) {
-            float ov[8];
+        float bm = M;
+        for (int j = 0; j < cn; ++j)
+            if (s_l[j] > 0.0f) bm = fmaxf(bm, s_m[j]);
+        if (bm != M) {  // block-uniform
+            const float r = (M == -INFINITY) ? 0.0f : __expf(M - bm);
+            L *= r;
+            O *= r;
+            M = bm;
+        }
+        if (M != -INFINITY) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) ov[j] = (s_l[k + j] > 0.0f) ? src.o(c0 + k + j, d) : 0.0f;
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-                if (s_l[k + j] > 0.0f) {
-                    L = fmaf(s_l[k + j], s_e[k + j], L);
-                    O = fmaf(ov[j], s_e[k + j], O);
+            for (int j = 0; j < kBatch; ++j)
+                if (j < cn && s_l[j] > 0.0f) {
+                    const float e = __expf(s_m[j] - M);
+                    L = fmaf(s_l[j], e, L);
+                    O = fmaf(ov[j], e, O);
                 }
         }
-        for (; k < cn; ++k)
-            if (s_l[k] > 0.0f) {
-                L = fmaf(s_l[k], s_e[k], L);
-                O = fmaf(src.o(c0 + k, d), s_e[k], O);
-            }
-        __syncthreads();
+        __syncthreads();  // the batch's (m, l) slots are refilled next
     }
 }
 
