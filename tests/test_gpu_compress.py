@@ -247,3 +247,17 @@ def test_hadamard_rotate_keeps_infinities(ops, oracle, cuda_device):
             r = r.astype(np.float16).astype(np.float32)
         assert np.array_equal(np.isnan(g), np.isnan(r)) and np.array_equal(g[~np.isnan(g)], r[~np.isnan(r)])
     assert np.isinf(ref[0]).all()
+
+
+def test_full_compress_workload_equals_oracle(ops, oracle, cuda_device):
+    """The whole compress benchmark workload -- 8 kv heads x 131072 tokens of
+    K and V (heavy-tailed fp16), 2 097 152 vectors -- through the same launch
+    shape the benchmark times, every block bit-exact with the oracle."""
+    k, v = workloads.make_c2(seed=0, L=131072, device=cuda_device)
+    for x in (k, v):
+        pool = torch.empty((1, 8, 131072, 128), dtype=torch.uint8, device=cuda_device)
+        ops.compress_into(x, pool, rotate=True)
+        got = pool.reshape(-1, 128).cpu().numpy()
+        ref = oracle.compress(x.reshape(-1, 128).cpu().numpy(), rotate=True)
+        bad = np.nonzero((got != ref).any(1))[0]
+        assert bad.size == 0, f"{bad.size} of {got.shape[0]} blocks differ, first {bad[:8]}"
