@@ -43,8 +43,9 @@ BLOCK = 128
 COMPRESS_TOKENS = 131072
 
 # DRAM bytes per unit measured with ncu (dram__bytes_read.sum +
-# dram__bytes_write.sum of one launch divided by the units it processed), see
-# profiles/decode_tma_b8_hq32_hkv8_ctx64k.md and profiles/compress_8x131072.md.
+# dram__bytes_write.sum of one launch of the decode kernel at B8 x 8 kv heads x
+# 65542 tokens, and of one compress launch of 8 x 131072 vectors, divided by the
+# units each processed).
 # Decode: per (token, kv head), algorithmic 256 B.  Compress: per vector,
 # algorithmic 384 B; the output blocks of a launch partly stay in the 126 MB L2
 # when the launch ends, so DRAM writes are counted below 128 B per vector.
