@@ -233,7 +233,26 @@ struct CompressJob {
     int64_t bs_b, bs_h;
     FastDiv div_h, div_l;
     uint32_t n_vec, n_tiles;
+    const int *pos_dev;  // token offset read from device memory when set (launches replayed from a graph)
+    int64_t cap;         // tokens per (b, h) row of the pool, for the offset check
 };
+
+__device__ int g_compress_error;  // a device-side position was out of range
+
+// Byte offset of a job's destination: *pos_dev tokens when the position lives
+// in device memory.  A position with pos < 0 or pos + L > cap writes nothing
+// and raises g_compress_error (read by ecc_device_status).
+__device__ __forceinline__ bool job_offset(const CompressJob &jb, int64_t &off) {
+    off = 0;
+    if (!jb.pos_dev) return true;
+    const int64_t p = *jb.pos_dev;
+    if (p < 0 || p + (int64_t)jb.div_l.d > jb.cap) {
+        if (threadIdx.x == 0) atomicExch(&g_compress_error, 3);
+        return false;
+    }
+    off = p * kBlockBytes;
+    return true;
+}
 // Up to two jobs in one launch (K and V of one append): tiles [0, n_tiles of
 // job 0) belong to job 0, the rest to job 1.
 struct CompressJobs {
@@ -460,18 +479,19 @@ struct VecRef {
     bool valid;
 };
 
-__device__ __forceinline__ void load_vec(const CompressJob &jb, uint32_t tile, uint4 (&raw)[4], VecRef &ref) {
+__device__ __forceinline__ void load_vec(const CompressJob &jb, uint32_t tile, uint4 (&raw)[4], VecRef &ref,
+                                         int64_t off = 0, bool enabled = true) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane & 3, vsub = lane >> 2;
     const uint32_t vi = tile * kVecPerTile + warp * kVecPerWarp + vsub;
-    ref.valid = vi < jb.n_vec;
+    ref.valid = enabled && vi < jb.n_vec;
     const uint32_t v = min(vi, jb.n_vec - 1u);  // lanes past the end re-read the last vector, store nothing
     const uint32_t row = fdiv(v, jb.div_l);
     const int64_t l = v - row * jb.div_l.d;
     const uint32_t bq = fdiv(row, jb.div_h);
     const int64_t b = bq, h = row - bq * jb.div_h.d;
     const __half *src = jb.x + b * jb.xs_b + h * jb.xs_h + l * jb.xs_l + 8 * g;
-    ref.dst = jb.blocks + (b * jb.bs_b + h * jb.bs_h + l) * kBlockBytes;
+    ref.dst = jb.blocks + off + (b * jb.bs_b + h * jb.bs_h + l) * kBlockBytes;
 #pragma unroll
     for (int c = 0; c < 4; ++c)
         raw[c] = __ldcs(reinterpret_cast<const uint4 *>(src + 32 * c));
@@ -702,22 +722,32 @@ __global__ void __launch_bounds__(kCompressWarps * 32, 3) compress_kernel(const 
     const uint32_t tabq = (uint32_t)__cvta_generic_to_shared(tab + (lane & (kReplicas - 1)));
     const uint32_t t0 = jobs.j[0].n_tiles;
     const uint32_t n_tiles = t0 + (jobs.njobs > 1 ? jobs.j[1].n_tiles : 0u);
+    int64_t off0, off1 = 0;
+    const bool en0 = job_offset(jobs.j[0], off0);
+    const bool en1 = jobs.njobs > 1 ? job_offset(jobs.j[1], off1) : true;
     // the next tile's inputs are loaded before the current tile is processed
     uint32_t tile = blockIdx.x;
     uint4 raw[4];
     VecRef ref;
-    if (tile < n_tiles) load_vec(tile >= t0 ? jobs.j[1] : jobs.j[0], tile >= t0 ? tile - t0 : tile, raw, ref);
+    if (tile < n_tiles) {
+        if (tile >= t0) load_vec(jobs.j[1], tile - t0, raw, ref, off1, en1);
+        else load_vec(jobs.j[0], tile, raw, ref, off0, en0);
+    }
     while (tile < n_tiles) {
         const uint32_t next = tile + gridDim.x;
         uint4 nraw[4];
         VecRef nref;
-        if (next < n_tiles) load_vec(next >= t0 ? jobs.j[1] : jobs.j[0], next >= t0 ? next - t0 : next, nraw, nref);
+        if (next < n_tiles) {
+            if (next >= t0) load_vec(jobs.j[1], next - t0, nraw, nref, off1, en1);
+            else load_vec(jobs.j[0], next, nraw, nref, off0, en0);
+        }
         if (!compress_fast<kRotate>(raw, ref, tabq, red, st)) {
             const bool second = tile >= t0;  // block-uniform
             const CompressJob &jb = second ? jobs.j[1] : jobs.j[0];
             const uint32_t t = second ? tile - t0 : tile;
-            compress_warp_exact<kRotate>(jb.x, jb.xs_b, jb.xs_h, jb.xs_l, jb.blocks, jb.bs_b, jb.bs_h, jb.div_h,
-                                         jb.div_l, jb.n_vec, t, tab, st);
+            compress_warp_exact<kRotate>(jb.x, jb.xs_b, jb.xs_h, jb.xs_l, jb.blocks + (second ? off1 : off0), jb.bs_b,
+                                         jb.bs_h, jb.div_h, jb.div_l, (second ? en1 : en0) ? jb.n_vec : 0u, t, tab,
+                                         st);
         }
 #pragma unroll
         for (int c = 0; c < 4; ++c) raw[c] = nraw[c];
@@ -754,10 +784,12 @@ __global__ void __launch_bounds__(kCompressWarps * 32, 3)
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane & 3;
     uint32_t *st = stage[warp][lane >> 2];
     const QEntry *mytab = tab + (lane & (kReplicas - 1));
+    int64_t off;
+    const bool en = job_offset(jb, off);
     for (uint32_t tile = blockIdx.x; tile < jb.n_tiles; tile += gridDim.x) {
         uint4 raw[4];
         VecRef ref;
-        load_vec(jb, tile, raw, ref);
+        load_vec(jb, tile, raw, ref, off, en);
         float v[4][8];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -1047,16 +1079,18 @@ extern "C" int ecc_compress_strided_pair(const void *x0_f16, int64_t x0s_b, int6
     return launch_jobs(jobs, rotate, stream);
 }
 
-extern "C" int ecc_compress_strided_calibrated(const void *x_f16, int64_t xs_b, int64_t xs_h, int64_t xs_l,
-                                               void *blocks, int64_t bs_b, int64_t bs_h, int B, int H, int64_t L,
-                                               int rotate, float scale, float zero, float alpha,
-                                               ecc_stream_t stream) {
+static int compress_calibrated_impl(const void *x_f16, int64_t xs_b, int64_t xs_h, int64_t xs_l, void *blocks,
+                                    int64_t bs_b, int64_t bs_h, int B, int H, int64_t L, int rotate, float scale,
+                                    float zero, float alpha, const int *pos_dev, int64_t capacity,
+                                    ecc_stream_t stream) {
     if (!(scale > 0.0f) || !std::isfinite(scale) || !std::isfinite(zero) || !std::isfinite(alpha))
         return ECC_ERR_PARAM;
     CompressJob jb{};
     int64_t n = 0;
     int rc = make_job(x_f16, xs_b, xs_h, xs_l, blocks, bs_b, bs_h, B, H, L, &jb, &n);
     if (rc != ECC_OK || n == 0) return rc;
+    jb.pos_dev = pos_dev;
+    jb.cap = capacity;
     DevInfo *di = nullptr;
     rc = dev_info(&di);
     if (rc != ECC_OK) return rc;
@@ -1071,6 +1105,71 @@ extern "C" int ecc_compress_strided_calibrated(const void *x_f16, int64_t xs_b, 
     if (e != cudaSuccess) return ECC_ERR_LAUNCH;
     return launch_status();
 }
+
+extern "C" int ecc_compress_strided_calibrated(const void *x_f16, int64_t xs_b, int64_t xs_h, int64_t xs_l,
+                                               void *blocks, int64_t bs_b, int64_t bs_h, int B, int H, int64_t L,
+                                               int rotate, float scale, float zero, float alpha,
+                                               ecc_stream_t stream) {
+    return compress_calibrated_impl(x_f16, xs_b, xs_h, xs_l, blocks, bs_b, bs_h, B, H, L, rotate, scale, zero, alpha,
+                                    nullptr, 0, stream);
+}
+
+// Device-side positions: the destination token offset is read from
+// *pos_dev when the kernel runs, so one recorded launch serves every step of
+// a growing cache (CUDA graph replay).  blocks point at token 0 of the pools.
+static int at_checks(const int *pos_dev, int64_t capacity, int64_t L) {
+    if (!pos_dev) return ECC_ERR_NULL;
+    if (!aligned(pos_dev, 4)) return ECC_ERR_ALIGN;
+    if (L < 1 || capacity < L) return ECC_ERR_SHAPE;
+    return ECC_OK;
+}
+
+extern "C" int ecc_compress_strided_pair_at(const void *x0_f16, int64_t x0s_b, int64_t x0s_h, int64_t x0s_l,
+                                            void *blocks0, int64_t b0s_b, int64_t b0s_h, const void *x1_f16,
+                                            int64_t x1s_b, int64_t x1s_h, int64_t x1s_l, void *blocks1,
+                                            int64_t b1s_b, int64_t b1s_h, int B, int H, int64_t L,
+                                            int64_t capacity, const int *pos_dev, int rotate, ecc_stream_t stream) {
+    int rc = at_checks(pos_dev, capacity, L);
+    if (rc != ECC_OK) return rc;
+    CompressJobs jobs{};
+    int64_t n0 = 0, n1 = 0;
+    rc = make_job(x0_f16, x0s_b, x0s_h, x0s_l, blocks0, b0s_b, b0s_h, B, H, L, &jobs.j[0], &n0);
+    if (rc != ECC_OK) return rc;
+    jobs.njobs = 1;
+    if (x1_f16 || blocks1) {
+        rc = make_job(x1_f16, x1s_b, x1s_h, x1s_l, blocks1, b1s_b, b1s_h, B, H, L, &jobs.j[1], &n1);
+        if (rc != ECC_OK) return rc;
+        jobs.njobs = 2;
+    }
+    if (n0 == 0) return ECC_OK;
+    for (int k = 0; k < jobs.njobs; ++k) {
+        jobs.j[k].pos_dev = pos_dev;
+        jobs.j[k].cap = capacity;
+    }
+    return launch_jobs(jobs, rotate, stream);
+}
+
+extern "C" int ecc_compress_strided_calibrated_at(const void *x_f16, int64_t xs_b, int64_t xs_h, int64_t xs_l,
+                                                  void *blocks, int64_t bs_b, int64_t bs_h, int B, int H, int64_t L,
+                                                  int64_t capacity, const int *pos_dev, int rotate, float scale,
+                                                  float zero, float alpha, ecc_stream_t stream) {
+    int rc = at_checks(pos_dev, capacity, L);
+    if (rc != ECC_OK) return rc;
+    return compress_calibrated_impl(x_f16, xs_b, xs_h, xs_l, blocks, bs_b, bs_h, B, H, L, rotate, scale, zero, alpha,
+                                    pos_dev, capacity, stream);
+}
+
+namespace ecc {
+int compress_device_error(int reset) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_compress_error, sizeof(int)) != cudaSuccess) return ECC_ERR_CUDA;
+    if (reset) {
+        const int z = 0;
+        if (cudaMemcpyToSymbol(g_compress_error, &z, sizeof(int)) != cudaSuccess) return ECC_ERR_CUDA;
+    }
+    return v;
+}
+}  // namespace ecc
 
 extern "C" int ecc_compress(const void *x_f16, void *blocks, int64_t n, int rotate, ecc_stream_t stream) {
     if (n < 0) return ECC_ERR_SHAPE;

@@ -26,6 +26,10 @@ int launch_decode_tma(const void *q, const void *kb, const void *vb, int64_t bs_
                       float *pl, float *po, int B, int Hq, int Hkv, int64_t seq_len, int64_t chunk, int ns,
                       float scale_log2, int flags, cudaStream_t s);
 int tma_default_splits(int B, int Hkv, int64_t seq_len);
+int launch_decode_tma_dev(const void *q, const void *kb, const void *vb, int64_t bs_b, int64_t bs_h, float *pm,
+                          float *pl, float *po, int B, int Hq, int Hkv, int64_t max_len, const int *seq_len_dev,
+                          int ns, float scale_log2, int flags, cudaStream_t s);
+void tma_dev_plan(int B, int Hkv, int64_t max_len, int *grid, int *nslots);
 
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -456,6 +460,43 @@ extern "C" int ecc_decode(const void *q_f16, const void *k_blocks, const void *v
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     rc = run_partials(q_f16, k_blocks, v_blocks, bs_b, bs_h, pm, pl, po, B, Hq, Hkv, seq_len, chunk, ns, sm_scale,
                       flags & (ECC_DECODE_ROTATE_Q | ECC_DECODE_CUDA_CORES | ECC_DECODE_REGISTER_PATH), s);
+    if (rc != ECC_OK) return rc;
+    return ecc_lse_merge(pm, pl, po, (int64_t)B * Hq, ns, out_f16, flags & ECC_DECODE_UNROTATE_OUT, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Decode with the context length in device memory, for launches recorded once
+// in a CUDA graph and replayed while the context grows.
+// ---------------------------------------------------------------------------
+extern "C" size_t ecc_decode_dev_workspace_size(int B, int Hq, int Hkv, int64_t max_len) {
+    if (B <= 0 || Hq <= 0 || Hkv <= 0 || max_len <= 0) return 0;
+    int grid = 0, ns = 0;
+    tma_dev_plan(B, Hkv, max_len, &grid, &ns);
+    return (size_t)B * Hq * ns * sizeof(float) * (2 + kD) + 256;
+}
+
+extern "C" int ecc_decode_dev(const void *q_f16, const void *k_blocks, const void *v_blocks, int64_t bs_b,
+                              int64_t bs_h, void *out_f16, void *workspace, size_t workspace_bytes, int B, int Hq,
+                              int Hkv, int64_t max_len, const int *seq_len_dev, float sm_scale, int flags,
+                              ecc_stream_t stream) {
+    int rc = check_decode_args(q_f16, k_blocks, v_blocks, B, Hq, Hkv, max_len);
+    if (rc != ECC_OK) return rc;
+    if (!out_f16 || !seq_len_dev) return ECC_ERR_NULL;
+    if (max_len < 1 || Hq / Hkv > 8) return ECC_ERR_SHAPE;
+    const size_t need = ecc_decode_dev_workspace_size(B, Hq, Hkv, max_len);
+    if (!workspace || workspace_bytes < need) return ECC_ERR_WORKSPACE;
+    int grid = 0, ns = 0;
+    tma_dev_plan(B, Hkv, max_len, &grid, &ns);
+    const size_t parts = (size_t)B * Hq * ns;
+    uintptr_t base = (reinterpret_cast<uintptr_t>(workspace) + 255) & ~(uintptr_t)255;
+    float *po = reinterpret_cast<float *>(base);
+    float *pm = po + parts * kD;
+    float *pl = pm + parts;
+    if (!(sm_scale > 0.0f)) sm_scale = 1.0f / std::sqrt((float)kD);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    rc = launch_decode_tma_dev(q_f16, k_blocks, v_blocks, bs_b, bs_h, pm, pl, po, B, Hq, Hkv, max_len, seq_len_dev,
+                               ns, sm_scale * kLog2e, flags & ECC_DECODE_ROTATE_Q, s);
+    if (rc > 0) return ECC_ERR_SHAPE;  // a pool layout or device the TMA kernel does not take
     if (rc != ECC_OK) return rc;
     return ecc_lse_merge(pm, pl, po, (int64_t)B * Hq, ns, out_f16, flags & ECC_DECODE_UNROTATE_OUT, stream);
 }

@@ -455,7 +455,7 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap mkc, const __grid_constant
                   const __grid_constant__ CUtensorMap mvc, const __grid_constant__ CUtensorMap mvs,
                   const __half *__restrict__ q, float *__restrict__ pm, float *__restrict__ pl,
                   float *__restrict__ po, int Hq, int Hkv, int64_t seq_len, int tpr, int64_t T, int nslots,
-                  float scale_log2, int flags) {
+                  float scale_log2, int flags, const int *__restrict__ seq_len_dev) {
     extern __shared__ __align__(1024) uint8_t sm[];
     // broadcast from lane 0 so that the compiler treats the warp index, and
     // the tile cursors derived from it, as warp-uniform values
@@ -491,6 +491,16 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap mkc, const __grid_constant
     pdl_trigger();
     pdl_wait();  // everything above touched shared memory only
 
+    if (seq_len_dev) {
+        // Length in device memory (a launch recorded once and replayed as the
+        // context grows): seq_len, tpr, T above describe the capacity the
+        // tensor maps cover; the partition is rebuilt for the current length,
+        // clamped to [1, capacity].
+        const int64_t rows = T / tpr;
+        seq_len = max((int64_t)1, min((int64_t)*seq_len_dev, seq_len));
+        tpr = (int)((seq_len + kTile - 1) / kTile);
+        T = rows * tpr;
+    }
     // at most one warp per tile, so that every range is non-empty and the
     // partial slots of a row have no holes
     const int64_t NW = min((int64_t)gridDim.x * kWarps, T);
@@ -772,7 +782,8 @@ static int make_map(CUtensorMap *m, const void *base, int64_t seq_len, int Hkv, 
 template <int G>
 static int launch_g(const CUtensorMap &kc, const CUtensorMap &ks, const CUtensorMap &vc, const CUtensorMap &vs,
                     const void *q, float *pm, float *pl, float *po, int Hq, int Hkv, int64_t seq_len, int tpr,
-                    int64_t T, int grid, int ns, float scale_log2, int flags, cudaStream_t s) {
+                    int64_t T, int grid, int ns, float scale_log2, int flags, cudaStream_t s,
+                    const int *seq_len_dev = nullptr) {
     static bool configured[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -784,7 +795,7 @@ static int launch_g(const CUtensorMap &kc, const CUtensorMap &ks, const CUtensor
     }
     if (launch_pdl(decode_tma_kernel<G>, dim3(grid), dim3(kThreads), kSmBytes, s, kc, ks, vc, vs,
                    reinterpret_cast<const __half *>(q), pm, pl, po, Hq, Hkv, seq_len, tpr, T, ns, scale_log2,
-                   flags) != cudaSuccess)
+                   flags, seq_len_dev) != cudaSuccess)
         return ECC_ERR_LAUNCH;
     return launch_status();
 }
@@ -862,6 +873,51 @@ int launch_decode_tma(const void *q, const void *kb, const void *vb, int64_t bs_
     }
 }
 
+// Partial slots that cover the balanced partition of every length up to
+// max_len with the grid used for max_len: a row's tiles touch fewer than
+// NW / rows + 2 warps (NW <= grid * kWarps), and never more than its tiles.
+void tma_dev_plan(int B, int Hkv, int64_t max_len, int *grid, int *nslots) {
+    using namespace tmak;
+    const Plan p = make_plan(B, Hkv, max_len);
+    const int64_t rows = (int64_t)B * Hkv;
+    *grid = p.grid;
+    *nslots = (int)std::min<int64_t>(p.tpr, (int64_t)p.grid * kWarps / rows + 2);
+}
+
+// The TMA decode with the length read from device memory at *seq_len_dev
+// (clamped to [1, max_len]); tensor maps over max_len tokens.  Returns ECC_OK,
+// a positive value when the shape is not one the TMA kernel handles, or an
+// error.
+int launch_decode_tma_dev(const void *q, const void *kb, const void *vb, int64_t bs_b, int64_t bs_h, float *pm,
+                          float *pl, float *po, int B, int Hq, int Hkv, int64_t max_len, const int *seq_len_dev,
+                          int ns, float scale_log2, int flags, cudaStream_t s) {
+    using namespace tmak;
+    const int G = Hq / Hkv;
+    if (G < 1 || G > 8 || max_len < 1 || max_len > (1ll << 30)) return 1;
+    if (((uintptr_t)kb % 16) || ((uintptr_t)vb % 16) || ((uintptr_t)q % 16)) return 1;
+    int grid = 0, need = 0;
+    tma_dev_plan(B, Hkv, max_len, &grid, &need);
+    if (ns < need) return 1;
+    const Plan plan = make_plan(B, Hkv, max_len);
+    if (!reserve_matches()) return 1;
+    if (get_encode() != ECC_OK) return 1;
+    CUtensorMap kc, ks, vc, vs;
+    if (make_map(&kc, kb, max_len, Hkv, B, bs_h, bs_b, 64) != ECC_OK ||
+        make_map(&ks, kb, max_len, Hkv, B, bs_h, bs_b, 32) != ECC_OK ||
+        make_map(&vc, vb, max_len, Hkv, B, bs_h, bs_b, 64) != ECC_OK ||
+        make_map(&vs, vb, max_len, Hkv, B, bs_h, bs_b, 32) != ECC_OK)
+        return 1;
+    switch (G) {
+#define ECC_TMA_CASE(N) \
+    case N: return launch_g<N>(kc, ks, vc, vs, q, pm, pl, po, Hq, Hkv, max_len, (int)plan.tpr, plan.T, grid, ns, scale_log2, flags, s, seq_len_dev);
+        ECC_TMA_CASE(1) ECC_TMA_CASE(2) ECC_TMA_CASE(3) ECC_TMA_CASE(4)
+        ECC_TMA_CASE(5) ECC_TMA_CASE(6) ECC_TMA_CASE(7)
+        default: return launch_g<8>(kc, ks, vc, vs, q, pm, pl, po, Hq, Hkv, max_len, (int)plan.tpr, plan.T, grid, ns,
+                                    scale_log2, flags, s, seq_len_dev);
+#undef ECC_TMA_CASE
+    }
+}
+
 }  // namespace ecc
 
 namespace ecc {
@@ -901,6 +957,10 @@ extern "C" int ecc_selftest_wait_timeout(long long limit_cycles, int *host_gave_
     return rc;
 }
 
+namespace ecc {
+int compress_device_error(int reset);
+}
+
 extern "C" int ecc_device_status(int reset) {
     int v = 0;
     if (cudaMemcpyFromSymbol(&v, ecc::g_device_error, sizeof(int)) != cudaSuccess) return ECC_ERR_CUDA;
@@ -908,5 +968,7 @@ extern "C" int ecc_device_status(int reset) {
         const int z = 0;
         if (cudaMemcpyToSymbol(ecc::g_device_error, &z, sizeof(int)) != cudaSuccess) return ECC_ERR_CUDA;
     }
-    return v;
+    const int c = ecc::compress_device_error(reset);
+    if (c < 0) return c;
+    return v ? v : c;
 }

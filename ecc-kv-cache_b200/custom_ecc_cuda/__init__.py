@@ -27,6 +27,7 @@ __all__ = [
     "hadamard_rotate", "compress_and_store", "get_block_metadata", "rotate_and_compress",
     "compress_into", "decode_attention", "decode_partials", "lse_merge", "dequantize", "pack_soa",
     "decode_workspace_size", "default_splits", "library_path", "EccError", "compress_calibrated_into",
+    "compress_pair_at", "compress_calibrated_at", "decode_attention_dev", "decode_dev_workspace_size",
 ]
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -64,6 +65,12 @@ def _load():
                                        i32, p], i32),
         "ecc_compress_strided_calibrated": ([p, i64, i64, i64, p, i64, i64, i32, i32, i64, i32, f32, f32, f32, p],
                                             i32),
+        "ecc_compress_strided_pair_at": ([p, i64, i64, i64, p, i64, i64, p, i64, i64, i64, p, i64, i64, i32, i32,
+                                          i64, i64, p, i32, p], i32),
+        "ecc_compress_strided_calibrated_at": ([p, i64, i64, i64, p, i64, i64, i32, i32, i64, i64, p, i32, f32, f32,
+                                                f32, p], i32),
+        "ecc_decode_dev_workspace_size": ([i32, i32, i32, i64], sz),
+        "ecc_decode_dev": ([p, p, p, i64, i64, p, p, sz, i32, i32, i32, i64, p, f32, i32, p], i32),
         "ecc_get_block_metadata": ([p, i64, i64, p, p], i32),
         "ecc_dequantize": ([p, p, i64, p], i32),
         "ecc_pack_soa": ([p, i64, p, i64, p, i64, p, i64, p], i32),
@@ -506,9 +513,106 @@ def version() -> int:
 
 
 def device_status(reset: bool = False) -> int:
-    """1 if a kernel on the current device gave up a bounded wait since the
-    last reset (it returned early instead of hanging), else 0."""
+    """Device-side error flag of the current device since the last reset:
+    1 (or 2) if a decode kernel gave up a bounded wait (it returned early
+    instead of hanging), 3 if an append at a device-side position was out of
+    range (it wrote nothing), else 0."""
     rc = int(_lib.ecc_device_status(1 if reset else 0))
     if rc < 0:
         _check(rc, "device_status")
     return rc
+
+
+# ---------------------------------------------------------------------------
+# Positions and lengths in device memory (CUDA-graph replay of decode steps)
+# ---------------------------------------------------------------------------
+def _dev_int(t: torch.Tensor, name: str, device) -> None:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda or t.dtype != torch.int32 or t.numel() < 1:
+        raise RuntimeError(f"{name} must be an int32 CUDA tensor")
+    if t.device != device:
+        raise RuntimeError(f"{name} must be on the device of the pools")
+
+
+def _whole_pool(x: torch.Tensor, pool: torch.Tensor, name: str):
+    _require_cuda(x, name)
+    if x.dtype != torch.float16 or x.dim() != 4 or x.shape[-1] != D or x.stride(-1) != 1:
+        raise RuntimeError(f"{name} must be float16 [B, H, L, 128] with a contiguous last dimension")
+    bs = _pool_strides(pool, "pool")
+    if pool.shape[-4] != x.shape[0] or pool.shape[-3] != x.shape[1]:
+        raise RuntimeError("pool batch/head dims do not match")
+    if x.device != pool.device:
+        raise RuntimeError(f"{name} and pool must be on the same device")
+    return bs
+
+
+def compress_pair_at(k: torch.Tensor, v: torch.Tensor | None, kpool: torch.Tensor, vpool: torch.Tensor | None,
+                     pos_dev: torch.Tensor, rotate: bool = True) -> None:
+    """compress_pair_into at token position ``pos_dev[0]`` (int32 on the GPU,
+    read when the kernel runs), so that a launch recorded in a CUDA graph
+    appends at the current end of a growing cache.  ``v``/``vpool`` None:
+    ``k`` alone.  An out-of-range position writes nothing and raises the flag
+    device_status() reports."""
+    kbs = _whole_pool(k, kpool, "k")
+    _dev_int(pos_dev, "pos_dev", k.device)
+    B, H, L, _ = k.shape
+    if v is not None:
+        if v.shape != k.shape or vpool is None or vpool.shape[-2] != kpool.shape[-2]:
+            raise RuntimeError("v, vpool must match k, kpool")
+        vbs = _whole_pool(v, vpool, "v")
+        vargs = (_ptr(v), v.stride(0), v.stride(1), v.stride(2), _ptr(vpool), vbs[0], vbs[1])
+    else:
+        vargs = (None, 0, 0, 0, None, 0, 0)
+    with torch.cuda.device(k.device):
+        rc = _lib.ecc_compress_strided_pair_at(_ptr(k), k.stride(0), k.stride(1), k.stride(2), _ptr(kpool), kbs[0],
+                                               kbs[1], *vargs, B, H, L, kpool.shape[-2], _ptr(pos_dev),
+                                               int(bool(rotate)), _stream(k))
+    _check(rc, "compress_pair_at")
+
+
+def compress_calibrated_at(x: torch.Tensor, pool: torch.Tensor, scale: float, zero: float, alpha: float,
+                           pos_dev: torch.Tensor, rotate: bool = True) -> None:
+    """compress_calibrated_into at the device-side position ``pos_dev[0]``."""
+    bs = _whole_pool(x, pool, "x")
+    _dev_int(pos_dev, "pos_dev", x.device)
+    B, H, L, _ = x.shape
+    with torch.cuda.device(x.device):
+        rc = _lib.ecc_compress_strided_calibrated_at(_ptr(x), x.stride(0), x.stride(1), x.stride(2), _ptr(pool), bs[0],
+                                                     bs[1], B, H, L, pool.shape[-2], _ptr(pos_dev), int(bool(rotate)),
+                                                     float(scale), float(zero), float(alpha), _stream(x))
+    _check(rc, "compress_calibrated_at")
+
+
+def decode_dev_workspace_size(B: int, hq: int, hkv: int, max_len: int) -> int:
+    return int(_lib.ecc_decode_dev_workspace_size(B, hq, hkv, max_len))
+
+
+def decode_attention_dev(query: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, seq_len_dev: torch.Tensor,
+                         sm_scale: float | None = None, rotate_q: bool = False, unrotate_out: bool = False,
+                         out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """decode_attention over the first ``seq_len_dev[0]`` tokens (int32 on the
+    GPU, read when the kernel runs, clamped to [1, pool capacity]): one
+    recorded launch serves every length of a growing cache.  The split count
+    is fixed by the pool capacity; GQA groups of up to 8."""
+    q3 = _query(query)
+    kbs = _pool_strides(k_pool, "k_pool")
+    vbs = _pool_strides(v_pool, "v_pool")
+    if kbs != vbs or k_pool.shape != v_pool.shape:
+        raise RuntimeError("k_pool and v_pool must have the same shape and strides")
+    B, hq, _ = q3.shape
+    hkv, cap = k_pool.shape[-3], k_pool.shape[-2]
+    if k_pool.shape[-4] != B or hq % hkv:
+        raise RuntimeError("pool batch or GQA shape does not match the query")
+    _dev_int(seq_len_dev, "seq_len_dev", q3.device)
+    if out is None:
+        out = torch.empty((B, hq, 1, D), dtype=torch.float16, device=q3.device)
+    flags = (ROTATE_Q if rotate_q else 0) | (UNROTATE_OUT if unrotate_out else 0)
+    need = decode_dev_workspace_size(B, hq, hkv, cap)
+    with torch.cuda.device(q3.device):
+        ws = workspace if workspace is not None else _workspace(q3.device, need)
+        if ws.numel() < need:
+            raise RuntimeError(f"workspace too small: {ws.numel()} < {need} bytes")
+        rc = _lib.ecc_decode_dev(_ptr(q3), _ptr(k_pool), _ptr(v_pool), kbs[0], kbs[1], _ptr(out), _ptr(ws), ws.numel(),
+                                 B, hq, hkv, cap, _ptr(seq_len_dev), float(sm_scale) if sm_scale else 0.0, flags,
+                                 _stream(q3))
+    _check(rc, "decode_attention_dev")
+    return out

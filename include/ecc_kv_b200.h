@@ -117,6 +117,39 @@ int ecc_compress_strided_calibrated(const void *x_f16, int64_t xs_b, int64_t xs_
                                     void *blocks, int64_t bs_b, int64_t bs_h, int B, int H, int64_t L,
                                     int rotate, float scale, float zero, float alpha, ecc_stream_t stream);
 
+/* Positions and lengths in device memory.  For a decode step recorded once
+ * in a CUDA graph and replayed while the context grows (no counterpart in the
+ * reference, whose decode runs eagerly, custom_kv/patch.py:100), the token
+ * position of an append and the context length of a decode are read from
+ * device memory when the kernel runs.  blocks point at token 0 of pools with
+ * `capacity` tokens per (b, h) row.
+ *
+ * ecc_compress_strided_pair_at: ecc_compress_strided_pair into token
+ * positions *pos_dev .. *pos_dev + L - 1 (x1_f16 = blocks1 = NULL: one
+ * tensor).  A position with pos < 0 or pos + L > capacity writes nothing and
+ * raises the flag ecc_device_status reports (3). */
+int ecc_compress_strided_pair_at(const void *x0_f16, int64_t x0s_b, int64_t x0s_h, int64_t x0s_l,
+                                 void *blocks0, int64_t b0s_b, int64_t b0s_h,
+                                 const void *x1_f16, int64_t x1s_b, int64_t x1s_h, int64_t x1s_l,
+                                 void *blocks1, int64_t b1s_b, int64_t b1s_h,
+                                 int B, int H, int64_t L, int64_t capacity, const int *pos_dev, int rotate,
+                                 ecc_stream_t stream);
+/* ecc_compress_strided_calibrated at the device-side position *pos_dev. */
+int ecc_compress_strided_calibrated_at(const void *x_f16, int64_t xs_b, int64_t xs_h, int64_t xs_l,
+                                       void *blocks, int64_t bs_b, int64_t bs_h, int B, int H, int64_t L,
+                                       int64_t capacity, const int *pos_dev, int rotate, float scale,
+                                       float zero, float alpha, ecc_stream_t stream);
+
+/* ecc_decode over the first *seq_len_dev tokens (read when the kernel runs,
+ * clamped to [1, max_len]) of pools holding max_len tokens per row; the split
+ * count is fixed by (B, Hkv, max_len), so one recorded launch serves every
+ * length.  GQA groups up to 8 and pools the tensor-map kernel takes
+ * (ECC_ERR_SHAPE otherwise).  Workspace: ecc_decode_dev_workspace_size. */
+size_t ecc_decode_dev_workspace_size(int B, int Hq, int Hkv, int64_t max_len);
+int ecc_decode_dev(const void *q_f16, const void *k_blocks, const void *v_blocks, int64_t bs_b, int64_t bs_h,
+                   void *out_f16, void *workspace, size_t workspace_bytes, int B, int Hq, int Hkv,
+                   int64_t max_len, const int *seq_len_dev, float sm_scale, int flags, ecc_stream_t stream);
+
 /* Copy the fp16 (scale, zero, alpha) of block block_idx to host memory as
  * fp32.  Synchronous on `stream`.  Replaces custom_ecc_cuda.get_block_metadata
  * (csrc/ecc_ops.cpp:98). */
