@@ -192,8 +192,10 @@ def run_model_e2e(args):
     random fp16 weights (no checkpoint is available offline), a 32768-token
     seeded random prompt, 200 greedy tokens through transformers generate():
     once with the ECC cache (prefill on fp16 K/V with every layer compressed
-    into the block pools, every decode step through the fused kernel) and once
-    with transformers' own fp16 cache.  Prints one JSON object."""
+    into the block pools, every decode step through the fused kernel), once
+    with transformers' own fp16 cache, and once with the ECC cache and every
+    decode step one CUDA-graph replay (custom_kv.graph: same kernels, lengths
+    in device memory, no per-token host work).  Prints one JSON object."""
     import torch
     from transformers import LlamaConfig, LlamaForCausalLM
     from custom_kv import ecc_cache
@@ -232,7 +234,36 @@ def run_model_e2e(args):
     def ecc_ctx():
         return ecc_cache(model, batch_size=1, max_cache_len=prompt_len + new_tokens + 8, device=str(dev))
 
+    def graph_decode():
+        # prefill eagerly, then every decode step one CUDA-graph replay
+        from custom_kv.graph import GraphDecoder
+        with torch.no_grad(), ecc_ctx() as cache:
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            logits = model(prompt, attention_mask=mask, past_key_values=cache, use_cache=True).logits[:, -1]
+            first = logits.argmax(-1, keepdim=True)
+            torch.cuda.synchronize()
+            t_pre = time.perf_counter() - t0
+            t0 = time.perf_counter()
+            dec = GraphDecoder(model, cache, first)
+            torch.cuda.synchronize()
+            t_setup = time.perf_counter() - t0
+            toks = torch.empty((new_tokens,), dtype=torch.long, device=dev)
+            toks[0] = first[0, 0]
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for i in range(1, new_tokens):
+                toks[i] = dec.step()[0, 0]
+            torch.cuda.synchronize()
+            dt = time.perf_counter() - t0
+            n = new_tokens - 1
+            return {"prefill_s": t_pre, "graph_setup_s": t_setup, "decode_tok_s": n / dt,
+                    "decode_ms_per_token": 1e3 * dt / n, "tokens": toks.tolist()[:8]}
+
     res = {}
+    graph_decode()  # warm-up
+    res["ecc_cache_cuda_graph"] = graph_decode()
+    torch.cuda.empty_cache()
     for name, ctx in (("ecc_cache", ecc_ctx), ("fp16_cache", _NoCache)):
         timed_generate(2, ctx)  # warm-up: kernels, allocator, tensor maps
         t_pre, _, _ = timed_generate(1, ctx)
@@ -243,7 +274,8 @@ def run_model_e2e(args):
         if mem:
             res[name]["cache_memory"] = mem
         torch.cuda.empty_cache()
-    same_first = res["ecc_cache"]["tokens"][0] == res["fp16_cache"]["tokens"][0]
+    same_first = (res["ecc_cache"]["tokens"][0] == res["fp16_cache"]["tokens"][0]
+                  == res["ecc_cache_cuda_graph"]["tokens"][0])
     print(json.dumps({"workload": f"Llama-3.1-8B shape, random fp16 weights, {prompt_len}-token prompt, "
                                   f"{new_tokens} greedy tokens, batch 1, transformers generate()",
                       "data": "synthetic", **res, "first_token_equal": same_first}), flush=True)

@@ -116,6 +116,11 @@ class ErrorCorrectedCache(_HFCache):
         self._seen_tokens = 0
         self._layer_fill: List[int] = [0] * self._num_layers
         self._last_layer = 0
+        # device-side lengths (CUDA-graph decode), see enable_device_lengths
+        self._dev_mode = False
+        self._pos_dev: Optional[torch.Tensor] = None
+        self._len_dev: Optional[torch.Tensor] = None
+        self._dev_ws: Optional[torch.Tensor] = None
 
         shape = (self._num_layers, self.batch_size, self.num_heads, self._max_cache_len, BLOCK_BYTES)
         self._k_pool = torch.zeros(shape, dtype=torch.uint8, device=dev)
@@ -165,7 +170,9 @@ class ErrorCorrectedCache(_HFCache):
         v16 = value_states if value_states.dtype == torch.float16 else value_states.to(torch.float16)
         kp, vp = self.layer_pools(layer_idx)
         kcal = self._key_calibration(layer_idx)
-        if kcal is not None:
+        if self._dev_mode and L_new == 1:
+            self._append_at_device_position(k16, v16, kp, vp, kcal)
+        elif kcal is not None:
             ops.compress_calibrated_into(k16, kp, kcal["scale"], kcal["zero"], kcal["alpha"], pos=pos, rotate=True)
             ops.compress_into(v16, vp, pos=pos, rotate=self.rotate_values)
         elif self.rotate_values:
@@ -200,6 +207,50 @@ class ErrorCorrectedCache(_HFCache):
         y = x.to(torch.float32 if x.dtype not in (torch.float16, torch.float32) else x.dtype).contiguous().clone()
         ops.hadamard_rotate(y.view(-1, y.shape[-1]))
         return y.to(x.dtype)
+
+    # ------------------------------------------------------------------ #
+    # device-side lengths: decode steps replayed from a CUDA graph         #
+    # ------------------------------------------------------------------ #
+    def enable_device_lengths(self, enable: bool = True) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Single-token updates append at, and decode attention reads up to,
+        lengths held in two device int32 counters -- ``pos`` (tokens already
+        cached; where the next token goes) and ``len = pos + 1`` -- instead of
+        the host-side fill, so that a decode step recorded once in a CUDA graph
+        can be replayed while the cache grows.  The counters start at the
+        current fill; ``advance_device_lengths()`` (recordable in the graph) or
+        ``set_device_lengths(n)`` move them.  Every layer shares them, so all
+        layers must hold the same number of tokens.  Returns (pos, len)."""
+        if enable:
+            fill = self._layer_fill[0]
+            if any(f != fill for f in self._layer_fill):
+                raise RuntimeError("device-side lengths need every layer at the same length")
+            self._pos_dev = torch.full((1,), fill, dtype=torch.int32, device=self._device)
+            self._len_dev = torch.full((1,), fill + 1, dtype=torch.int32, device=self._device)
+            need = ops.decode_dev_workspace_size(self.batch_size, self.num_attention_heads, self.num_heads,
+                                                 self._max_cache_len)
+            self._dev_ws = torch.empty(need, dtype=torch.uint8, device=self._device)
+        self._dev_mode = bool(enable)
+        return self._pos_dev, self._len_dev
+
+    def set_device_lengths(self, n_cached: int) -> None:
+        """pos = n_cached, len = n_cached + 1 (stream-ordered device writes)."""
+        self._pos_dev.fill_(int(n_cached))
+        self._len_dev.fill_(int(n_cached) + 1)
+
+    def advance_device_lengths(self) -> None:
+        """pos += 1, len += 1 on the device: the end of one decode step."""
+        self._pos_dev.add_(1)
+        self._len_dev.add_(1)
+
+    def _append_at_device_position(self, k16, v16, kp, vp, kcal) -> None:
+        if kcal is not None:
+            ops.compress_calibrated_at(k16, kp, kcal["scale"], kcal["zero"], kcal["alpha"], self._pos_dev, rotate=True)
+            ops.compress_pair_at(v16, None, vp, None, self._pos_dev, rotate=self.rotate_values)
+        elif self.rotate_values:
+            ops.compress_pair_at(k16, v16, kp, vp, self._pos_dev, rotate=True)
+        else:
+            ops.compress_pair_at(k16, None, kp, None, self._pos_dev, rotate=True)
+            ops.compress_pair_at(v16, None, vp, None, self._pos_dev, rotate=False)
 
     def _key_calibration(self, layer_idx: int) -> Optional[Dict[str, float]]:
         """The calibrated {scale, zero, alpha} of a layer's keys, or None."""
@@ -241,8 +292,12 @@ class ErrorCorrectedCache(_HFCache):
         compressed context of ``layer_idx`` (the new token already appended)."""
         kp, vp = self.layer_pools(layer_idx)
         q16 = query if query.dtype == torch.float16 else query.to(torch.float16)
-        out = ops.decode_attention(q16, kp, vp, seq_len=self._layer_fill[layer_idx], sm_scale=sm_scale,
-                                   rotate_q=True, unrotate_out=self.rotate_values, num_splits=self.num_splits)
+        if self._dev_mode:
+            out = ops.decode_attention_dev(q16, kp, vp, self._len_dev, sm_scale=sm_scale, rotate_q=True,
+                                           unrotate_out=self.rotate_values, workspace=self._dev_ws)
+        else:
+            out = ops.decode_attention(q16, kp, vp, seq_len=self._layer_fill[layer_idx], sm_scale=sm_scale,
+                                       rotate_q=True, unrotate_out=self.rotate_values, num_splits=self.num_splits)
         return out if query.dtype == torch.float16 else out.to(query.dtype)
 
     # ------------------------------------------------------------------ #

@@ -123,3 +123,54 @@ def test_graph_of_append_and_decode_replays_a_growing_cache(ops, oracle, cuda_de
         ops.compress_into(newk, blk, rotate=True)
         assert torch.equal(blk[:, :, 0], kp[:, :, L])
     del graph
+
+
+def _tiny_llama(seed=0, layers=2):
+    from transformers import LlamaConfig, LlamaForCausalLM
+    torch.manual_seed(seed)
+    cfg = LlamaConfig(hidden_size=512, intermediate_size=1024, num_hidden_layers=layers, num_attention_heads=4,
+                      num_key_value_heads=2, head_dim=128, vocab_size=1000, max_position_embeddings=4096,
+                      rope_theta=500000.0, attn_implementation="sdpa")
+    return LlamaForCausalLM(cfg).half().cuda().eval()
+
+
+def test_graph_decoder_replays_eager_decode_steps(cuda_device):
+    """transformers Llama over the ECC cache: every replayed step (model
+    forward, appends, fused decodes, argmax) gives the logits and token of the
+    same step run eagerly with device-side lengths, bit for bit; and the
+    tokens follow the ordinary eager ECC decode."""
+    from custom_kv import ecc_cache
+    from custom_kv.graph import GraphDecoder
+    model = _tiny_llama(seed=2, layers=3)
+    prompt = torch.randint(0, 1000, (1, 200), generator=torch.Generator().manual_seed(1)).cuda()
+    steps = 8
+    with torch.no_grad():
+        # eager, device-side lengths
+        with ecc_cache(model, batch_size=1, max_cache_len=256, device="cuda") as cache:
+            logits = model(prompt, past_key_values=cache, use_cache=True).logits[:, -1]
+            tok = logits.argmax(-1, keepdim=True)
+            cache.enable_device_lengths()
+            eager_logits, eager_toks = [], []
+            pos = 200
+            for _ in range(steps):
+                out = model(input_ids=tok, position_ids=torch.tensor([[pos]], device="cuda"),
+                            cache_position=torch.tensor([pos], device="cuda"), past_key_values=cache, use_cache=True)
+                eager_logits.append(out.logits[:, -1].clone())
+                tok = out.logits[:, -1].argmax(-1, keepdim=True)
+                eager_toks.append(tok.clone())
+                cache.advance_device_lengths()
+                pos += 1
+        # graph replays
+        with ecc_cache(model, batch_size=1, max_cache_len=256, device="cuda") as cache:
+            logits = model(prompt, past_key_values=cache, use_cache=True).logits[:, -1]
+            dec = GraphDecoder(model, cache, logits.argmax(-1, keepdim=True))
+            for i in range(steps):
+                t = dec.step()
+                torch.cuda.synchronize()
+                assert torch.equal(dec.logits, eager_logits[i]), f"step {i}"
+                assert torch.equal(t, eager_toks[i])
+            assert dec.sync_host_lengths() == 200 + steps
+        # the ordinary eager path (host lengths) follows the same tokens
+        with ecc_cache(model, batch_size=1, max_cache_len=256, device="cuda") as cache:
+            got = model.generate(prompt, past_key_values=cache, max_new_tokens=4, do_sample=False)
+    assert torch.equal(got[0, 201:204].cpu(), torch.cat(eager_toks[:3]).flatten().cpu())
