@@ -593,25 +593,84 @@ def run_long(args):
     except Exception:
         gpu_id = str(local)
     clk = ClockSampler(gpu_id).__enter__()
-    ln = chunk_ctx
-    for i in range(W):
-        ln += 1 if grows else 0
-        step(i, ln)
-    barrier()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ln0 = ln
-    clk.mark_start()
-    start.record(stream)
-    for i in range(K):
-        ln += 1 if grows else 0
-        step(W + i, ln, ev[i])
-    stop.record(stream)
-    barrier()
+    ln = chunk_ctx
+    graph = None
+    if args.graph:
+        # every step one CUDA-graph replay: the append position, the local
+        # length and the step's inputs come from device counters that the
+        # recorded step advances itself
+        pos_dev = torch.full((1,), chunk_ctx, dtype=torch.int32, device=dev)
+        len_dev = torch.full((1,), chunk_ctx + (1 if grows else 0), dtype=torch.int32, device=dev)
+        step_dev = torch.zeros((1,), dtype=torch.long, device=dev)
+        if world > 1 and mode == "seq":
+            nspl = max(nspl, ops.decode_dev_splits(Bl, HKV, cap))
+        ws1 = torch.empty(ops.decode_dev_workspace_size(Bl, hq_l, hkv_l, cap), dtype=torch.uint8, device=dev)
+
+        def body():
+            q_i = torch.index_select(qs, 0, step_dev)[0]
+            if grows:
+                k_i = torch.index_select(new_k, 0, step_dev)[0]
+                v_i = torch.index_select(new_v, 0, step_dev)[0]
+                ops.compress_pair_at(k_i, v_i, kpool, vpool, pos_dev, rotate=True)
+            if world == 1:
+                ops.decode_attention_dev(q_i, kpool, vpool, len_dev, rotate_q=True, unrotate_out=True, out=out,
+                                         workspace=ws1)
+            else:
+                shard.step(q_i, kpool, vpool, 0, num_splits=nspl, out=full, seq_len_dev=len_dev)
+            if grows:
+                pos_dev.add_(1)
+                len_dev.add_(1)
+            step_dev.add_(1)
+
+        def reset():
+            pos_dev.fill_(chunk_ctx)
+            len_dev.fill_(chunk_ctx + (1 if grows else 0))
+            step_dev.zero_()
+
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                body()
+        stream.wait_stream(side)
+        barrier()
+        reset()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            body()
+        reset()
+        for i in range(W):
+            graph.replay()
+        ln += W if grows else 0
+        barrier()
+        ln0 = ln
+        clk.mark_start()
+        start.record(stream)
+        for i in range(K):
+            graph.replay()
+        stop.record(stream)
+        ln += K if grows else 0
+        barrier()
+        dec_ms = None
+    else:
+        for i in range(W):
+            ln += 1 if grows else 0
+            step(i, ln)
+        barrier()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+        ln0 = ln
+        clk.mark_start()
+        start.record(stream)
+        for i in range(K):
+            ln += 1 if grows else 0
+            step(W + i, ln, ev[i])
+        stop.record(stream)
+        barrier()
+        dec_ms = sum(a.elapsed_time(b) for a, b in ev) / K
     clk.mark_stop()
     clk.__exit__(None, None, None)
     total_ms = start.elapsed_time(stop)
-    dec_ms = sum(a.elapsed_time(b) for a, b in ev) / K
     if world > 1:
         t = torch.tensor([total_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -634,10 +693,12 @@ def run_long(args):
                        "parallelism": {"kv": "kv-head", "seq": "seq-chunk"}[mode] if world > 1 else "single",
                        "per_rank": f"{hkv_l} kv heads x {chunk_ctx} tokens"},
             "decode_tok_s": Bl * K / (total_ms / 1e3),
-            "rank0_decode_gbs": rank_bytes / (dec_ms / 1e3) / 1e9, "peak": peak, "peak_kind": peak_kind,
+            "rank0_decode_gbs": rank_bytes / (dec_ms / 1e3) / 1e9 if dec_ms else None,
+            "cuda_graph": bool(args.graph), "peak": peak, "peak_kind": peak_kind,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
+    del graph  # a graph holding NCCL work is released before the process group
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -723,6 +784,8 @@ def main():
                     help="run the Llama-3.1-8B-shaped 32k-prompt generate() comparison and print its JSON object")
     ap.add_argument("--long", choices=["kv", "seq"], default=None,
                     help="long-context decode (B16, 131072 tokens) sharded by kv head or by sequence chunk")
+    ap.add_argument("--graph", action="store_true",
+                    help="with --long: every step one CUDA-graph replay (device-side lengths)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

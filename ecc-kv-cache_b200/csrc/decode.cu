@@ -475,6 +475,28 @@ extern "C" size_t ecc_decode_dev_workspace_size(int B, int Hq, int Hkv, int64_t 
     return (size_t)B * Hq * ns * sizeof(float) * (2 + kD) + 256;
 }
 
+extern "C" int ecc_decode_dev_splits(int B, int Hkv, int64_t max_len) {
+    if (B <= 0 || Hkv <= 0 || max_len <= 0) return 0;
+    int grid = 0, ns = 0;
+    tma_dev_plan(B, Hkv, max_len, &grid, &ns);
+    return ns;
+}
+
+extern "C" int ecc_decode_partials_dev(const void *q_f16, const void *k_blocks, const void *v_blocks, int64_t bs_b,
+                                       int64_t bs_h, float *part_m, float *part_l, float *part_o, int B, int Hq,
+                                       int Hkv, int64_t max_len, const int *seq_len_dev, float sm_scale, int flags,
+                                       int num_splits, ecc_stream_t stream) {
+    int rc = check_decode_args(q_f16, k_blocks, v_blocks, B, Hq, Hkv, max_len);
+    if (rc != ECC_OK) return rc;
+    if (!part_m || !part_l || !part_o || !seq_len_dev) return ECC_ERR_NULL;
+    if (max_len < 1 || Hq / Hkv > 8 || num_splits < ecc_decode_dev_splits(B, Hkv, max_len)) return ECC_ERR_SHAPE;
+    if (!(sm_scale > 0.0f)) sm_scale = 1.0f / std::sqrt((float)kD);
+    rc = launch_decode_tma_dev(q_f16, k_blocks, v_blocks, bs_b, bs_h, part_m, part_l, part_o, B, Hq, Hkv, max_len,
+                               seq_len_dev, num_splits, sm_scale * kLog2e, flags & ECC_DECODE_ROTATE_Q,
+                               reinterpret_cast<cudaStream_t>(stream));
+    return rc > 0 ? ECC_ERR_SHAPE : rc;
+}
+
 extern "C" int ecc_decode_dev(const void *q_f16, const void *k_blocks, const void *v_blocks, int64_t bs_b,
                               int64_t bs_h, void *out_f16, void *workspace, size_t workspace_bytes, int B, int Hq,
                               int Hkv, int64_t max_len, const int *seq_len_dev, float sm_scale, int flags,

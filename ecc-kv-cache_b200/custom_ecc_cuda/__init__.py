@@ -28,6 +28,7 @@ __all__ = [
     "compress_into", "decode_attention", "decode_partials", "lse_merge", "dequantize", "pack_soa",
     "decode_workspace_size", "default_splits", "library_path", "EccError", "compress_calibrated_into",
     "compress_pair_at", "compress_calibrated_at", "decode_attention_dev", "decode_dev_workspace_size",
+    "decode_partials_dev", "decode_dev_splits",
 ]
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -70,6 +71,8 @@ def _load():
         "ecc_compress_strided_calibrated_at": ([p, i64, i64, i64, p, i64, i64, i32, i32, i64, i64, p, i32, f32, f32,
                                                 f32, p], i32),
         "ecc_decode_dev_workspace_size": ([i32, i32, i32, i64], sz),
+        "ecc_decode_dev_splits": ([i32, i32, i64], i32),
+        "ecc_decode_partials_dev": ([p, p, p, i64, i64, p, p, p, i32, i32, i32, i64, p, f32, i32, i32, p], i32),
         "ecc_decode_dev": ([p, p, p, i64, i64, p, p, sz, i32, i32, i32, i64, p, f32, i32, p], i32),
         "ecc_get_block_metadata": ([p, i64, i64, p, p], i32),
         "ecc_dequantize": ([p, p, i64, p], i32),
@@ -616,3 +619,37 @@ def decode_attention_dev(query: torch.Tensor, k_pool: torch.Tensor, v_pool: torc
                                  _stream(q3))
     _check(rc, "decode_attention_dev")
     return out
+
+
+def decode_dev_splits(B: int, hkv: int, max_len: int) -> int:
+    """Split count of the device-length decode for pools of max_len tokens."""
+    return int(_lib.ecc_decode_dev_splits(B, hkv, max_len))
+
+
+def decode_partials_dev(query: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, seq_len_dev: torch.Tensor,
+                        num_splits: int, sm_scale: float | None = None, rotate_q: bool = False,
+                        out: tuple | None = None):
+    """decode_partials over the first ``seq_len_dev[0]`` tokens (int32 on the
+    GPU, read when the kernel runs); ``num_splits`` >= decode_dev_splits(B,
+    Hkv, capacity).  Returns (m, l, o) like decode_partials (``out``: reuse
+    three such tensors)."""
+    q3 = _query(query)
+    kbs = _pool_strides(k_pool, "k_pool")
+    if kbs != _pool_strides(v_pool, "v_pool") or k_pool.shape != v_pool.shape:
+        raise RuntimeError("k_pool and v_pool must have the same shape and strides")
+    B, hq, _ = q3.shape
+    hkv, cap = k_pool.shape[-3], k_pool.shape[-2]
+    _dev_int(seq_len_dev, "seq_len_dev", q3.device)
+    if out is None:
+        pm = torch.empty((B, hq, num_splits), dtype=torch.float32, device=q3.device)
+        pl = torch.empty_like(pm)
+        po = torch.empty((B, hq, num_splits, D), dtype=torch.float32, device=q3.device)
+    else:
+        pm, pl, po = out
+    with torch.cuda.device(q3.device):
+        rc = _lib.ecc_decode_partials_dev(_ptr(q3), _ptr(k_pool), _ptr(v_pool), kbs[0], kbs[1], _ptr(pm), _ptr(pl),
+                                          _ptr(po), B, hq, hkv, cap, _ptr(seq_len_dev),
+                                          float(sm_scale) if sm_scale else 0.0, ROTATE_Q if rotate_q else 0,
+                                          int(num_splits), _stream(q3))
+    _check(rc, "decode_partials_dev")
+    return pm, pl, po

@@ -97,7 +97,8 @@ class ShardedDecode:
 
     def step(self, query: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, local_len: int,
              num_splits: int = 0, rotate_q: bool = True, unrotate_out: bool = True,
-             out: Optional[torch.Tensor] = None, mark: Optional[torch.cuda.Event] = None) -> torch.Tensor:
+             out: Optional[torch.Tensor] = None, mark: Optional[torch.cuda.Event] = None,
+             seq_len_dev: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Attention output of this step for every query head, [B, Hq, 1, 128] fp16.
 
         kv mode: ``query`` holds this rank's query heads [B, Hq/N, 1, 128] and
@@ -107,13 +108,23 @@ class ShardedDecode:
         partials; give one that covers every local length of the run so that
         the exchange shapes stay fixed.  ``mark``, if given, is recorded on
         the current stream after this rank's own attention work and before the
-        exchange (to time the two apart)."""
+        exchange (to time the two apart).  ``seq_len_dev`` (an int32 CUDA
+        tensor): the local length is read from it when the kernels run instead
+        of ``local_len``, so the step can be recorded once in a CUDA graph and
+        replayed while the cache grows (seq mode then needs num_splits >=
+        custom_ecc_cuda.decode_dev_splits(B, Hkv, pool capacity))."""
         ops, W = self.ops, self.world
         B, hq_l = query.shape[0], query.shape[1]
         if self.mode == "kv":
             loc = self._buf("loc", (B, hq_l, 1, D), torch.float16, query.device)
-            ops.decode_attention(query, k_pool, v_pool, seq_len=local_len, rotate_q=rotate_q,
-                                 unrotate_out=unrotate_out, out=loc)
+            if seq_len_dev is not None:
+                ws = self._buf("ws", (ops.decode_dev_workspace_size(B, hq_l, k_pool.shape[-3], k_pool.shape[-2]),),
+                               torch.uint8, query.device)
+                ops.decode_attention_dev(query, k_pool, v_pool, seq_len_dev, rotate_q=rotate_q,
+                                         unrotate_out=unrotate_out, out=loc, workspace=ws)
+            else:
+                ops.decode_attention(query, k_pool, v_pool, seq_len=local_len, rotate_q=rotate_q,
+                                     unrotate_out=unrotate_out, out=loc)
             if mark is not None:
                 mark.record()
             if W == 1:
@@ -129,8 +140,15 @@ class ShardedDecode:
         # sequence chunks
         if num_splits <= 0:
             raise ValueError("seq mode needs a fixed num_splits")
-        pm, pl, po = ops.decode_partials(query, k_pool, v_pool, seq_len=local_len, num_splits=num_splits,
-                                         rotate_q=rotate_q)
+        if seq_len_dev is not None:
+            parts = (self._buf("pm", (B, hq_l, num_splits), torch.float32, query.device),
+                     self._buf("pl", (B, hq_l, num_splits), torch.float32, query.device),
+                     self._buf("po", (B, hq_l, num_splits, D), torch.float32, query.device))
+            pm, pl, po = ops.decode_partials_dev(query, k_pool, v_pool, seq_len_dev, num_splits, rotate_q=rotate_q,
+                                                 out=parts)
+        else:
+            pm, pl, po = ops.decode_partials(query, k_pool, v_pool, seq_len=local_len, num_splits=num_splits,
+                                             rotate_q=rotate_q)
         rec = self._buf("rec", (B, hq_l, ops.RECORD_FLOATS), torch.float32, query.device)
         ops.lse_merge_to_record(pm, pl, po, out=rec)
         if mark is not None:

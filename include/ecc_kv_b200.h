@@ -146,6 +146,15 @@ int ecc_compress_strided_calibrated_at(const void *x_f16, int64_t xs_b, int64_t 
  * length.  GQA groups up to 8 and pools the tensor-map kernel takes
  * (ECC_ERR_SHAPE otherwise).  Workspace: ecc_decode_dev_workspace_size. */
 size_t ecc_decode_dev_workspace_size(int B, int Hq, int Hkv, int64_t max_len);
+/* Split count of the device-length decode for pools of max_len tokens. */
+int ecc_decode_dev_splits(int B, int Hkv, int64_t max_len);
+/* ecc_decode_partials over the first *seq_len_dev tokens (clamped to
+ * [1, max_len]); num_splits >= ecc_decode_dev_splits(B, Hkv, max_len), the
+ * partial arrays sized for num_splits. */
+int ecc_decode_partials_dev(const void *q_f16, const void *k_blocks, const void *v_blocks, int64_t bs_b,
+                            int64_t bs_h, float *part_m, float *part_l, float *part_o, int B, int Hq, int Hkv,
+                            int64_t max_len, const int *seq_len_dev, float sm_scale, int flags, int num_splits,
+                            ecc_stream_t stream);
 int ecc_decode_dev(const void *q_f16, const void *k_blocks, const void *v_blocks, int64_t bs_b, int64_t bs_h,
                    void *out_f16, void *workspace, size_t workspace_bytes, int B, int Hq, int Hkv,
                    int64_t max_len, const int *seq_len_dev, float sm_scale, int flags, ecc_stream_t stream);
