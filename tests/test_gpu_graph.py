@@ -78,6 +78,30 @@ def test_decode_with_device_length_equals_oracle(ops, oracle, cuda_device, hq, h
            oracle.decode(q.cpu().numpy(), kb, vb, hkv=hkv, seq_len=cap, rotate_q=True, unrotate_out=True))
 
 
+def test_partials_with_device_length(ops, oracle, cuda_device):
+    """decode_partials_dev + lse_merge equals decode_attention_dev bit for bit
+    and the oracle within tolerance; too few splits are rejected."""
+    B, hq, hkv, cap = 2, 16, 4, 2500
+    k16, v16, _ = workloads.make_c1(seed=29, B=B, hkv=hkv, hq=hq, L=cap)
+    kp = torch.empty((B, hkv, cap, 128), dtype=torch.uint8, device=cuda_device)
+    vp = torch.empty_like(kp)
+    ops.compress_into(k16.to(cuda_device), kp, rotate=True)
+    ops.compress_into(v16.to(cuda_device), vp, rotate=True)
+    q = torch.randn(B, hq, 1, 128, generator=torch.Generator().manual_seed(8)).half().to(cuda_device)
+    ns = ops.decode_dev_splits(B, hkv, cap)
+    for L in (1, 100, 2047, 2500):
+        n = torch.tensor([L], dtype=torch.int32, device=cuda_device)
+        pm, pl, po = ops.decode_partials_dev(q, kp, vp, n, ns + 3, rotate_q=True)
+        merged = ops.lse_merge(pm, pl, po, unrotate_out=True)
+        whole = ops.decode_attention_dev(q, kp, vp, n, rotate_q=True, unrotate_out=True)
+        assert torch.equal(merged.reshape(whole.shape), whole)
+        ref = oracle.decode(q.cpu().numpy(), kp.cpu().numpy(), vp.cpu().numpy(), hkv=hkv, seq_len=L, rotate_q=True,
+                            unrotate_out=True)
+        _close(whole, ref)
+    with pytest.raises(RuntimeError):
+        ops.decode_partials_dev(q, kp, vp, n, ns - 1, rotate_q=True)
+
+
 def test_graph_of_append_and_decode_replays_a_growing_cache(ops, oracle, cuda_device):
     """Record append + decode once; replay for 6 steps while the device-side
     length grows; every step equals the oracle on the pools at that length."""
