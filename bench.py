@@ -505,6 +505,7 @@ def run_ours(args):
 
 
 LONG_B, LONG_CTX = 16, 131072
+LONG_B, LONG_CTX = 16, 131072
 
 
 def run_long(args):
