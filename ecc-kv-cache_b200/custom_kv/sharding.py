@@ -127,15 +127,17 @@ class ShardedDecode:
                                      unrotate_out=unrotate_out, out=loc)
             if mark is not None:
                 mark.record()
+            if out is None:
+                out = torch.empty((B, W * hq_l, 1, D), dtype=torch.float16, device=query.device)
             if W == 1:
-                res = loc
+                out.copy_(loc)
+            elif B == 1 and out.is_contiguous():
+                # rank r's heads are one contiguous chunk of the output: gather in place
+                _all_gather(out.view(W, 1, hq_l, 1, D), loc, self.group)
             else:
                 g = self._buf("gather", (W, B, hq_l, 1, D), torch.float16, query.device)
                 _all_gather(g, loc, self.group)
-                res = g.permute(1, 0, 2, 3, 4).reshape(B, W * hq_l, 1, D)
-            if out is None:
-                return res.clone() if res is loc else res
-            out.copy_(res)
+                out.view(B, W, hq_l, 1, D).copy_(g.permute(1, 0, 2, 3, 4))  # one copy into place
             return out
         # sequence chunks
         if num_splits <= 0:

@@ -129,10 +129,10 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("mode,L", [("kv", 300), ("seq", 300), ("seq", 257)])
-def test_two_gloo_ranks_equal_whole_cache_decode(oracle, mode, L):
+@pytest.mark.parametrize("mode,L,B", [("kv", 300, 2), ("kv", 300, 1), ("seq", 300, 2), ("seq", 257, 2)])
+def test_two_gloo_ranks_equal_whole_cache_decode(oracle, mode, L, B):
     import torch.multiprocessing as mp
-    mp.start_processes(_worker, args=(2, _free_port(), mode, 2, 4, 16, L, 11), nprocs=2, start_method="spawn")
+    mp.start_processes(_worker, args=(2, _free_port(), mode, B, 4, 16, L, 11), nprocs=2, start_method="spawn")
 
 
 def test_shard_ranges():
