@@ -756,6 +756,199 @@ __global__ void __launch_bounds__(kCompressWarps * 32, 3) compress_kernel(const 
     }
 }
 
+// ---- small calls: one warp per vector ---------------------------------------
+// A decode step appends one token per (sequence, kv head): a few hundred
+// vectors, one or two tiles of compress_kernel, whose lanes each run the
+// whole chain over 32 elements while the rest of the GPU idles; that chain
+// sets the launch's duration.  Here a warp owns one vector and lane i holds
+// elements i + 32m (m = 0..3): WHT strides 1..16 are lane exchanges, 32 and
+// 64 stay in registers, lane 8a + l is torch's accumulator acc[a][l], the
+// syndrome words are ballots and the block is one coalesced 128-byte store.
+// Element by element the arithmetic is that of compress_warp (same quotient,
+// sums, std, table and exact fallback), so the blocks are identical.
+#ifndef ECC_COMPRESS_LATENCY_MAX
+#define ECC_COMPRESS_LATENCY_MAX 4096
+#endif
+constexpr int64_t kLatencyMaxVectors = ECC_COMPRESS_LATENCY_MAX;  // calls up to this many vectors
+constexpr int kLatWarps = 8;
+
+// torch-order fp32 sum of the 128 elements spread as above; every lane gets it
+__device__ __forceinline__ float tsum_warp(const float (&v)[4], int lane) {
+    float acc = __fadd_rn(0.0f, v[0]);
+    acc = __fadd_rn(acc, v[1]);
+    acc = __fadd_rn(acc, v[2]);
+    acc = __fadd_rn(acc, v[3]);
+    const int l = lane & 7;
+    const float a0 = __shfl_sync(kFull, acc, l), a1 = __shfl_sync(kFull, acc, l + 8);
+    const float a2 = __shfl_sync(kFull, acc, l + 16), a3 = __shfl_sync(kFull, acc, l + 24);
+    const float t = __fadd_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3);  // t[l]
+    float tk[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) tk[k] = __shfl_sync(kFull, t, k);
+    float s = tk[0];
+#pragma unroll
+    for (int k = 1; k < 8; ++k) s = __fadd_rn(s, tk[k]);
+    return s;
+}
+
+template <bool kRotate>
+__global__ void __launch_bounds__(kLatWarps * 32) compress_lat_kernel(const __grid_constant__ CompressJobs jobs) {
+    __shared__ QEntry tab[kCells * kReplicas];
+    build_qtable(tab);
+    __syncthreads();
+    pdl_trigger();
+    pdl_wait();  // the table set-up above touched shared memory only
+
+    const int lane = threadIdx.x & 31;
+    int64_t off0 = 0, off1 = 0;
+    const bool en0 = job_offset(jobs.j[0], off0);
+    const bool en1 = jobs.njobs > 1 ? job_offset(jobs.j[1], off1) : true;
+    const uint32_t n0 = jobs.j[0].n_vec;
+    const uint32_t n = n0 + (jobs.njobs > 1 ? jobs.j[1].n_vec : 0u);
+    const uint32_t w = blockIdx.x * kLatWarps + (threadIdx.x >> 5);
+    if (w >= n) return;  // warp-uniform
+    const bool second = w >= n0;
+    if (!(second ? en1 : en0)) return;
+    const CompressJob &jb = second ? jobs.j[1] : jobs.j[0];
+    const uint32_t vi = second ? w - n0 : w;
+    const uint32_t row = fdiv(vi, jb.div_l);
+    const int64_t l = vi - row * jb.div_l.d;
+    const uint32_t bq = fdiv(row, jb.div_h);
+    const int64_t b = bq, h = row - bq * jb.div_h.d;
+
+    float v[4];
+    {
+        const __half *src = jb.x + b * jb.xs_b + h * jb.xs_h + l * jb.xs_l + lane;
+#pragma unroll
+        for (int m = 0; m < 4; ++m) v[m] = __half2float(src[32 * m]);
+    }
+    if (kRotate) {
+#pragma unroll
+        for (int s = 1; s < 32; s <<= 1) {  // strides 1..16: partner lane ^ s
+            // lower index: mine + partner; upper index: partner - mine (an
+            // FMA with multiplier +-1 rounds exactly like the add / sub)
+            const float sgn = (lane & s) ? -1.0f : 1.0f;
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+                const float p = __shfl_xor_sync(kFull, v[m], s);
+                v[m] = __fmaf_rn(sgn, v[m], p);
+            }
+        }
+        float a = v[0], c = v[1];  // stride 32
+        v[0] = __fadd_rn(a, c);
+        v[1] = __fsub_rn(a, c);
+        a = v[2];
+        c = v[3];
+        v[2] = __fadd_rn(a, c);
+        v[3] = __fsub_rn(a, c);
+        a = v[0];  // stride 64
+        c = v[2];
+        v[0] = __fadd_rn(a, c);
+        v[2] = __fsub_rn(a, c);
+        a = v[1];
+        c = v[3];
+        v[1] = __fadd_rn(a, c);
+        v[3] = __fsub_rn(a, c);
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {  // quotient by fp32(sqrt(128)), as in wht_group
+            const float x = v[m];
+            const float q0 = __fmul_rn(x, kInvSqrt128);
+            const float rem = __fmaf_rn(-q0, kSqrt128, x);
+            v[m] = fabsf(q0) == INFINITY ? q0 : __fmaf_rn(rem, kInvSqrt128, q0);
+        }
+    }
+
+    const float zero = __fmul_rn(tsum_warp(v, lane), 0.0078125f);  // ops_cpu.py:72
+
+    // unbiased std (ops_cpu.py:73): fp64 tree sum; near an fp32 rounding
+    // midpoint the sum is redone in element order like the CPU
+    const double md = (double)zero;
+    double acc = 0.0;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const double dx = (double)v[m] - md;
+        acc = fma(dx, dx, acc);
+    }
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) acc += __shfl_xor_sync(kFull, acc, o);
+    double sd = __dsqrt_rn(__ddiv_rn(acc, 127.0));
+    float s32 = __double2float_rn(sd);
+    {
+        const double lo = (double)s32;
+        const double nb = (double)(lo <= sd ? nextafterf(s32, INFINITY) : nextafterf(s32, 0.0f));
+        const double mid = 0.5 * (lo + nb);
+        if (__any_sync(kFull, fabs(sd - mid) <= 1e-12 * sd)) {
+            double ex = 0.0;
+#pragma unroll
+            for (int m = 0; m < 4; ++m)
+#pragma unroll 1
+                for (int k = 0; k < 32; ++k) {
+                    const float xv = __shfl_sync(kFull, v[m], k);
+                    const double dx = __dsub_rn((double)xv, md);
+                    ex = __dadd_rn(ex, __dmul_rn(dx, dx));
+                }
+            sd = __dsqrt_rn(__ddiv_rn(ex, 127.0));
+            s32 = __double2float_rn(sd);
+        }
+    }
+    const float scale = __double2float_rn(__dadd_rn((double)s32, 1e-8));
+    const float rs = __frcp_rn(scale);
+
+    // quantise, residual, syndrome
+    const QEntry *mytab = tab + (lane & (kReplicas - 1));
+    uint32_t cw[4], syn[4];
+    float ab[4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const float xv = v[m];
+        const float d = __fsub_rn(xv, zero);
+        const float u = __fmul_rn(d, rs);
+        const unsigned cell = min((unsigned)cell_of(u), (unsigned)(kCells - 1));
+        const QEntry e = mytab[cell * kReplicas];
+        const bool hi = u > e.thr;
+        float cq = hi ? e.c_hi : e.c_lo;
+        int q = e.q_lo + (hi ? 1 : 0);
+        if (fabsf(__fsub_rn(u, e.thr)) < kBand) {
+            q = exact_code(d, scale);
+            cq = lm(0);
+#pragma unroll
+            for (int k = 1; k < 16; ++k) cq = (q == k) ? lm(k) : cq;
+        }
+        const float kt = __fadd_rn(__fmul_rn(cq, scale), zero);
+        const float eps = __fsub_rn(xv, kt);
+        syn[m] = __ballot_sync(kFull, eps >= 0.0f);  // syndrome word m: elements 32m..32m+31
+        ab[m] = fabsf(eps);
+        // code word 4m + lane/8 (elements 8(4m + lane/8) + 0..7, nibble lane % 8)
+        uint32_t x = (uint32_t)q << (4 * (lane & 7));
+        x |= __shfl_xor_sync(kFull, x, 1);
+        x |= __shfl_xor_sync(kFull, x, 2);
+        x |= __shfl_xor_sync(kFull, x, 4);
+        cw[m] = x;
+    }
+    const float alpha = __fmul_rn(tsum_warp(ab, lane), 0.0078125f);
+
+    // lane i writes word i of the block: codes 0..15, syndrome 16..19,
+    // scale | zero << 16, alpha, zeros
+    const int src = 8 * (lane & 3);
+    const uint32_t c0 = __shfl_sync(kFull, cw[0], src), c1 = __shfl_sync(kFull, cw[1], src);
+    const uint32_t c2 = __shfl_sync(kFull, cw[2], src), c3 = __shfl_sync(kFull, cw[3], src);
+    uint32_t word = 0u;
+    if (lane < 16) {
+        const int m = lane >> 2;
+        word = m == 0 ? c0 : m == 1 ? c1 : m == 2 ? c2 : c3;
+    } else if (lane < 20) {
+        const int m = lane - 16;
+        word = m == 0 ? syn[0] : m == 1 ? syn[1] : m == 2 ? syn[2] : syn[3];
+    } else if (lane == 20) {
+        word = (uint32_t)__half_as_ushort(__float2half_rn(scale)) |
+               ((uint32_t)__half_as_ushort(__float2half_rn(zero)) << 16);
+    } else if (lane == 21) {
+        word = (uint32_t)__half_as_ushort(__float2half_rn(alpha));
+    }
+    uint8_t *dst = jb.blocks + (second ? off1 : off0) + (b * jb.bs_b + h * jb.bs_h + l) * kBlockBytes;
+    reinterpret_cast<uint32_t *>(dst)[lane] = word;
+}
+
 // ---- calibrated compress ---------------------------------------------------
 // Fixed quantiser parameters instead of per-vector statistics: the per-layer
 // scale, zero point and alpha of a calibration config (custom_kv/calibration.py
@@ -1039,12 +1232,20 @@ static int launch_jobs(CompressJobs &jobs, int rotate, ecc_stream_t stream) {
     }
     if (jobs.njobs == 0) return ECC_OK;
     DevInfo *di = nullptr;
-    int rc = dev_info(&di);
+    const int rc = dev_info(&di);
     if (rc != ECC_OK) return rc;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const int64_t nvec = (int64_t)jobs.j[0].n_vec + (jobs.njobs > 1 ? jobs.j[1].n_vec : 0);
+    if (nvec <= kLatencyMaxVectors) {  // appends: one warp per vector
+        const dim3 grid((unsigned)((nvec + kLatWarps - 1) / kLatWarps)), block(kLatWarps * 32);
+        const cudaError_t e = rotate ? launch_pdl(compress_lat_kernel<true>, grid, block, 0, s, jobs)
+                                     : launch_pdl(compress_lat_kernel<false>, grid, block, 0, s, jobs);
+        if (e != cudaSuccess) return ECC_ERR_LAUNCH;
+        return launch_status();
+    }
     const int64_t tiles = (int64_t)jobs.j[0].n_tiles + (jobs.njobs > 1 ? jobs.j[1].n_tiles : 0);
     if (tiles >= (int64_t)0xffffff00ll) return ECC_ERR_SHAPE;
     const int64_t grid = std::min<int64_t>(tiles, (int64_t)di->sms * di->compress_ctas_per_sm[rotate ? 1 : 0]);
-    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const cudaError_t e = rotate ? launch_pdl(compress_kernel<true>, dim3((unsigned)grid), dim3(kCompressWarps * 32),
                                               0, s, jobs)
                                  : launch_pdl(compress_kernel<false>, dim3((unsigned)grid),

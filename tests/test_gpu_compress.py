@@ -110,6 +110,30 @@ def test_ragged_counts(ops, oracle, cuda_device, n):
     assert np.array_equal(got, oracle.compress(x16.numpy(), rotate=True))
 
 
+@pytest.mark.parametrize("rotate", [True, False])
+def test_small_and_tiled_calls_agree(ops, oracle, cuda_device, rotate):
+    """Calls of up to 4096 vectors run one warp per vector, larger calls the
+    tiled kernel: the same rows give the same blocks through both, equal to
+    the oracle's (heavy tails, c1 rows and the hand-made edge rows)."""
+    x16 = torch.cat([workloads.make_heavy(seed=58, n=4000), workloads.make_c1(seed=7, L=16)[0].reshape(-1, 128),
+                     workloads.make_edge()] * 2)
+    n = x16.shape[0]
+    assert n > 4096
+    xd = x16.to(cuda_device)
+
+    def run(x):
+        if rotate:
+            return ops.rotate_and_compress(x)
+        out = torch.empty((x.shape[0], 128), dtype=torch.uint8, device=cuda_device)
+        ops.compress_and_store(x, out)
+        return out
+
+    tiled = run(xd).cpu().numpy()
+    small = np.concatenate([run(xd[i:i + 4096]).cpu().numpy() for i in range(0, n, 4096)])
+    assert np.array_equal(small, tiled)
+    assert np.array_equal(small, oracle.compress(x16.numpy(), rotate=rotate))
+
+
 def test_empty_input(ops, cuda_device):
     x = torch.empty((0, 128), dtype=torch.float16, device=cuda_device)
     assert ops.rotate_and_compress(x).shape == (0, 128)

@@ -130,3 +130,65 @@ def test_fast_pass_band_near_thresholds(oracle):
     wrong = (j + (w >= 0)) != q_ref
     assert not np.any(wrong & (np.abs(w) >= BAND_FAST))
     assert np.abs(w[wrong]).max() < BAND_FAST / 4
+
+
+def _lanes_tsum(V):
+    """compress_lat_kernel's torch-order sum over lanes: V [N, 32 lanes, 4]
+    (lane i holds elements i + 32m); lane 8a + l is accumulator acc[a][l]."""
+    acc = np.float32(0.0) + V[..., 0]
+    for m in range(1, 4):
+        acc = (acc + V[..., m]).astype(np.float32)
+    t = [(((acc[:, l] + acc[:, l + 8]).astype(np.float32) + acc[:, l + 16]).astype(np.float32)
+          + acc[:, l + 24]).astype(np.float32) for l in range(8)]
+    s = t[0]
+    for k in range(1, 8):
+        s = (s + t[k]).astype(np.float32)
+    return s
+
+
+def test_warp_per_vector_layout(oracle):
+    """The small-call compress kernel's lane layout emulated in numpy float32:
+    WHT strides 1..16 as lane exchanges (upper lane: partner - mine), 32 and
+    64 in registers; mean and alpha summed lane-wise in torch's order; code
+    word 4m + i/8 by OR over lanes 8(i/8)..+7, syndrome word m as the ballot
+    of element group m, block word i written by lane i.  The result equals the
+    oracle's blocks."""
+    x16 = np.concatenate([workloads.make_heavy(seed=33, n=512).numpy(),
+                          workloads.make_c1(seed=6, L=16)[0].reshape(-1, 128).numpy(),
+                          workloads.make_edge().numpy()])
+    r = oracle.compress_np(x16, rotate=True)
+    n = x16.shape[0]
+    lane = np.arange(32)
+    V = x16.astype(np.float32).reshape(n, 4, 32).transpose(0, 2, 1).copy()  # V[:, i, m] = x[32m + i]
+    with np.errstate(all="ignore"):
+        for s in (1, 2, 4, 8, 16):
+            P = V[:, lane ^ s, :]
+            V = np.where(((lane & s) != 0)[None, :, None], (P - V).astype(np.float32), (V + P).astype(np.float32))
+        for a, c in ((0, 1), (2, 3), (0, 2), (1, 3)):
+            va, vc = V[..., a].copy(), V[..., c].copy()
+            V[..., a], V[..., c] = va + vc, va - vc
+        V = (V / np.float32(np.sqrt(128.0))).astype(np.float32)
+        xr = V.transpose(0, 2, 1).reshape(n, 128)
+        assert np.array_equal(xr, r["x_rot"], equal_nan=True)
+        zero = (_lanes_tsum(V) * np.float32(1 / 128)).astype(np.float32)
+        assert np.array_equal(zero, r["zero"], equal_nan=True)
+        q = r["q"].reshape(n, 4, 32).transpose(0, 2, 1).astype(np.uint32)  # code of lane i, group m
+        kt = ((oracle.LM_CENTROIDS[r["q"]] * r["scale"][:, None]).astype(np.float32) + r["zero"][:, None])
+        eps = (r["x_rot"] - kt.astype(np.float32)).astype(np.float32)
+        E = eps.reshape(n, 4, 32).transpose(0, 2, 1)
+        alpha = (_lanes_tsum(np.abs(E)) * np.float32(1 / 128)).astype(np.float32)
+        assert np.array_equal(alpha, r["alpha"], equal_nan=True)
+    # code words: lanes 8k..8k+7 OR their nibbles q << 4 (lane % 8) -> word 4m + k
+    nib = q << (4 * (lane % 8))[None, :, None].astype(np.uint32)
+    cw = np.zeros((n, 4, 4), np.uint32)  # [vector, m, k]
+    for k in range(4):
+        cw[:, :, k] = np.bitwise_or.reduce(nib[:, 8 * k:8 * k + 8, :], axis=1)
+    syn = ((E >= 0).astype(np.uint64) << lane[None, :, None].astype(np.uint64)).sum(1).astype(np.uint32)  # ballots
+    words = np.zeros((n, 32), np.uint32)
+    for i in range(16):
+        words[:, i] = cw[:, i >> 2, i & 3]  # lane i reads word i from lane 8 (i % 4), group i / 4
+    words[:, 16:20] = syn
+    meta = np.stack([r["scale"], r["zero"], r["alpha"]], 1).astype(np.float16).view(np.uint16).astype(np.uint32)
+    words[:, 20] = meta[:, 0] | (meta[:, 1] << 16)
+    words[:, 21] = meta[:, 2]
+    assert np.array_equal(words.view(np.uint8).reshape(n, 128), r["blocks"])
