@@ -303,7 +303,8 @@ def run_ours(args):
     gen = torch.Generator(device=dev).manual_seed(1234 + rank)
 
     # --- block pools filled by the compress kernel from seeded N(0,1) ---
-    kpool = torch.empty((B, HKV, cap, BLOCK), dtype=torch.uint8, device=dev)
+    rb = args.block_bytes  # 128-byte blocks, or the 96-byte records of the option
+    kpool = torch.empty((B, HKV, cap, rb), dtype=torch.uint8, device=dev)
     vpool = torch.empty_like(kpool)
     chunk = 8192
     for t0 in range(0, CTX, chunk):
@@ -390,8 +391,8 @@ def run_ours(args):
     mean_ctx = seq0 + (K + 1) / 2.0
     # K + V blocks read per step: the last rank's chunk grows, the others' are CTX
     rank_ctx = mean_ctx if (world == 1 or rank == world - 1) else float(CTX)
-    bytes_per_step = B * HKV * rank_ctx * 2 * BLOCK
-    job_bytes_per_step = B * HKV * ((world - 1) * CTX + mean_ctx) * 2 * BLOCK
+    bytes_per_step = B * HKV * rank_ctx * 2 * rb
+    job_bytes_per_step = B * HKV * ((world - 1) * CTX + mean_ctx) * 2 * rb
     value = job_bytes_per_step * K / (total_ms / 1e3) / 1e9
     tok_s = B * K / (total_ms / 1e3)
     dec_avg_ms = sum(dec_ms) / len(dec_ms)
@@ -458,7 +459,7 @@ def run_ours(args):
         barrier()
         e2e_ms = s2.elapsed_time(e2)
         mean_ctx_e = seq + (K + 1) / 2.0
-        e2e = {"value": B * HKV * mean_ctx_e * 2 * BLOCK * K / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
+        e2e = {"value": B * HKV * mean_ctx_e * 2 * rb * K / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
                "tok_s": B * K / (e2e_ms / 1e3), "ms_per_step": e2e_ms / K,
                "h2d_bytes_per_step": (dq[0].numel() + dk[0].numel() + dv[0].numel()) * 2,
                "d2h_bytes_per_step": dout[0].numel() * 2,
@@ -485,11 +486,13 @@ def run_ours(args):
                        "batch": B, "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "context_per_rank": CTX,
                        "parallelism": "seq-chunk" if world > 1 else "single",
                        "num_splits": nspl if world > 1 else "default (balanced tile partition)",
-                       "l2": "inputs 1.07 GB/rank > L2 (no flush needed)"},
+                       "l2": f"inputs {B * HKV * CTX * 2 * rb / 1e9:.2f} GB/rank > L2 (no flush needed)",
+                       "block_bytes": rb},
             "decode_tok_s": tok_s, "pct_peak": value / world / peak,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": DECODE_DRAM_BYTES_PER_UNIT * B * HKV * rank_ctx,
-                         "note": f"decode (split partials + merge) per step: 256 B per (token, kv head), "
+                         "frac": achieved / peak,
+                         "traffic": DECODE_DRAM_BYTES_PER_UNIT * B * HKV * rank_ctx if rb == BLOCK else None,
+                         "note": f"decode (split partials + merge) per step: {2 * rb} B per (token, kv head), "
                                  f"{B * HKV} (b, kv head) rows x mean {rank_ctx:.0f} tokens; traffic from ncu "
                                  f"(per launch of the decode kernel); peak {peak_kind}"},
             "gpu_launches": K * (3 if world == 1 else (4 if rank == world - 1 else 3)),
@@ -779,6 +782,9 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=CTX)
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-compress", action="store_true")
+    ap.add_argument("--block-bytes", type=int, default=BLOCK, choices=[BLOCK, 96],
+                    help="record size of the decode pools: the 128-byte block (default, the reference's "
+                         "format) or the 96-byte record without the pad sector")
     ap.add_argument("--compress-only", action="store_true",
                     help="run only the compress benchmark and print its JSON object")
     ap.add_argument("--model-e2e", action="store_true",

@@ -235,6 +235,7 @@ struct CompressJob {
     uint32_t n_vec, n_tiles;
     const int *pos_dev;  // token offset read from device memory when set (launches replayed from a graph)
     int64_t cap;         // tokens per (b, h) row of the pool, for the offset check
+    uint32_t rec;        // bytes per block record in the pool: 128, or 96 without the pad sector
 };
 
 __device__ int g_compress_error;  // a device-side position was out of range
@@ -250,7 +251,7 @@ __device__ __forceinline__ bool job_offset(const CompressJob &jb, int64_t &off) 
         if (threadIdx.x == 0) atomicExch(&g_compress_error, 3);
         return false;
     }
-    off = p * kBlockBytes;
+    off = p * jb.rec;
     return true;
 }
 // Up to two jobs in one launch (K and V of one append): tiles [0, n_tiles of
@@ -270,7 +271,7 @@ template <bool kRotate, bool kExact>
 __device__ __forceinline__ bool compress_warp(const __half *__restrict__ x, int64_t xs_b, int64_t xs_h, int64_t xs_l,
                                               uint8_t *__restrict__ blocks, int64_t bs_b, int64_t bs_h,
                                               FastDiv div_h, FastDiv div_l, uint32_t n_vec, uint32_t tile,
-                                              const QEntry *tab, uint32_t *st) {
+                                              const QEntry *tab, uint32_t *st, uint32_t rec) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane & 3, vsub = lane >> 2, base = lane & ~3;
     const uint32_t vi = tile * kVecPerTile + warp * kVecPerWarp + vsub;
@@ -384,7 +385,7 @@ __device__ __forceinline__ bool compress_warp(const __half *__restrict__ x, int6
     }
     __syncwarp();
     if (valid) {
-        uint8_t *dst = blocks + (b * bs_b + h * bs_h + l) * kBlockBytes;
+        uint8_t *dst = blocks + (b * bs_b + h * bs_h + l) * rec;
         const uint4 w0 = *reinterpret_cast<const uint4 *>(st + 4 * g);
         uint4 w1;
         if (g == 0) {
@@ -398,7 +399,7 @@ __device__ __forceinline__ bool compress_warp(const __half *__restrict__ x, int6
             w1 = make_uint4(0u, 0u, 0u, 0u);
         }
         __stcs(reinterpret_cast<uint4 *>(dst + 16 * g), w0);
-        __stcs(reinterpret_cast<uint4 *>(dst + 64 + 16 * g), w1);
+        if (64 + 16 * g < (int)rec) __stcs(reinterpret_cast<uint4 *>(dst + 64 + 16 * g), w1);
     }
     __syncwarp();
     return true;
@@ -408,8 +409,8 @@ template <bool kRotate>
 __device__ __noinline__ void compress_warp_exact(const __half *__restrict__ x, int64_t xs_b, int64_t xs_h,
                                                  int64_t xs_l, uint8_t *__restrict__ blocks, int64_t bs_b,
                                                  int64_t bs_h, FastDiv div_h, FastDiv div_l, uint32_t n_vec,
-                                                 uint32_t tile, const QEntry *tab, uint32_t *st) {
-    compress_warp<kRotate, true>(x, xs_b, xs_h, xs_l, blocks, bs_b, bs_h, div_h, div_l, n_vec, tile, tab, st);
+                                                 uint32_t tile, const QEntry *tab, uint32_t *st, uint32_t rec) {
+    compress_warp<kRotate, true>(x, xs_b, xs_h, xs_l, blocks, bs_b, bs_h, div_h, div_l, n_vec, tile, tab, st, rec);
 }
 
 // ---- packed fast pass -------------------------------------------------------
@@ -477,6 +478,7 @@ __device__ __forceinline__ float tsum_finish(const float2 (&A)[4], float *red, i
 struct VecRef {
     uint8_t *dst;  // its block
     bool valid;
+    bool tail;     // this lane also writes bytes 64 + 16g.. of the block (false for the pad sector of a 96-byte record)
 };
 
 __device__ __forceinline__ void load_vec(const CompressJob &jb, uint32_t tile, uint4 (&raw)[4], VecRef &ref,
@@ -491,7 +493,8 @@ __device__ __forceinline__ void load_vec(const CompressJob &jb, uint32_t tile, u
     const uint32_t bq = fdiv(row, jb.div_h);
     const int64_t b = bq, h = row - bq * jb.div_h.d;
     const __half *src = jb.x + b * jb.xs_b + h * jb.xs_h + l * jb.xs_l + 8 * g;
-    ref.dst = jb.blocks + off + (b * jb.bs_b + h * jb.bs_h + l) * kBlockBytes;
+    ref.dst = jb.blocks + off + (b * jb.bs_b + h * jb.bs_h + l) * jb.rec;
+    ref.tail = 64 + 16 * g < (int)jb.rec;
 #pragma unroll
     for (int c = 0; c < 4; ++c)
         raw[c] = __ldcs(reinterpret_cast<const uint4 *>(src + 32 * c));
@@ -700,7 +703,7 @@ __device__ __forceinline__ bool compress_fast(const uint4 (&raw)[4], const VecRe
             w1 = make_uint4(0u, 0u, 0u, 0u);
         }
         __stcs(reinterpret_cast<uint4 *>(ref.dst + 16 * g), w0);
-        __stcs(reinterpret_cast<uint4 *>(ref.dst + 64 + 16 * g), w1);
+        if (ref.tail) __stcs(reinterpret_cast<uint4 *>(ref.dst + 64 + 16 * g), w1);
     }
     __syncwarp();
     return true;
@@ -747,7 +750,7 @@ __global__ void __launch_bounds__(kCompressWarps * 32, 3) compress_kernel(const 
             const uint32_t t = second ? tile - t0 : tile;
             compress_warp_exact<kRotate>(jb.x, jb.xs_b, jb.xs_h, jb.xs_l, jb.blocks + (second ? off1 : off0), jb.bs_b,
                                          jb.bs_h, jb.div_h, jb.div_l, (second ? en1 : en0) ? jb.n_vec : 0u, t, tab,
-                                         st);
+                                         st, jb.rec);
         }
 #pragma unroll
         for (int c = 0; c < 4; ++c) raw[c] = nraw[c];
@@ -945,8 +948,8 @@ __global__ void __launch_bounds__(kLatWarps * 32) compress_lat_kernel(const __gr
     } else if (lane == 21) {
         word = (uint32_t)__half_as_ushort(__float2half_rn(alpha));
     }
-    uint8_t *dst = jb.blocks + (second ? off1 : off0) + (b * jb.bs_b + h * jb.bs_h + l) * kBlockBytes;
-    reinterpret_cast<uint32_t *>(dst)[lane] = word;
+    uint8_t *dst = jb.blocks + (second ? off1 : off0) + (b * jb.bs_b + h * jb.bs_h + l) * jb.rec;
+    if (4 * lane < (int)jb.rec) reinterpret_cast<uint32_t *>(dst)[lane] = word;
 }
 
 // ---- calibrated compress ---------------------------------------------------
@@ -1041,7 +1044,7 @@ __global__ void __launch_bounds__(kCompressWarps * 32, 3)
                 w1 = make_uint4(hs | (hz << 16), ha, 0u, 0u);
             }
             __stcs(reinterpret_cast<uint4 *>(ref.dst + 16 * g), w0);
-            __stcs(reinterpret_cast<uint4 *>(ref.dst + 64 + 16 * g), w1);
+            if (ref.tail) __stcs(reinterpret_cast<uint4 *>(ref.dst + 64 + 16 * g), w1);
         }
         __syncwarp();
     }
@@ -1199,15 +1202,20 @@ using namespace ecc;
 static inline bool aligned(const void *p, size_t a) { return ((uintptr_t)p % a) == 0; }
 
 // Validates one strided compress request and fills its job; *n_out = vectors.
+// mode: the entry points' `rotate` argument (ECC_COMPRESS_* bits).
 static int make_job(const void *x_f16, int64_t xs_b, int64_t xs_h, int64_t xs_l, void *blocks, int64_t bs_b,
-                    int64_t bs_h, int B, int H, int64_t L, CompressJob *jb, int64_t *n_out) {
+                    int64_t bs_h, int B, int H, int64_t L, int mode, CompressJob *jb, int64_t *n_out) {
+    *n_out = 0;
+    if (mode & ~(ECC_COMPRESS_ROTATE | ECC_COMPRESS_BLOCK96)) return ECC_ERR_SHAPE;
+    jb->rec = (mode & ECC_COMPRESS_BLOCK96) ? 96u : (uint32_t)kBlockBytes;
     if (B < 0 || H < 0 || L < 0) return ECC_ERR_SHAPE;
     const int64_t n = (int64_t)B * H * L;
     *n_out = n;
     if (n == 0) return ECC_OK;
     if (n >= (int64_t)0xffffff00ll) return ECC_ERR_SHAPE;  // 32-bit vector index
     if (!x_f16 || !blocks) return ECC_ERR_NULL;
-    if (!aligned(x_f16, 16) || !aligned(blocks, 128)) return ECC_ERR_ALIGN;
+    // 128-byte blocks start on 128-byte boundaries; 96-byte records on 32-byte ones
+    if (!aligned(x_f16, 16) || !aligned(blocks, jb->rec == 96u ? 32 : 128)) return ECC_ERR_ALIGN;
     if ((xs_b % 8) || (xs_h % 8) || (xs_l % 8)) return ECC_ERR_ALIGN;
     jb->x = reinterpret_cast<const __half *>(x_f16);
     jb->xs_b = xs_b;
@@ -1223,7 +1231,8 @@ static int make_job(const void *x_f16, int64_t xs_b, int64_t xs_h, int64_t xs_l,
     return ECC_OK;
 }
 
-static int launch_jobs(CompressJobs &jobs, int rotate, ecc_stream_t stream) {
+static int launch_jobs(CompressJobs &jobs, int mode, ecc_stream_t stream) {
+    const bool rotate = (mode & ECC_COMPRESS_ROTATE) != 0;
     // drop empty jobs
     if (jobs.njobs > 1 && jobs.j[1].n_vec == 0) jobs.njobs = 1;
     if (jobs.njobs > 0 && jobs.j[0].n_vec == 0) {
@@ -1259,7 +1268,7 @@ extern "C" int ecc_compress_strided(const void *x_f16, int64_t xs_b, int64_t xs_
                                     ecc_stream_t stream) {
     CompressJobs jobs{};
     int64_t n = 0;
-    const int rc = make_job(x_f16, xs_b, xs_h, xs_l, blocks, bs_b, bs_h, B, H, L, &jobs.j[0], &n);
+    const int rc = make_job(x_f16, xs_b, xs_h, xs_l, blocks, bs_b, bs_h, B, H, L, rotate, &jobs.j[0], &n);
     if (rc != ECC_OK || n == 0) return rc;
     jobs.njobs = 1;
     return launch_jobs(jobs, rotate, stream);
@@ -1271,9 +1280,9 @@ extern "C" int ecc_compress_strided_pair(const void *x0_f16, int64_t x0s_b, int6
                                          int64_t b1s_h, int B, int H, int64_t L, int rotate, ecc_stream_t stream) {
     CompressJobs jobs{};
     int64_t n0 = 0, n1 = 0;
-    int rc = make_job(x0_f16, x0s_b, x0s_h, x0s_l, blocks0, b0s_b, b0s_h, B, H, L, &jobs.j[0], &n0);
+    int rc = make_job(x0_f16, x0s_b, x0s_h, x0s_l, blocks0, b0s_b, b0s_h, B, H, L, rotate, &jobs.j[0], &n0);
     if (rc != ECC_OK) return rc;
-    rc = make_job(x1_f16, x1s_b, x1s_h, x1s_l, blocks1, b1s_b, b1s_h, B, H, L, &jobs.j[1], &n1);
+    rc = make_job(x1_f16, x1s_b, x1s_h, x1s_l, blocks1, b1s_b, b1s_h, B, H, L, rotate, &jobs.j[1], &n1);
     if (rc != ECC_OK) return rc;
     if (n0 == 0) return ECC_OK;
     jobs.njobs = 2;
@@ -1288,7 +1297,7 @@ static int compress_calibrated_impl(const void *x_f16, int64_t xs_b, int64_t xs_
         return ECC_ERR_PARAM;
     CompressJob jb{};
     int64_t n = 0;
-    int rc = make_job(x_f16, xs_b, xs_h, xs_l, blocks, bs_b, bs_h, B, H, L, &jb, &n);
+    int rc = make_job(x_f16, xs_b, xs_h, xs_l, blocks, bs_b, bs_h, B, H, L, rotate, &jb, &n);
     if (rc != ECC_OK || n == 0) return rc;
     jb.pos_dev = pos_dev;
     jb.cap = capacity;
@@ -1301,7 +1310,7 @@ static int compress_calibrated_impl(const void *x_f16, int64_t xs_b, int64_t xs_
     const int64_t grid = std::min<int64_t>(jb.n_tiles, (int64_t)di->sms * 3);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const cudaError_t e =
-        rotate ? launch_pdl(compress_cal_kernel<true>, dim3((unsigned)grid), dim3(kCompressWarps * 32), 0, s, jb, cp)
+        (rotate & ECC_COMPRESS_ROTATE) ? launch_pdl(compress_cal_kernel<true>, dim3((unsigned)grid), dim3(kCompressWarps * 32), 0, s, jb, cp)
                : launch_pdl(compress_cal_kernel<false>, dim3((unsigned)grid), dim3(kCompressWarps * 32), 0, s, jb, cp);
     if (e != cudaSuccess) return ECC_ERR_LAUNCH;
     return launch_status();
@@ -1334,11 +1343,11 @@ extern "C" int ecc_compress_strided_pair_at(const void *x0_f16, int64_t x0s_b, i
     if (rc != ECC_OK) return rc;
     CompressJobs jobs{};
     int64_t n0 = 0, n1 = 0;
-    rc = make_job(x0_f16, x0s_b, x0s_h, x0s_l, blocks0, b0s_b, b0s_h, B, H, L, &jobs.j[0], &n0);
+    rc = make_job(x0_f16, x0s_b, x0s_h, x0s_l, blocks0, b0s_b, b0s_h, B, H, L, rotate, &jobs.j[0], &n0);
     if (rc != ECC_OK) return rc;
     jobs.njobs = 1;
     if (x1_f16 || blocks1) {
-        rc = make_job(x1_f16, x1s_b, x1s_h, x1s_l, blocks1, b1s_b, b1s_h, B, H, L, &jobs.j[1], &n1);
+        rc = make_job(x1_f16, x1s_b, x1s_h, x1s_l, blocks1, b1s_b, b1s_h, B, H, L, rotate, &jobs.j[1], &n1);
         if (rc != ECC_OK) return rc;
         jobs.njobs = 2;
     }

@@ -366,6 +366,12 @@ static int run_partials(const void *q, const void *kb, const void *vb, int64_t b
     if (!(sm_scale > 0.0f)) sm_scale = 1.0f / std::sqrt((float)kD);
     const float scale_log2 = sm_scale * kLog2e;
     const int group = Hq / Hkv;
+    if (flags & ECC_DECODE_BLOCK96) {  // 96-byte records: the TMA-fed kernel only
+        if (group > 8 || (flags & (ECC_DECODE_CUDA_CORES | ECC_DECODE_REGISTER_PATH))) return ECC_ERR_SHAPE;
+        const int rc = launch_decode_tma(q, kb, vb, bs_b, bs_h, pm, pl, po, B, Hq, Hkv, seq_len, chunk, ns,
+                                         scale_log2, flags & (ECC_DECODE_ROTATE_Q | ECC_DECODE_BLOCK96), s);
+        return rc > 0 ? ECC_ERR_SHAPE : rc;
+    }
     if (group <= 8 && !(flags & ECC_DECODE_CUDA_CORES)) {
         if (!(flags & ECC_DECODE_REGISTER_PATH)) {
             const int rc = launch_decode_tma(q, kb, vb, bs_b, bs_h, pm, pl, po, B, Hq, Hkv, seq_len, chunk, ns,
@@ -403,7 +409,7 @@ extern "C" int ecc_decode_partials(const void *q_f16, const void *k_blocks, cons
         chunk = cdiv(cdiv(std::max<int64_t>(seq_len, 1), num_splits), 64) * 64;
     }
     return run_partials(q_f16, k_blocks, v_blocks, bs_b, bs_h, part_m, part_l, part_o, B, Hq, Hkv, seq_len, chunk,
-                        num_splits, sm_scale, flags & (ECC_DECODE_ROTATE_Q | ECC_DECODE_CUDA_CORES | ECC_DECODE_REGISTER_PATH),
+                        num_splits, sm_scale, flags & (ECC_DECODE_ROTATE_Q | ECC_DECODE_CUDA_CORES | ECC_DECODE_REGISTER_PATH | ECC_DECODE_BLOCK96),
                         reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -459,7 +465,7 @@ extern "C" int ecc_decode(const void *q_f16, const void *k_blocks, const void *v
     float *pl = pm + parts;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     rc = run_partials(q_f16, k_blocks, v_blocks, bs_b, bs_h, pm, pl, po, B, Hq, Hkv, seq_len, chunk, ns, sm_scale,
-                      flags & (ECC_DECODE_ROTATE_Q | ECC_DECODE_CUDA_CORES | ECC_DECODE_REGISTER_PATH), s);
+                      flags & (ECC_DECODE_ROTATE_Q | ECC_DECODE_CUDA_CORES | ECC_DECODE_REGISTER_PATH | ECC_DECODE_BLOCK96), s);
     if (rc != ECC_OK) return rc;
     return ecc_lse_merge(pm, pl, po, (int64_t)B * Hq, ns, out_f16, flags & ECC_DECODE_UNROTATE_OUT, stream);
 }
@@ -492,7 +498,7 @@ extern "C" int ecc_decode_partials_dev(const void *q_f16, const void *k_blocks, 
     if (max_len < 1 || Hq / Hkv > 8 || num_splits < ecc_decode_dev_splits(B, Hkv, max_len)) return ECC_ERR_SHAPE;
     if (!(sm_scale > 0.0f)) sm_scale = 1.0f / std::sqrt((float)kD);
     rc = launch_decode_tma_dev(q_f16, k_blocks, v_blocks, bs_b, bs_h, part_m, part_l, part_o, B, Hq, Hkv, max_len,
-                               seq_len_dev, num_splits, sm_scale * kLog2e, flags & ECC_DECODE_ROTATE_Q,
+                               seq_len_dev, num_splits, sm_scale * kLog2e, flags & (ECC_DECODE_ROTATE_Q | ECC_DECODE_BLOCK96),
                                reinterpret_cast<cudaStream_t>(stream));
     return rc > 0 ? ECC_ERR_SHAPE : rc;
 }
@@ -517,7 +523,7 @@ extern "C" int ecc_decode_dev(const void *q_f16, const void *k_blocks, const voi
     if (!(sm_scale > 0.0f)) sm_scale = 1.0f / std::sqrt((float)kD);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     rc = launch_decode_tma_dev(q_f16, k_blocks, v_blocks, bs_b, bs_h, pm, pl, po, B, Hq, Hkv, max_len, seq_len_dev,
-                               ns, sm_scale * kLog2e, flags & ECC_DECODE_ROTATE_Q, s);
+                               ns, sm_scale * kLog2e, flags & (ECC_DECODE_ROTATE_Q | ECC_DECODE_BLOCK96), s);
     if (rc > 0) return ECC_ERR_SHAPE;  // a pool layout or device the TMA kernel does not take
     if (rc != ECC_OK) return rc;
     return ecc_lse_merge(pm, pl, po, (int64_t)B * Hq, ns, out_f16, flags & ECC_DECODE_UNROTATE_OUT, stream);

@@ -763,14 +763,16 @@ static int get_encode() {
     return ECC_OK;
 }
 
-// 4-D map over a block pool: (byte in block, token, kv head, batch).
+// 4-D map over a block pool: (byte in record, token, kv head, batch); rb =
+// bytes per record (128, or 96 without the pad sector).  The boxes read bytes
+// 0..63 and 64..95 of a record, so both sizes take the same kernel.
 static int make_map(CUtensorMap *m, const void *base, int64_t seq_len, int Hkv, int B, int64_t bs_h, int64_t bs_b,
-                    uint32_t box_x) {
-    cuuint64_t dims[4] = {128, (cuuint64_t)seq_len, (cuuint64_t)Hkv, (cuuint64_t)B};
-    cuuint64_t sh = (cuuint64_t)bs_h * 128, sb = (cuuint64_t)bs_b * 128;
-    if (Hkv == 1) sh = (cuuint64_t)seq_len * 128;  // stride of an extent-1 dim is unused
+                    uint32_t box_x, int rb) {
+    cuuint64_t dims[4] = {(cuuint64_t)rb, (cuuint64_t)seq_len, (cuuint64_t)Hkv, (cuuint64_t)B};
+    cuuint64_t sh = (cuuint64_t)bs_h * rb, sb = (cuuint64_t)bs_b * rb;
+    if (Hkv == 1) sh = (cuuint64_t)seq_len * rb;  // stride of an extent-1 dim is unused
     if (B == 1) sb = sh * (cuuint64_t)Hkv;
-    cuuint64_t strides[3] = {128, sh, sb};
+    cuuint64_t strides[3] = {(cuuint64_t)rb, sh, sb};
     cuuint32_t box[4] = {box_x, (cuuint32_t)kTile, 1, 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};
     const CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void *>(base), dims, strides, box,
@@ -856,11 +858,13 @@ int launch_decode_tma(const void *q, const void *kb, const void *vb, int64_t bs_
     if (ns < plan.nslots) return 1;  // fewer partial slots than the partition writes
     if (!reserve_matches()) return 1;
     if (get_encode() != ECC_OK) return 1;
+    const int rb = (flags & ECC_DECODE_BLOCK96) ? 96 : kBlockBytes;
+    flags &= ECC_DECODE_ROTATE_Q;
     CUtensorMap kc, ks, vc, vs;
-    if (make_map(&kc, kb, seq_len, Hkv, B, bs_h, bs_b, 64) != ECC_OK ||
-        make_map(&ks, kb, seq_len, Hkv, B, bs_h, bs_b, 32) != ECC_OK ||
-        make_map(&vc, vb, seq_len, Hkv, B, bs_h, bs_b, 64) != ECC_OK ||
-        make_map(&vs, vb, seq_len, Hkv, B, bs_h, bs_b, 32) != ECC_OK)
+    if (make_map(&kc, kb, seq_len, Hkv, B, bs_h, bs_b, 64, rb) != ECC_OK ||
+        make_map(&ks, kb, seq_len, Hkv, B, bs_h, bs_b, 32, rb) != ECC_OK ||
+        make_map(&vc, vb, seq_len, Hkv, B, bs_h, bs_b, 64, rb) != ECC_OK ||
+        make_map(&vs, vb, seq_len, Hkv, B, bs_h, bs_b, 32, rb) != ECC_OK)
         return 1;
     switch (G) {
 #define ECC_TMA_CASE(N) \
@@ -901,11 +905,13 @@ int launch_decode_tma_dev(const void *q, const void *kb, const void *vb, int64_t
     const Plan plan = make_plan(B, Hkv, max_len);
     if (!reserve_matches()) return 1;
     if (get_encode() != ECC_OK) return 1;
+    const int rb = (flags & ECC_DECODE_BLOCK96) ? 96 : kBlockBytes;
+    flags &= ECC_DECODE_ROTATE_Q;
     CUtensorMap kc, ks, vc, vs;
-    if (make_map(&kc, kb, max_len, Hkv, B, bs_h, bs_b, 64) != ECC_OK ||
-        make_map(&ks, kb, max_len, Hkv, B, bs_h, bs_b, 32) != ECC_OK ||
-        make_map(&vc, vb, max_len, Hkv, B, bs_h, bs_b, 64) != ECC_OK ||
-        make_map(&vs, vb, max_len, Hkv, B, bs_h, bs_b, 32) != ECC_OK)
+    if (make_map(&kc, kb, max_len, Hkv, B, bs_h, bs_b, 64, rb) != ECC_OK ||
+        make_map(&ks, kb, max_len, Hkv, B, bs_h, bs_b, 32, rb) != ECC_OK ||
+        make_map(&vc, vb, max_len, Hkv, B, bs_h, bs_b, 64, rb) != ECC_OK ||
+        make_map(&vs, vb, max_len, Hkv, B, bs_h, bs_b, 32, rb) != ECC_OK)
         return 1;
     switch (G) {
 #define ECC_TMA_CASE(N) \

@@ -39,9 +39,12 @@ ROTATE_Q = 1
 UNROTATE_OUT = 2
 CUDA_CORES = 4
 REGISTER_PATH = 8
+BLOCK96 = 16           # decode flag: the pools hold 96-byte records
+COMPRESS_BLOCK96 = 2   # compress mode bit: write 96-byte records
 _KERNEL_FLAGS = {"auto": 0, "tma": 0, "register": REGISTER_PATH, "cuda_cores": CUDA_CORES}
 D = 128
 BLOCK_BYTES = 128
+RECORD96 = 96          # the block without its zero pad sector (bytes 96..127)
 
 
 class EccError(RuntimeError):
@@ -192,17 +195,31 @@ def get_block_metadata(cache_raw: torch.Tensor, block_idx: int) -> torch.Tensor:
 # pool ops used by custom_kv
 # ---------------------------------------------------------------------------
 def _pool_strides(pool: torch.Tensor, name: str):
-    """A block pool is a uint8 tensor [..., B, H, L, 128] whose last two dims
-    are contiguous blocks; returns (bs_b, bs_h) in blocks."""
+    """A block pool is a uint8 tensor [..., B, H, L, R] whose last two dims
+    are contiguous records of R = 128 bytes (the block) or 96 (the block
+    without its zero pad sector, RECORD96); returns (bs_b, bs_h) in records."""
     _require_cuda(pool, name)
-    if pool.dtype != torch.uint8 or pool.dim() < 4 or pool.shape[-1] != BLOCK_BYTES:
-        raise RuntimeError(f"{name} must be a uint8 block pool [B, H, L, 128]")
-    if pool.stride(-1) != 1 or pool.stride(-2) != BLOCK_BYTES:
-        raise RuntimeError(f"{name}: blocks along L must be contiguous 128-byte rows")
+    if pool.dtype != torch.uint8 or pool.dim() < 4 or pool.shape[-1] not in (BLOCK_BYTES, RECORD96):
+        raise RuntimeError(f"{name} must be a uint8 block pool [B, H, L, 128] (or [B, H, L, 96])")
+    rb = pool.shape[-1]
+    if pool.stride(-1) != 1 or pool.stride(-2) != rb:
+        raise RuntimeError(f"{name}: blocks along L must be contiguous {rb}-byte rows")
     sb, sh = pool.stride(-4), pool.stride(-3)
-    if sb % BLOCK_BYTES or sh % BLOCK_BYTES:
+    if sb % rb or sh % rb:
         raise RuntimeError(f"{name}: batch/head strides must be whole blocks")
-    return sb // BLOCK_BYTES, sh // BLOCK_BYTES
+    return sb // rb, sh // rb
+
+
+def _cmode(rotate: bool, *pools) -> int:
+    """The compress entry points' `rotate` argument: WHT bit and record size."""
+    rbs = {p.shape[-1] for p in pools if p is not None}
+    if len(rbs) != 1:
+        raise RuntimeError("the pools of one call must have the same record size")
+    return int(bool(rotate)) | (COMPRESS_BLOCK96 if rbs.pop() == RECORD96 else 0)
+
+
+def _rec_flag(k_pool: torch.Tensor) -> int:
+    return BLOCK96 if k_pool.shape[-1] == RECORD96 else 0
 
 
 def compress_into(x: torch.Tensor, pool: torch.Tensor, pos: int = 0, rotate: bool = True) -> None:
@@ -227,7 +244,7 @@ def compress_into(x: torch.Tensor, pool: torch.Tensor, pos: int = 0, rotate: boo
     dst = pool[..., pos:, :] if pos else pool
     with torch.cuda.device(x.device):
         rc = _lib.ecc_compress_strided(_ptr(x), x.stride(0), x.stride(1), x.stride(2), _ptr(dst), bs_b, bs_h,
-                                       B, H, L, int(bool(rotate)), _stream(x))
+                                       B, H, L, _cmode(rotate, pool), _stream(x))
     _check(rc, "compress_into")
 
 
@@ -261,7 +278,7 @@ def compress_calibrated_into(x: torch.Tensor, pool: torch.Tensor, scale: float, 
     B, H, L, _ = x.shape
     with torch.cuda.device(x.device):
         rc = _lib.ecc_compress_strided_calibrated(_ptr(x), x.stride(0), x.stride(1), x.stride(2), _ptr(dst), bs[0],
-                                                  bs[1], B, H, L, int(bool(rotate)), float(scale), float(zero),
+                                                  bs[1], B, H, L, _cmode(rotate, pool), float(scale), float(zero),
                                                   float(alpha), _stream(x))
     _check(rc, "compress_calibrated_into")
 
@@ -278,7 +295,7 @@ def compress_pair_into(k: torch.Tensor, v: torch.Tensor, kpool: torch.Tensor, vp
     with torch.cuda.device(k.device):
         rc = _lib.ecc_compress_strided_pair(_ptr(k), k.stride(0), k.stride(1), k.stride(2), _ptr(kdst), kbs[0],
                                             kbs[1], _ptr(v), v.stride(0), v.stride(1), v.stride(2), _ptr(vdst),
-                                            vbs[0], vbs[1], B, H, L, int(bool(rotate)), _stream(k))
+                                            vbs[0], vbs[1], B, H, L, _cmode(rotate, kpool, vpool), _stream(k))
     _check(rc, "compress_pair_into")
 
 
@@ -297,9 +314,14 @@ def rotate_and_compress(x: torch.Tensor, blocks: torch.Tensor | None = None) -> 
 
 
 def dequantize(blocks: torch.Tensor) -> torch.Tensor:
-    """[..., 128] u8 contiguous blocks -> [..., 128] fp16 reconstructions
-    (C[q]*scale + zero) + alpha*s (custom_kv/fused_decode.py:229-241)."""
+    """[..., 128] u8 contiguous blocks (or [..., 96] records) -> [..., 128]
+    fp16 reconstructions (C[q]*scale + zero) + alpha*s
+    (custom_kv/fused_decode.py:229-241)."""
     _require_input(blocks, "blocks")
+    if blocks.dim() < 1 or blocks.shape[-1] not in (BLOCK_BYTES, RECORD96):
+        raise RuntimeError("blocks must be [..., 128] (or [..., 96]) uint8")
+    if blocks.shape[-1] == RECORD96:  # the pad sector back in place (zeros)
+        blocks = torch.nn.functional.pad(blocks, (0, BLOCK_BYTES - RECORD96))
     n = blocks.numel() // BLOCK_BYTES
     out = torch.empty(blocks.shape[:-1] + (D,), dtype=torch.float16, device=blocks.device)
     with torch.cuda.device(blocks.device):
@@ -404,7 +426,7 @@ def decode_attention(query: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Te
     elif not out.is_contiguous() or out.dtype != torch.float16 or out.numel() != B * hq * D:
         raise RuntimeError("out must be a contiguous float16 tensor of B*Hq*128 elements")
     flags = (ROTATE_Q if rotate_q else 0) | (UNROTATE_OUT if unrotate_out else 0) | (CUDA_CORES if cuda_cores else 0)
-    flags |= _KERNEL_FLAGS[kernel]
+    flags |= _KERNEL_FLAGS[kernel] | _rec_flag(k_pool)
     scale = float(sm_scale) if sm_scale is not None else 0.0
     need = decode_workspace_size(B, hq, hkv, seq_len, num_splits)
     with torch.cuda.device(q3.device):
@@ -426,8 +448,8 @@ def decode_partials(query: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Ten
     q3 = _query(query)
     kbs = _pool_strides(k_pool, "k_pool")
     vbs = _pool_strides(v_pool, "v_pool")
-    if kbs != vbs:
-        raise RuntimeError("k_pool and v_pool must have the same strides")
+    if kbs != vbs or k_pool.shape[-1] != v_pool.shape[-1]:
+        raise RuntimeError("k_pool and v_pool must have the same strides and record size")
     B, hq, _ = q3.shape
     hkv = k_pool.shape[-3]
     if num_splits <= 0:
@@ -441,7 +463,7 @@ def decode_partials(query: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Ten
                                       _ptr(po), B, hq, hkv, int(seq_len),
                                       float(sm_scale) if sm_scale is not None else 0.0,
                                       (ROTATE_Q if rotate_q else 0) | (CUDA_CORES if cuda_cores else 0)
-                                      | _KERNEL_FLAGS[kernel], int(num_splits), _stream(q3))
+                                      | _KERNEL_FLAGS[kernel] | _rec_flag(k_pool), int(num_splits), _stream(q3))
     _check(rc, "decode_partials")
     return pm, pl, po
 
@@ -568,7 +590,7 @@ def compress_pair_at(k: torch.Tensor, v: torch.Tensor | None, kpool: torch.Tenso
     with torch.cuda.device(k.device):
         rc = _lib.ecc_compress_strided_pair_at(_ptr(k), k.stride(0), k.stride(1), k.stride(2), _ptr(kpool), kbs[0],
                                                kbs[1], *vargs, B, H, L, kpool.shape[-2], _ptr(pos_dev),
-                                               int(bool(rotate)), _stream(k))
+                                               _cmode(rotate, kpool, vpool if v is not None else None), _stream(k))
     _check(rc, "compress_pair_at")
 
 
@@ -580,7 +602,7 @@ def compress_calibrated_at(x: torch.Tensor, pool: torch.Tensor, scale: float, ze
     B, H, L, _ = x.shape
     with torch.cuda.device(x.device):
         rc = _lib.ecc_compress_strided_calibrated_at(_ptr(x), x.stride(0), x.stride(1), x.stride(2), _ptr(pool), bs[0],
-                                                     bs[1], B, H, L, pool.shape[-2], _ptr(pos_dev), int(bool(rotate)),
+                                                     bs[1], B, H, L, pool.shape[-2], _ptr(pos_dev), _cmode(rotate, pool),
                                                      float(scale), float(zero), float(alpha), _stream(x))
     _check(rc, "compress_calibrated_at")
 
@@ -608,7 +630,7 @@ def decode_attention_dev(query: torch.Tensor, k_pool: torch.Tensor, v_pool: torc
     _dev_int(seq_len_dev, "seq_len_dev", q3.device)
     if out is None:
         out = torch.empty((B, hq, 1, D), dtype=torch.float16, device=q3.device)
-    flags = (ROTATE_Q if rotate_q else 0) | (UNROTATE_OUT if unrotate_out else 0)
+    flags = (ROTATE_Q if rotate_q else 0) | (UNROTATE_OUT if unrotate_out else 0) | _rec_flag(k_pool)
     need = decode_dev_workspace_size(B, hq, hkv, cap)
     with torch.cuda.device(q3.device):
         ws = workspace if workspace is not None else _workspace(q3.device, need)
@@ -649,7 +671,8 @@ def decode_partials_dev(query: torch.Tensor, k_pool: torch.Tensor, v_pool: torch
     with torch.cuda.device(q3.device):
         rc = _lib.ecc_decode_partials_dev(_ptr(q3), _ptr(k_pool), _ptr(v_pool), kbs[0], kbs[1], _ptr(pm), _ptr(pl),
                                           _ptr(po), B, hq, hkv, cap, _ptr(seq_len_dev),
-                                          float(sm_scale) if sm_scale else 0.0, ROTATE_Q if rotate_q else 0,
-                                          int(num_splits), _stream(q3))
+                                          float(sm_scale) if sm_scale else 0.0,
+                                          (ROTATE_Q if rotate_q else 0) | _rec_flag(k_pool), int(num_splits),
+                                          _stream(q3))
     _check(rc, "decode_partials_dev")
     return pm, pl, po

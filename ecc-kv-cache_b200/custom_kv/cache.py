@@ -35,6 +35,7 @@ except ImportError:  # pragma: no cover
     _HF_CACHE_IMPORTED = False
 
 BLOCK_BYTES = 128
+RECORD96 = 96  # the block without its zero pad sector (bytes 96..127)
 HEAD_DIM = 128
 
 
@@ -49,11 +50,12 @@ def soa_views(pool: torch.Tensor):
 
 def pool_of_views(int4: torch.Tensor, syn: torch.Tensor, meta: torch.Tensor) -> Optional[torch.Tensor]:
     """If the SoA trio are views of one block pool (as soa_views makes them),
-    return that pool [..., 128] u8 as a view; else None."""
+    return that pool [..., 128] (or [..., 96]) u8 as a view; else None."""
     if int4.dtype != torch.uint8 or syn.dtype != torch.uint8 or meta.dtype != torch.float16:
         return None
-    if int4.dim() < 2 or int4.stride(-1) != 1 or int4.stride(-2) != BLOCK_BYTES:
+    if int4.dim() < 2 or int4.stride(-1) != 1 or int4.stride(-2) not in (BLOCK_BYTES, RECORD96):
         return None
+    rb = int4.stride(-2)
     base = int4.data_ptr()
     if syn.data_ptr() != base + 64 or meta.data_ptr() != base + 80:
         return None
@@ -63,7 +65,7 @@ def pool_of_views(int4: torch.Tensor, syn: torch.Tensor, meta: torch.Tensor) -> 
         return None
     if syn.shape[:-1] != int4.shape[:-1] or meta.shape[:-1] != int4.shape[:-1]:
         return None
-    return torch.as_strided(int4, int4.shape[:-1] + (BLOCK_BYTES,), int4.stride()[:-1] + (1,))
+    return torch.as_strided(int4, int4.shape[:-1] + (rb,), int4.stride()[:-1] + (1,))
 
 
 class ErrorCorrectedCache(_HFCache):
@@ -80,10 +82,16 @@ class ErrorCorrectedCache(_HFCache):
     are quantised with that layer's calibrated scale / zero point and store its
     alpha, instead of each vector's own statistics; values keep per-vector
     statistics (the config calibrates keys only).
+
+    ``block_bytes=96`` stores each block without its zero pad sector (bytes
+    96..127; codes, syndrome and metadata at the same offsets): a quarter
+    less cache memory and decode traffic.  Not the reference's format; the
+    decode then always takes the TMA-fed kernel (GQA groups up to 8).
     """
 
     def __init__(self, config, batch_size: int = 1, max_cache_len: int = 128_000, device: Optional[str] = None,
-                 rotate_values: bool = True, num_splits: int = 0, calibration: Optional[dict] = None):
+                 rotate_values: bool = True, num_splits: int = 0, calibration: Optional[dict] = None,
+                 block_bytes: int = BLOCK_BYTES):
         try:
             super().__init__()
         except (TypeError, ValueError):
@@ -110,6 +118,11 @@ class ErrorCorrectedCache(_HFCache):
             raise RuntimeError(f"ErrorCorrectedCache stores 128-dim heads (the 128-byte block format); "
                                f"got head_dim={self.head_dim}")
         self._num_layers = int(config.num_hidden_layers)
+        if block_bytes not in (BLOCK_BYTES, RECORD96):
+            raise RuntimeError(f"block_bytes must be {BLOCK_BYTES} or {RECORD96}, got {block_bytes}")
+        if block_bytes == RECORD96 and self.num_attention_heads // self.num_heads > 8:
+            raise RuntimeError("96-byte records are read by the TMA-fed decode, which takes GQA groups up to 8")
+        self.block_bytes = int(block_bytes)
         self.rotate_values = bool(rotate_values)
         self.num_splits = int(num_splits)
         self.calibration = calibration
@@ -122,7 +135,7 @@ class ErrorCorrectedCache(_HFCache):
         self._len_dev: Optional[torch.Tensor] = None
         self._dev_ws: Optional[torch.Tensor] = None
 
-        shape = (self._num_layers, self.batch_size, self.num_heads, self._max_cache_len, BLOCK_BYTES)
+        shape = (self._num_layers, self.batch_size, self.num_heads, self._max_cache_len, self.block_bytes)
         self._k_pool = torch.zeros(shape, dtype=torch.uint8, device=dev)
         self._v_pool = torch.zeros(shape, dtype=torch.uint8, device=dev)
         # reference-shaped SoA views (custom_kv/cache.py:79-84), layer 0
@@ -133,7 +146,7 @@ class ErrorCorrectedCache(_HFCache):
     # pools                                                               #
     # ------------------------------------------------------------------ #
     def layer_pools(self, layer_idx: int) -> Tuple[torch.Tensor, torch.Tensor]:
-        """(K pool, V pool) of one layer, each [B, Hkv, max_cache_len, 128] u8."""
+        """(K pool, V pool) of one layer, each [B, Hkv, max_cache_len, block_bytes] u8."""
         return self._k_pool[layer_idx], self._v_pool[layer_idx]
 
     def _pool_for_store(self, store: torch.Tensor) -> Tuple[torch.Tensor, int]:

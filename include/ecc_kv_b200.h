@@ -47,6 +47,21 @@ enum {
 #define ECC_DECODE_REGISTER_PATH 8 /* tensor-core kernel with per-lane global loads instead of the
                                       TMA-fed warp-specialised one (used automatically when a
                                       pool layout cannot be described by a tensor map) */
+#define ECC_DECODE_BLOCK96 16      /* the pools hold 96-byte records (ECC_COMPRESS_BLOCK96); block
+                                      strides count records.  TMA-fed kernel only: GQA groups up
+                                      to 8 and at least its own split count (ecc_decode: the
+                                      default, num_splits <= 0; the partials entry points: any
+                                      count >= the default); ECC_ERR_SHAPE for requests only the
+                                      other kernels take */
+
+/* Bits of the `rotate` argument of the compress entry points.  0/1 keep
+ * their meaning (input already rotated / WHT applied first). */
+#define ECC_COMPRESS_ROTATE 1   /* apply the WHT first, as compress_cpu does */
+#define ECC_COMPRESS_BLOCK96 2  /* write 96-byte records: the block without its zero pad sector
+                                   (bytes 96..127), offsets 0..95 unchanged; block strides and
+                                   positions count records; pool base 32-byte aligned.  Not a
+                                   format of the reference: an option that cuts cache memory and
+                                   decode DRAM traffic by a quarter */
 
 /* Name of an error code (static string). */
 const char *ecc_strerror(int code);
