@@ -330,7 +330,7 @@ def run_ours(args):
         from custom_kv.sharding import ShardedDecode
         # two-level combine: each rank merges its splits into one record
         # {m, l, o[128]} per (b, q head); one all-gather of the records
-        shard = ShardedDecode("seq", pg)
+        shard = ShardedDecode("seq", pg, exchange=args.exchange)
 
     def step(i, seq_len, events=None):
         # append the new token (sharded run: the last rank owns the newest chunk)
@@ -495,14 +495,24 @@ def run_ours(args):
                          "note": f"decode (split partials + merge) per step: {2 * rb} B per (token, kv head), "
                                  f"{B * HKV} (b, kv head) rows x mean {rank_ctx:.0f} tokens; traffic from ncu "
                                  f"(per launch of the decode kernel); peak {peak_kind}"},
-            "gpu_launches": K * (3 if world == 1 else (4 if rank == world - 1 else 3)),
+            "gpu_launches": K * (3 if world == 1 else
+                                 (2 if args.exchange == "p2p" else 3) + (1 if rank == world - 1 else 0)),
             "clocks": clocks, "e2e": e2e, "compress": comp, "cpu_baseline": cpu,
         }
+        if world > 1:
+            line["exchange"] = {"p2p": "one kernel: records stored into every rank's buffer over NVLink "
+                                       "(CUDA IPC), epoch flags, merge",
+                                "nccl": "merge to records, NCCL all-gather, merge"}[args.exchange]
         if comp:
             line["compress_tok_s"] = comp["tok_s"]
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
+        torch.cuda.synchronize()
+        if args.exchange == "p2p":
+            if ops.device_status() != 0:  # a bounded wait in the exchange gave up: the numbers are void
+                raise RuntimeError(f"rank {rank}: peer exchange reported device status {ops.device_status()}")
+            shard._peer.close()
         dist.barrier()
         dist.destroy_process_group()
 
@@ -782,6 +792,9 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=CTX)
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-compress", action="store_true")
+    ap.add_argument("--exchange", default="nccl", choices=["nccl", "p2p"],
+                    help="N > 1: how the ranks' records are combined (NCCL all-gather, or one kernel over "
+                         "peer memory)")
     ap.add_argument("--block-bytes", type=int, default=BLOCK, choices=[BLOCK, 96],
                     help="record size of the decode pools: the 128-byte block (default, the reference's "
                          "format) or the 96-byte record without the pad sector")

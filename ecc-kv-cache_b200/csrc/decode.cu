@@ -12,6 +12,7 @@
 // combines (m, l, o) of the splits.
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 
 #include "ecc_common.cuh"
 
@@ -299,6 +300,122 @@ lse_merge_records_kernel(const float *__restrict__ rec, int n, int64_t stride, _
     write_out(L, O, out, blockIdx.x, threadIdx.x, flags, sh);
 }
 
+// ---------------------------------------------------------------------------
+// Record exchange over peer memory (sequence-sharded decode, one GPU per
+// rank, no NCCL): one kernel per rank and step does the two-level combine of
+// lse_merge_record_kernel -> all-gather -> lse_merge_records_kernel.
+//
+// Every rank owns an exchange buffer that all ranks can store to (a CUDA IPC
+// mapping on each peer): records float [2][W][rows][kRec], then epoch flags
+// uint32 [2][W][grid].  Call e (epoch e >= 1, the same sequence on every
+// rank) uses half p = e & 1.  CTA b of rank s merges its split partials of
+// rows b, b + grid, ... into records, stores them into slot [p][s][row] of
+// every rank's buffer, and then sets flag [p][s][b] = e in every buffer
+// (release, system scope, after a system-scope fence).  It then waits until
+// flag [p][q][b] = e in its own buffer for every rank q -- the same CTA index
+// of every rank, which stored exactly the same rows -- and merges the W
+// records of each of its rows.  A CTA depends only on the same-index CTAs of
+// the other GPUs, the grid is at most the SM count (all CTAs resident on an
+// idle GPU) and the launch is a plain one (it starts after the previous
+// kernel has finished and lets no dependent start early), so no CTA waits
+// for one that cannot run.  Half p is reused two calls later: a rank can only
+// start call e + 2 after every rank's records of call e + 1 arrived, which
+// each rank stores after finishing its merge of call e.  The wait is bounded;
+// a CTA that gives up raises g_exchange_error (ecc_device_status reports 4)
+// and writes nothing.
+// ---------------------------------------------------------------------------
+constexpr int kExchMaxRanks = ECC_EXCHANGE_MAX_RANKS;
+constexpr int kExchMaxGrid = 128;
+struct PeerBufs {
+    float *base[kExchMaxRanks];
+};
+__device__ int g_exchange_error;
+
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// Records written by other GPUs: loads that skip L1.
+struct PeerRecordSrc {
+    const float *rec;
+    int64_t row, stride;
+    __device__ const float *at(int i) const { return rec + i * stride + row * kRec; }
+    __device__ float m(int i) const { return __ldcg(at(i)); }
+    __device__ float l(int i) const { return __ldcg(at(i) + 1); }
+    __device__ float o(int i, int d) const { return __ldcg(at(i) + 2 + d); }
+};
+
+__global__ void __launch_bounds__(kD)
+lse_exchange_kernel(const float *__restrict__ pm, const float *__restrict__ pl, const float *__restrict__ po, int n,
+                    int64_t rows, int W, int rank, PeerBufs peers, uint32_t epoch, long long wait_cycles,
+                    __half *__restrict__ out, int flags) {
+    __shared__ float sh[kD];
+    __shared__ int s_ok;
+    const int d = threadIdx.x;
+    const int grid = gridDim.x, b = blockIdx.x;
+    const int64_t half = epoch & 1u;
+    const int64_t rec_floats = 2 * (int64_t)W * rows * kRec;
+    // 1. this rank's record of each row, stored into every rank's buffer
+    for (int64_t r = b; r < rows; r += grid) {
+        float M, L, O;
+        lse_combine(n, d, SplitSrc{pm, pl, po, r, n}, M, L, O);
+        for (int q = 0; q < W; ++q) {
+            float *dst = peers.base[q] + ((half * W + rank) * rows + r) * kRec;
+            if (d == 0) {
+                dst[0] = M;
+                dst[1] = L;
+            }
+            dst[2 + d] = O;
+        }
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (d < W) {
+        uint32_t *fl = reinterpret_cast<uint32_t *>(peers.base[d] + rec_floats) + (half * W + rank) * grid + b;
+        __threadfence_system();
+        st_release_sys(fl, epoch);
+    }
+    // 2. the same CTA of every rank (bounded wait)
+    if (d == 0) s_ok = 1;
+    __syncthreads();
+    if (d < W) {
+        const uint32_t *fl =
+            reinterpret_cast<const uint32_t *>(peers.base[rank] + rec_floats) + (half * W + d) * grid + b;
+        const long long t0 = clock64();
+        while (ld_acquire_sys(fl) != epoch) {
+            if (clock64() - t0 > wait_cycles) {
+                atomicExch(&g_exchange_error, 4);
+                s_ok = 0;
+                break;
+            }
+        }
+    }
+    __syncthreads();
+    if (!s_ok) return;  // block-uniform
+    __threadfence_system();
+    // 3. merge the W records of each row
+    const float *mine = peers.base[rank] + half * W * rows * kRec;
+    for (int64_t r = b; r < rows; r += grid) {
+        float M, L, O;
+        lse_combine(W, d, PeerRecordSrc{mine, r, rows * kRec}, M, L, O);
+        write_out(L, O, out, r, d, flags, sh);
+    }
+}
+
+int exchange_device_error(int reset) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_exchange_error, sizeof(int)) != cudaSuccess) return ECC_ERR_CUDA;
+    if (reset) {
+        const int z = 0;
+        if (cudaMemcpyToSymbol(g_exchange_error, &z, sizeof(int)) != cudaSuccess) return ECC_ERR_CUDA;
+    }
+    return v;
+}
+
 }  // namespace ecc
 
 using namespace ecc;
@@ -584,4 +701,79 @@ extern "C" int ecc_decode_static(const void *q_f16, const void *k_blocks, const 
     if (rc != ECC_OK) return rc;
     return ecc_decode(q_f16, k_blocks, v_blocks, bs_b, bs_h, out_f16, scratch, cap, B, Hq, Hkv, seq_len, sm_scale,
                       flags, ns_req, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Record exchange over peer memory (lse_exchange_kernel above).
+// ---------------------------------------------------------------------------
+extern "C" int ecc_exchange_grid(int64_t rows) {
+    if (rows <= 0) return 0;
+    return (int)std::min<int64_t>({rows, (int64_t)kExchMaxGrid, (int64_t)sm_count()});
+}
+
+extern "C" size_t ecc_exchange_buffer_bytes(int64_t rows, int world) {
+    if (rows <= 0 || world < 1 || world > kExchMaxRanks) return 0;
+    return (size_t)2 * world * rows * kRec * sizeof(float) + (size_t)2 * world * kExchMaxGrid * sizeof(uint32_t);
+}
+
+// The exchange buffer: a whole cudaMalloc allocation (so that its IPC handle
+// maps exactly it), zero-filled; the handle travels to the other ranks, which
+// map it on their own device with peer access enabled lazily.
+static_assert(sizeof(cudaIpcMemHandle_t) == ECC_IPC_HANDLE_BYTES, "IPC handle size");
+
+extern "C" int ecc_exchange_alloc(int64_t rows, int world, void **buffer, void *ipc_handle) {
+    const size_t bytes = ecc_exchange_buffer_bytes(rows, world);
+    if (!bytes) return ECC_ERR_SHAPE;
+    if (!buffer || !ipc_handle) return ECC_ERR_NULL;
+    void *p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) return ECC_ERR_CUDA;
+    cudaIpcMemHandle_t h;
+    if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess ||
+        cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+        cudaFree(p);
+        return ECC_ERR_CUDA;
+    }
+    std::memcpy(ipc_handle, &h, sizeof(h));
+    *buffer = p;
+    return ECC_OK;
+}
+
+extern "C" int ecc_exchange_open(const void *ipc_handle, void **peer_buffer) {
+    if (!ipc_handle || !peer_buffer) return ECC_ERR_NULL;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, ipc_handle, sizeof(h));
+    return cudaIpcOpenMemHandle(peer_buffer, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? ECC_OK
+                                                                                                 : ECC_ERR_CUDA;
+}
+
+extern "C" int ecc_exchange_close(void *peer_buffer) {
+    if (!peer_buffer) return ECC_ERR_NULL;
+    return cudaIpcCloseMemHandle(peer_buffer) == cudaSuccess ? ECC_OK : ECC_ERR_CUDA;
+}
+
+extern "C" int ecc_exchange_free(void *buffer) {
+    if (!buffer) return ECC_ERR_NULL;
+    return cudaFree(buffer) == cudaSuccess ? ECC_OK : ECC_ERR_CUDA;
+}
+
+extern "C" int ecc_lse_exchange_merge(const float *part_m, const float *part_l, const float *part_o, int64_t rows,
+                                      int n, void *const *peer_buffers, int world, int rank, uint32_t epoch,
+                                      long long wait_cycles, void *out_f16, int flags, ecc_stream_t stream) {
+    if (rows <= 0 || n <= 0 || world < 1 || world > kExchMaxRanks || rank < 0 || rank >= world || epoch == 0 ||
+        wait_cycles <= 0 || rows > 0x7fffffff)
+        return ECC_ERR_SHAPE;
+    if (!part_m || !part_l || !part_o || !peer_buffers || !out_f16) return ECC_ERR_NULL;
+    PeerBufs pb{};
+    for (int q = 0; q < world; ++q) {
+        if (!peer_buffers[q]) return ECC_ERR_NULL;
+        if ((uintptr_t)peer_buffers[q] % 16) return ECC_ERR_ALIGN;
+        pb.base[q] = reinterpret_cast<float *>(peer_buffers[q]);
+    }
+    const int grid = ecc_exchange_grid(rows);
+    // plain launch: starts after the previous kernel on the stream has
+    // finished, and no dependent kernel starts before this one ends
+    lse_exchange_kernel<<<grid, kD, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        part_m, part_l, part_o, n, rows, world, rank, pb, epoch, wait_cycles, reinterpret_cast<__half *>(out_f16),
+        flags & ECC_DECODE_UNROTATE_OUT);
+    return launch_status();
 }

@@ -965,6 +965,7 @@ extern "C" int ecc_selftest_wait_timeout(long long limit_cycles, int *host_gave_
 
 namespace ecc {
 int compress_device_error(int reset);
+int exchange_device_error(int reset);
 }
 
 extern "C" int ecc_device_status(int reset) {
@@ -976,5 +977,7 @@ extern "C" int ecc_device_status(int reset) {
     }
     const int c = ecc::compress_device_error(reset);
     if (c < 0) return c;
-    return v ? v : c;
+    const int x = ecc::exchange_device_error(reset);
+    if (x < 0) return x;
+    return v ? v : (c ? c : x);
 }

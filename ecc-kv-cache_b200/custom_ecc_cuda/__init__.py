@@ -28,7 +28,8 @@ __all__ = [
     "compress_into", "decode_attention", "decode_partials", "lse_merge", "dequantize", "pack_soa",
     "decode_workspace_size", "default_splits", "library_path", "EccError", "compress_calibrated_into",
     "compress_pair_at", "compress_calibrated_at", "decode_attention_dev", "decode_dev_workspace_size",
-    "decode_partials_dev", "decode_dev_splits",
+    "decode_partials_dev", "decode_dev_splits", "exchange_buffer_bytes", "lse_exchange_merge",
+    "exchange_alloc", "exchange_open", "exchange_close", "exchange_free",
 ]
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -88,6 +89,14 @@ def _load():
         "ecc_lse_merge_to_record": ([p, p, p, i64, i32, p, p], i32),
         "ecc_lse_merge_records": ([p, i64, i32, i64, p, i32, p], i32),
         "ecc_device_status": ([i32], i32),
+        "ecc_exchange_buffer_bytes": ([i64, i32], ctypes.c_size_t),
+        "ecc_exchange_grid": ([i64], i32),
+        "ecc_exchange_alloc": ([i64, i32, p, p], i32),
+        "ecc_exchange_open": ([p, p], i32),
+        "ecc_exchange_close": ([p], i32),
+        "ecc_exchange_free": ([p], i32),
+        "ecc_lse_exchange_merge": ([p, p, p, i64, i32, p, i32, i32, ctypes.c_uint32, ctypes.c_longlong, p, i32, p],
+                                   i32),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -492,11 +501,9 @@ def lse_merge(pm: torch.Tensor, pl: torch.Tensor, po: torch.Tensor, unrotate_out
 RECORD_FLOATS = 2 + D
 
 
-def lse_merge_to_record(pm: torch.Tensor, pl: torch.Tensor, po: torch.Tensor,
-                        out: torch.Tensor | None = None) -> torch.Tensor:
-    """Merge partials along their split axis into one partial record per row:
-    pm/pl [..., n], po [..., n, 128] -> [..., 130] fp32 {m, l, o[128]} (o
-    unnormalised).  Records of several devices merge with lse_merge_records."""
+def _check_partials(pm: torch.Tensor, pl: torch.Tensor, po: torch.Tensor):
+    """Contiguous fp32 CUDA split partials pm/pl [..., n], po [..., n, 128];
+    returns (rows, n)."""
     for t, nme in ((pm, "pm"), (pl, "pl"), (po, "po")):
         _require_input(t, nme)
         if t.dtype != torch.float32:
@@ -505,6 +512,15 @@ def lse_merge_to_record(pm: torch.Tensor, pl: torch.Tensor, po: torch.Tensor,
     rows = pm.numel() // max(n, 1)
     if pl.shape != pm.shape or po.shape != pm.shape + (D,):
         raise RuntimeError("partial shapes disagree")
+    return rows, n
+
+
+def lse_merge_to_record(pm: torch.Tensor, pl: torch.Tensor, po: torch.Tensor,
+                        out: torch.Tensor | None = None) -> torch.Tensor:
+    """Merge partials along their split axis into one partial record per row:
+    pm/pl [..., n], po [..., n, 128] -> [..., 130] fp32 {m, l, o[128]} (o
+    unnormalised).  Records of several devices merge with lse_merge_records."""
+    rows, n = _check_partials(pm, pl, po)
     if out is None:
         out = torch.empty(pm.shape[:-1] + (RECORD_FLOATS,), dtype=torch.float32, device=pm.device)
     elif not out.is_contiguous() or out.dtype != torch.float32 or out.numel() != rows * RECORD_FLOATS:
@@ -537,11 +553,78 @@ def version() -> int:
     return int(_lib.ecc_version())
 
 
+def exchange_buffer_bytes(rows: int, world: int) -> int:
+    """Bytes of one rank's peer-exchange buffer for ``rows`` rows (B * Hq)."""
+    return int(_lib.ecc_exchange_buffer_bytes(rows, world))
+
+
+IPC_HANDLE_BYTES = 64
+
+
+def exchange_alloc(rows: int, world: int, device: torch.device):
+    """This rank's zero-filled exchange buffer on ``device``: (device address,
+    IPC handle bytes for the other ranks).  Free with exchange_free."""
+    buf = ctypes.c_void_p()
+    handle = (ctypes.c_char * IPC_HANDLE_BYTES)()
+    with torch.cuda.device(device):
+        rc = _lib.ecc_exchange_alloc(int(rows), int(world), ctypes.byref(buf), handle)
+    _check(rc, "exchange_alloc")
+    return buf.value, bytes(handle)
+
+
+def exchange_open(handle: bytes, device: torch.device) -> int:
+    """Map another rank's exchange buffer (its IPC handle) on ``device``;
+    returns its device address in this process.  Unmap with exchange_close."""
+    if len(handle) != IPC_HANDLE_BYTES:
+        raise RuntimeError("bad IPC handle")
+    ptr = ctypes.c_void_p()
+    with torch.cuda.device(device):
+        rc = _lib.ecc_exchange_open(ctypes.create_string_buffer(handle, IPC_HANDLE_BYTES), ctypes.byref(ptr))
+    _check(rc, "exchange_open")
+    return ptr.value
+
+
+def exchange_close(ptr: int, device: torch.device) -> None:
+    with torch.cuda.device(device):
+        _check(_lib.ecc_exchange_close(ctypes.c_void_p(ptr)), "exchange_close")
+
+
+def exchange_free(ptr: int, device: torch.device) -> None:
+    with torch.cuda.device(device):
+        _check(_lib.ecc_exchange_free(ctypes.c_void_p(ptr)), "exchange_free")
+
+
+def lse_exchange_merge(pm: torch.Tensor, pl: torch.Tensor, po: torch.Tensor, peer_ptrs, rank: int, epoch: int,
+                       unrotate_out: bool = False, out: torch.Tensor | None = None,
+                       wait_cycles: int = 10_000_000_000) -> torch.Tensor:
+    """Sequence-sharded combine over peer memory: this rank's split partials
+    pm/pl [..., n], po [..., n, 128] are merged into one record per row,
+    stored into every rank's exchange buffer (``peer_ptrs``: device addresses
+    of all ranks' buffers as mapped in this process, ``peer_ptrs[rank]`` this
+    rank's own), and the records of all ranks merged into out [..., 128]
+    fp16 -- what lse_merge_to_record, an all-gather and lse_merge_records
+    give, in one kernel.  ``epoch``: 1, 2, ... in step on every rank."""
+    rows, n = _check_partials(pm, pl, po)
+    W = len(peer_ptrs)
+    if out is None:
+        out = torch.empty(pm.shape[:-1] + (D,), dtype=torch.float16, device=pm.device)
+    elif not out.is_contiguous() or out.dtype != torch.float16 or out.numel() != rows * D:
+        raise RuntimeError("out must be a contiguous float16 tensor of rows*128 elements")
+    arr = (ctypes.c_void_p * W)(*[int(x) for x in peer_ptrs])
+    with torch.cuda.device(pm.device):
+        rc = _lib.ecc_lse_exchange_merge(_ptr(pm), _ptr(pl), _ptr(po), rows, n, arr, W, int(rank), int(epoch),
+                                         int(wait_cycles), _ptr(out), UNROTATE_OUT if unrotate_out else 0,
+                                         _stream(pm))
+    _check(rc, "lse_exchange_merge")
+    return out
+
+
 def device_status(reset: bool = False) -> int:
     """Device-side error flag of the current device since the last reset:
     1 (or 2) if a decode kernel gave up a bounded wait (it returned early
     instead of hanging), 3 if an append at a device-side position was out of
-    range (it wrote nothing), else 0."""
+    range (it wrote nothing), 4 if lse_exchange_merge gave up waiting for
+    another rank's records (those rows were not written), else 0."""
     rc = int(_lib.ecc_device_status(1 if reset else 0))
     if rc < 0:
         _check(rc, "device_status")

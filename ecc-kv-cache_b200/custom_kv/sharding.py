@@ -10,7 +10,10 @@
   appended on the last rank.  Each rank computes split partials (m, l, o) of
   its chunk, merges them into one 130-float record {m, l, o[128]} per
   (sequence, query head), the records are all-gathered and merged (the
-  log-sum-exp combine of flash-decoding).
+  log-sum-exp combine of flash-decoding).  With ``exchange="p2p"`` the
+  record merge, the exchange and the final merge are one kernel per rank
+  that stores its records straight into every rank's buffer over NVLink
+  (``PeerExchange``) instead of an NCCL all-gather between two kernels.
 
 The reference keeps everything on one device (custom_kv/cache.py:79-84); this
 module is the multi-GPU layer around the same fused decode.  Every rank takes
@@ -67,6 +70,57 @@ def _all_gather(out: torch.Tensor, inp: torch.Tensor, group) -> None:
         dist.all_gather(list(out.unbind(0)), inp, group=group)
 
 
+class PeerExchange:
+    """Peer-memory exchange buffers for the records of ``rows`` rows (B * Hq)
+    on every rank of ``group`` (one GPU per rank, one node): each rank
+    allocates a zero-filled buffer, passes its CUDA IPC handle to the others
+    and maps theirs on its own device, so that
+    custom_ecc_cuda.lse_exchange_merge can store into all of them.  Made
+    collectively (every rank at the same point); calls of ``merge`` must then
+    be made in step on every rank, and ``close`` collectively at the end.
+    Not for CUDA-graph capture: each call's epoch is a kernel argument."""
+
+    def __init__(self, rows: int, group, device: torch.device, ops=None):
+        if ops is None:
+            import custom_ecc_cuda as ops  # noqa: F811
+        self.ops = ops
+        self.rows = int(rows)
+        self.group = group
+        self.device = device
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.own, handle = ops.exchange_alloc(self.rows, self.world, device)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=group)
+        self.ptrs = [self.own if q == self.rank else ops.exchange_open(h, device) for q, h in enumerate(handles)]
+        self.epoch = 0
+        dist.barrier(group=group)  # every buffer zeroed and mapped before the first call
+
+    def merge(self, pm: torch.Tensor, pl: torch.Tensor, po: torch.Tensor, unrotate_out: bool = True,
+              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if not self.ptrs:
+            raise RuntimeError("the exchange is closed")
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("the peer exchange cannot be recorded in a CUDA graph (use exchange='nccl')")
+        self.epoch += 1
+        return self.ops.lse_exchange_merge(pm, pl, po, self.ptrs, self.rank, self.epoch, unrotate_out=unrotate_out,
+                                           out=out)
+
+    def close(self) -> None:
+        """Unmap the other ranks' buffers and free this rank's (collective;
+        every rank's last merge must have finished)."""
+        if not self.ptrs:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for q, p in enumerate(self.ptrs):
+            if q != self.rank:
+                self.ops.exchange_close(p, self.device)
+        dist.barrier(group=self.group)  # nobody maps this rank's buffer any more
+        self.ops.exchange_free(self.own, self.device)
+        self.ptrs = []
+
+
 class ShardedDecode:
     """One decode step of a sharded layer on this rank.
 
@@ -74,11 +128,18 @@ class ShardedDecode:
     custom_ecc_cuda: decode_attention, decode_partials, lse_merge_to_record,
     lse_merge_records, RECORD_FLOATS).  Buffers for the exchange are made on
     first use and reused, so a steady decode loop allocates nothing.
+    ``exchange`` (seq mode): "nccl" (all-gather of the records between two
+    merge kernels) or "p2p" (one kernel over peer memory, PeerExchange; GPUs
+    of one node, not inside a CUDA graph).
     """
 
-    def __init__(self, mode: str, group=None, ops=None):
+    def __init__(self, mode: str, group=None, ops=None, exchange: str = "nccl"):
         if mode not in ("kv", "seq"):
             raise ValueError("mode must be 'kv' or 'seq'")
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError("exchange must be 'nccl' or 'p2p'")
+        self.exchange = exchange
+        self._peer: Optional[PeerExchange] = None
         if ops is None:
             import custom_ecc_cuda as ops  # noqa: F811
         self.mode = mode
@@ -151,6 +212,14 @@ class ShardedDecode:
         else:
             pm, pl, po = ops.decode_partials(query, k_pool, v_pool, seq_len=local_len, num_splits=num_splits,
                                              rotate_q=rotate_q)
+        if self.exchange == "p2p":
+            if mark is not None:
+                mark.record()
+            if self._peer is None or self._peer.rows != B * hq_l:
+                self._peer = PeerExchange(B * hq_l, self.group, query.device, ops=ops)
+            if out is None:
+                out = torch.empty((B, hq_l, 1, D), dtype=torch.float16, device=query.device)
+            return self._peer.merge(pm, pl, po, unrotate_out=unrotate_out, out=out)
         rec = self._buf("rec", (B, hq_l, ops.RECORD_FLOATS), torch.float32, query.device)
         ops.lse_merge_to_record(pm, pl, po, out=rec)
         if mark is not None:

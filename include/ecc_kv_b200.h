@@ -251,6 +251,44 @@ int ecc_lse_merge_to_record(const float *part_m, const float *part_l, const floa
 int ecc_lse_merge_records(const float *records, int64_t rows, int n, int64_t record_stride, void *out_f16,
                           int flags, ecc_stream_t stream);
 
+/* Record exchange over peer memory, for sequences sharded over the GPUs of
+ * one node (no counterpart in the reference, which runs on one GPU): the
+ * two-level combine above -- ecc_lse_merge_to_record, an all-gather of the
+ * records, ecc_lse_merge_records -- as one kernel per rank and step, with the
+ * records stored straight into every rank's exchange buffer over NVLink.
+ *   ecc_exchange_buffer_bytes(rows, world): bytes of one rank's exchange
+ *     buffer (zero-filled once before the first call).
+ *   ecc_exchange_grid(rows): CTAs per call (the same on every rank).
+ *   ecc_lse_exchange_merge: part_m/l/o as for ecc_lse_merge (this rank's n
+ *     split partials of every row); peer_buffers: HOST array of `world`
+ *     device pointers, entry q = rank q's exchange buffer as mapped in this
+ *     process (entry `rank` = this rank's own); epoch: 1, 2, 3, ... -- the
+ *     same sequence on every rank, one per call; wait_cycles: bound of the
+ *     wait for the other ranks' records (SM clock cycles), after which the
+ *     kernel raises the ecc_device_status flag (value 4) and returns without
+ *     writing those rows.  out [rows, 128] fp16 as ecc_lse_merge_records
+ *     writes it (bit-identical); flags may hold ECC_DECODE_UNROTATE_OUT.
+ *     Every rank must make the same sequence of calls with the same rows. */
+#define ECC_EXCHANGE_MAX_RANKS 8
+#define ECC_IPC_HANDLE_BYTES 64
+size_t ecc_exchange_buffer_bytes(int64_t rows, int world);
+/* Exchange buffers, one per rank, on the current device (synchronous):
+ *   ecc_exchange_alloc: allocates and zero-fills this rank's buffer and
+ *     writes its CUDA IPC handle (ECC_IPC_HANDLE_BYTES host bytes) for the
+ *     other ranks;
+ *   ecc_exchange_open: maps another rank's buffer from its handle into this
+ *     process on the current device (peer access enabled as needed);
+ *   ecc_exchange_close: unmaps a buffer ecc_exchange_open mapped;
+ *   ecc_exchange_free: frees this rank's buffer once every rank has closed it. */
+int ecc_exchange_alloc(int64_t rows, int world, void **buffer, void *ipc_handle);
+int ecc_exchange_open(const void *ipc_handle, void **peer_buffer);
+int ecc_exchange_close(void *peer_buffer);
+int ecc_exchange_free(void *buffer);
+int ecc_exchange_grid(int64_t rows);
+int ecc_lse_exchange_merge(const float *part_m, const float *part_l, const float *part_o, int64_t rows, int n,
+                           void *const *peer_buffers, int world, int rank, uint32_t epoch, long long wait_cycles,
+                           void *out_f16, int flags, ecc_stream_t stream);
+
 /* Bytes of the library-owned device array ecc_decode_static uses for its
  * split partials (4 MiB on every GPU that loads the library, kept until the
  * process exits). */

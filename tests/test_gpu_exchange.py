@@ -1,0 +1,120 @@
+"""The record exchange over peer memory (custom_ecc_cuda.lse_exchange_merge)
+on the GPU.  One GPU: with one rank the kernel's merge equals
+lse_merge_to_record + lse_merge_records bit for bit over successive epochs
+(both buffer halves), and a wait for a rank that never stores gives up,
+raises the device flag and leaves the GPU usable.  Two GPUs (skipped with
+fewer): sequence-sharded decode steps with the p2p exchange equal those with
+the NCCL all-gather bit for bit."""
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+D = 128
+
+
+@pytest.fixture(scope="module")
+def ops(cuda_device):
+    import custom_ecc_cuda
+    return custom_ecc_cuda
+
+
+def _partials(B, hq, n, seed, dev):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    pm = torch.randn(B, hq, n, device=dev, generator=g) * 3
+    pl = torch.rand(B, hq, n, device=dev, generator=g) * 5
+    pl[:, :, -1] = 0.0  # an empty split
+    pm[:, :, -1] = -float("inf")
+    po = torch.randn(B, hq, n, D, device=dev, generator=g)
+    return pm, pl, po
+
+
+@pytest.mark.parametrize("B,hq,n", [(8, 32, 29), (1, 4, 1), (3, 40, 70)])
+def test_single_rank_exchange_equals_two_level_merge(ops, cuda_device, B, hq, n):
+    rows = B * hq
+    buf = torch.zeros(ops.exchange_buffer_bytes(rows, 1), dtype=torch.uint8, device=cuda_device)
+    for epoch in range(1, 5):
+        pm, pl, po = _partials(B, hq, n, epoch, cuda_device)
+        unrot = bool(epoch & 1)
+        ref = ops.lse_merge_records(ops.lse_merge_to_record(pm, pl, po).unsqueeze(0), unrotate_out=unrot)
+        got = ops.lse_exchange_merge(pm, pl, po, [buf.data_ptr()], 0, epoch, unrotate_out=unrot)
+        assert torch.equal(got.reshape(ref.shape), ref), epoch
+    assert ops.device_status() == 0
+
+
+def test_exchange_argument_errors(ops, cuda_device):
+    pm, pl, po = _partials(1, 4, 3, 0, cuda_device)
+    buf = torch.zeros(ops.exchange_buffer_bytes(4, 1), dtype=torch.uint8, device=cuda_device)
+    with pytest.raises(RuntimeError):  # epochs start at 1
+        ops.lse_exchange_merge(pm, pl, po, [buf.data_ptr()], 0, 0)
+    with pytest.raises(RuntimeError):  # rank outside the peer list
+        ops.lse_exchange_merge(pm, pl, po, [buf.data_ptr()], 1, 1)
+    with pytest.raises(RuntimeError):  # more ranks than one node's limit
+        ops.lse_exchange_merge(pm, pl, po, [buf.data_ptr()] * 9, 0, 1)
+    assert ops.exchange_buffer_bytes(4, 9) == 0
+
+
+def test_wait_for_missing_rank_gives_up(ops, cuda_device):
+    """A second 'rank' whose buffer is local memory that no kernel ever flags:
+    the wait runs out after ~1e6 cycles, the kernel returns, the device flag
+    reads 4 and clears, and the next call on the device works."""
+    pm, pl, po = _partials(2, 8, 5, 1, cuda_device)
+    rows = 16
+    mine = torch.zeros(ops.exchange_buffer_bytes(rows, 2), dtype=torch.uint8, device=cuda_device)
+    other = torch.zeros_like(mine)
+    ops.device_status(reset=True)
+    ops.lse_exchange_merge(pm, pl, po, [mine.data_ptr(), other.data_ptr()], 0, 1, wait_cycles=1_000_000)
+    torch.cuda.synchronize()
+    assert ops.device_status(reset=True) == 4
+    assert ops.device_status() == 0
+    one = torch.zeros(ops.exchange_buffer_bytes(rows, 1), dtype=torch.uint8, device=cuda_device)
+    ref = ops.lse_merge_records(ops.lse_merge_to_record(pm, pl, po).unsqueeze(0))
+    got = ops.lse_exchange_merge(pm, pl, po, [one.data_ptr()], 0, 1)
+    assert torch.equal(got.reshape(ref.shape), ref)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _two_gpu_worker(rank, world, port):
+    import datetime
+    import torch.distributed as dist
+    import custom_ecc_cuda as ops
+    from custom_kv.sharding import ShardedDecode
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=dev)
+    try:
+        B, hkv, hq, cap = 2, 4, 16, 3000
+        g = torch.Generator(device=dev).manual_seed(100 + rank)
+        kp = torch.zeros((B, hkv, cap, 128), dtype=torch.uint8, device=dev)
+        vp = torch.zeros_like(kp)
+        n0 = 2500 + 137 * rank
+        ops.compress_into(torch.randn(B, hkv, n0, D, device=dev, generator=g).half(), kp, pos=0)
+        ops.compress_into(torch.randn(B, hkv, n0, D, device=dev, generator=g).half(), vp, pos=0)
+        ref, p2p = ShardedDecode("seq"), ShardedDecode("seq", exchange="p2p")
+        ns = ops.default_splits(B, hkv, cap) + 1
+        for step in range(6):
+            q = torch.randn(B, hq, 1, D, generator=torch.Generator().manual_seed(step)).half().to(dev)
+            a = ref.step(q, kp, vp, n0 + step, num_splits=ns)
+            b = p2p.step(q, kp, vp, n0 + step, num_splits=ns)
+            assert torch.equal(a, b), (rank, step)
+            if rank == world - 1:  # the last rank's chunk grows
+                ops.compress_into(torch.randn(B, hkv, 1, D, device=dev, generator=g).half(), kp, pos=n0 + step)
+        torch.cuda.synchronize()
+        assert ops.device_status() == 0
+        p2p._peer.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_gpus_p2p_exchange_equals_nccl():
+    import torch.multiprocessing as mp
+    mp.start_processes(_two_gpu_worker, args=(2, _free_port()), nprocs=2, start_method="spawn")
