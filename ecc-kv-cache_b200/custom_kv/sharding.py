@@ -212,13 +212,13 @@ class ShardedDecode:
         else:
             pm, pl, po = ops.decode_partials(query, k_pool, v_pool, seq_len=local_len, num_splits=num_splits,
                                              rotate_q=rotate_q)
+        if out is None:
+            out = torch.empty((B, hq_l, 1, D), dtype=torch.float16, device=query.device)
         if self.exchange == "p2p":
             if mark is not None:
                 mark.record()
             if self._peer is None or self._peer.rows != B * hq_l:
                 self._peer = PeerExchange(B * hq_l, self.group, query.device, ops=ops)
-            if out is None:
-                out = torch.empty((B, hq_l, 1, D), dtype=torch.float16, device=query.device)
             return self._peer.merge(pm, pl, po, unrotate_out=unrotate_out, out=out)
         rec = self._buf("rec", (B, hq_l, ops.RECORD_FLOATS), torch.float32, query.device)
         ops.lse_merge_to_record(pm, pl, po, out=rec)
