@@ -315,17 +315,20 @@ lse_merge_records_kernel(const float *__restrict__ rec, int n, int64_t stride, _
 // flag [p][q][b] = e in its own buffer for every rank q -- the same CTA index
 // of every rank, which stored exactly the same rows -- and merges the W
 // records of each of its rows.  A CTA depends only on the same-index CTAs of
-// the other GPUs, the grid is at most the SM count (all CTAs resident on an
-// idle GPU) and the launch is a plain one (it starts after the previous
-// kernel has finished and lets no dependent start early), so no CTA waits
-// for one that cannot run.  Half p is reused two calls later: a rank can only
+// the other GPUs, and every CTA of the grid can be resident at once (the grid
+// is capped by the kernel's occupancy times the SM count).  The kernel is a
+// programmatic dependent of the one before it (its launch overlaps that
+// kernel's tail; its CTAs start work after griddepcontrol.wait) and never
+// lets a dependent of its own start early, so once the previous kernel has
+// ended nothing else holds the SMs and no CTA waits for one that cannot run.
+// Half p is reused two calls later: a rank can only
 // start call e + 2 after every rank's records of call e + 1 arrived, which
 // each rank stores after finishing its merge of call e.  The wait is bounded;
 // a CTA that gives up raises g_exchange_error (ecc_device_status reports 4)
 // and writes nothing.
 // ---------------------------------------------------------------------------
 constexpr int kExchMaxRanks = ECC_EXCHANGE_MAX_RANKS;
-constexpr int kExchMaxGrid = 128;
+constexpr int kExchMaxGrid = 1024;
 struct PeerBufs {
     float *base[kExchMaxRanks];
 };
@@ -359,6 +362,7 @@ lse_exchange_kernel(const float *__restrict__ pm, const float *__restrict__ pl, 
     const int grid = gridDim.x, b = blockIdx.x;
     const int64_t half = epoch & 1u;
     const int64_t rec_floats = 2 * (int64_t)W * rows * kRec;
+    pdl_wait();  // the partials of the kernel before
     // 1. this rank's record of each row, stored into every rank's buffer
     for (int64_t r = b; r < rows; r += grid) {
         float M, L, O;
@@ -372,8 +376,7 @@ lse_exchange_kernel(const float *__restrict__ pm, const float *__restrict__ pl, 
             dst[2 + d] = O;
         }
     }
-    __threadfence_system();
-    __syncthreads();
+    __syncthreads();  // the CTA's record stores precede the flag threads' fences
     if (d < W) {
         uint32_t *fl = reinterpret_cast<uint32_t *>(peers.base[d] + rec_floats) + (half * W + rank) * grid + b;
         __threadfence_system();
@@ -393,10 +396,10 @@ lse_exchange_kernel(const float *__restrict__ pm, const float *__restrict__ pl, 
                 break;
             }
         }
+        __threadfence_system();
     }
-    __syncthreads();
+    __syncthreads();  // the acquires precede every thread's record loads
     if (!s_ok) return;  // block-uniform
-    __threadfence_system();
     // 3. merge the W records of each row
     const float *mine = peers.base[rank] + half * W * rows * kRec;
     for (int64_t r = b; r < rows; r += grid) {
@@ -706,9 +709,18 @@ extern "C" int ecc_decode_static(const void *q_f16, const void *k_blocks, const 
 // ---------------------------------------------------------------------------
 // Record exchange over peer memory (lse_exchange_kernel above).
 // ---------------------------------------------------------------------------
+// CTAs of one exchange call: one per row up to kExchMaxGrid, and never more
+// than can be resident at once on the device.
 extern "C" int ecc_exchange_grid(int64_t rows) {
     if (rows <= 0) return 0;
-    return (int)std::min<int64_t>({rows, (int64_t)kExchMaxGrid, (int64_t)sm_count()});
+    static int per_sm = 0;
+    if (!per_sm) {
+        int nb = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, lse_exchange_kernel, kD, 0) != cudaSuccess || nb < 1)
+            nb = 1;
+        per_sm = nb;
+    }
+    return (int)std::min<int64_t>({rows, (int64_t)kExchMaxGrid, (int64_t)per_sm * sm_count()});
 }
 
 extern "C" size_t ecc_exchange_buffer_bytes(int64_t rows, int world) {
@@ -770,10 +782,11 @@ extern "C" int ecc_lse_exchange_merge(const float *part_m, const float *part_l, 
         pb.base[q] = reinterpret_cast<float *>(peer_buffers[q]);
     }
     const int grid = ecc_exchange_grid(rows);
-    // plain launch: starts after the previous kernel on the stream has
-    // finished, and no dependent kernel starts before this one ends
-    lse_exchange_kernel<<<grid, kD, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-        part_m, part_l, part_o, n, rows, world, rank, pb, epoch, wait_cycles, reinterpret_cast<__half *>(out_f16),
-        flags & ECC_DECODE_UNROTATE_OUT);
+    // a programmatic dependent of the previous kernel; it never triggers its
+    // own dependents, so none starts before it ends
+    if (launch_pdl(lse_exchange_kernel, dim3(grid), dim3(kD), 0, reinterpret_cast<cudaStream_t>(stream), part_m,
+                   part_l, part_o, n, rows, world, rank, pb, epoch, wait_cycles,
+                   reinterpret_cast<__half *>(out_f16), flags & ECC_DECODE_UNROTATE_OUT) != cudaSuccess)
+        return ECC_ERR_LAUNCH;
     return launch_status();
 }
