@@ -306,105 +306,124 @@ lse_merge_records_kernel(const float *__restrict__ rec, int n, int64_t stride, _
 // lse_merge_record_kernel -> all-gather -> lse_merge_records_kernel.
 //
 // Every rank owns an exchange buffer that all ranks can store to (a CUDA IPC
-// mapping on each peer): records float [2][W][rows][kRec], then epoch flags
-// uint32 [2][W][grid].  Call e (epoch e >= 1, the same sequence on every
-// rank) uses half p = e & 1.  CTA b of rank s merges its split partials of
-// rows b, b + grid, ... into records, stores them into slot [p][s][row] of
-// every rank's buffer, and then sets flag [p][s][b] = e in every buffer
-// (release, system scope, after a system-scope fence).  It then waits until
-// flag [p][q][b] = e in its own buffer for every rank q -- the same CTA index
-// of every rank, which stored exactly the same rows -- and merges the W
-// records of each of its rows.  A CTA depends only on the same-index CTAs of
-// the other GPUs, and every CTA of the grid can be resident at once (the grid
-// is capped by the kernel's occupancy times the SM count).  The kernel is a
-// programmatic dependent of the one before it (its launch overlaps that
-// kernel's tail; its CTAs start work after griddepcontrol.wait) and never
-// lets a dependent of its own start early, so once the previous kernel has
-// ended nothing else holds the SMs and no CTA waits for one that cannot run.
-// Half p is reused two calls later: a rank can only
-// start call e + 2 after every rank's records of call e + 1 arrived, which
-// each rank stores after finishing its merge of call e.  The wait is bounded;
-// a CTA that gives up raises g_exchange_error (ecc_device_status reports 4)
-// and writes nothing.
+// mapping on each peer): records [2][W][rows][kRec] of 64-bit words, each
+// word = (epoch << 32) | bits of one float of the record.  Call e (epoch
+// e >= 1, the same sequence on every rank) uses half p = e & 1.  The CTA of
+// row r on rank s merges its split partials into the row's record and
+// stores it into slot [p][s][r] of every rank's buffer with single 64-bit
+// stores; it then reads slot [p][q][r] of its own buffer for every rank q,
+// polling each word until its tag is e (a word is written by one store, so a
+// word with the right tag carries that call's value: no fence and no
+// separate flag), and merges the W records with the arithmetic of
+// lse_combine.  A CTA depends only on the CTAs of the same row on other GPUs,
+// and every CTA of the grid can be resident at once (the grid is capped by
+// the kernel's occupancy times the SM count; a CTA takes rows r = b,
+// b + grid, ...).  The kernel is a programmatic dependent of the one before
+// it (its launch overlaps that kernel's tail; its CTAs start work after
+// griddepcontrol.wait) and never lets a dependent of its own start early, so
+// once the previous kernel has ended nothing else holds the SMs and no CTA
+// waits for one that cannot run.  Half p is reused two calls later: a rank
+// can only start call e + 2 after every rank's records of call e + 1
+// arrived, which each rank stores after its call-e kernel has ended.  The
+// wait is bounded; a CTA that gives up raises g_exchange_error
+// (ecc_device_status reports 4) and its rows' output is not valid.
 // ---------------------------------------------------------------------------
 constexpr int kExchMaxRanks = ECC_EXCHANGE_MAX_RANKS;
 constexpr int kExchMaxGrid = 1024;
 struct PeerBufs {
-    float *base[kExchMaxRanks];
+    unsigned long long *base[kExchMaxRanks];
 };
 __device__ int g_exchange_error;
 
-__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
-// Records written by other GPUs: loads that skip L1.
-struct PeerRecordSrc {
-    const float *rec;
-    int64_t row, stride;
-    __device__ const float *at(int i) const { return rec + i * stride + row * kRec; }
-    __device__ float m(int i) const { return __ldcg(at(i)); }
-    __device__ float l(int i) const { return __ldcg(at(i) + 1); }
-    __device__ float o(int i, int d) const { return __ldcg(at(i) + 2 + d); }
-};
+__device__ __forceinline__ unsigned long long tag(float v, uint32_t epoch) {
+    return ((unsigned long long)epoch << 32) | __float_as_uint(v);
+}
+// Poll one word until it carries `epoch` or the deadline passes (then the
+// device flag is raised and *ok cleared); returns its float.
+__device__ __forceinline__ float await_word(const unsigned long long *p, unsigned long long w, uint32_t epoch,
+                                            long long t0, long long wait_cycles, bool *ok) {
+    while ((uint32_t)(w >> 32) != epoch) {
+        if (clock64() - t0 > wait_cycles) {
+            atomicExch(&g_exchange_error, 4);
+            *ok = false;
+            break;
+        }
+        w = ld_relaxed_sys(p);
+    }
+    return __uint_as_float((uint32_t)w);
+}
 
 __global__ void __launch_bounds__(kD)
 lse_exchange_kernel(const float *__restrict__ pm, const float *__restrict__ pl, const float *__restrict__ po, int n,
                     int64_t rows, int W, int rank, PeerBufs peers, uint32_t epoch, long long wait_cycles,
                     __half *__restrict__ out, int flags) {
     __shared__ float sh[kD];
-    __shared__ int s_ok;
+    __shared__ float s_m[kExchMaxRanks], s_l[kExchMaxRanks];
     const int d = threadIdx.x;
-    const int grid = gridDim.x, b = blockIdx.x;
     const int64_t half = epoch & 1u;
-    const int64_t rec_floats = 2 * (int64_t)W * rows * kRec;
     pdl_wait();  // the partials of the kernel before
     // 1. this rank's record of each row, stored into every rank's buffer
-    for (int64_t r = b; r < rows; r += grid) {
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
         float M, L, O;
         lse_combine(n, d, SplitSrc{pm, pl, po, r, n}, M, L, O);
         for (int q = 0; q < W; ++q) {
-            float *dst = peers.base[q] + ((half * W + rank) * rows + r) * kRec;
+            unsigned long long *dst = peers.base[q] + ((half * W + rank) * rows + r) * kRec;
             if (d == 0) {
-                dst[0] = M;
-                dst[1] = L;
+                st_relaxed_sys(dst, tag(M, epoch));
+                st_relaxed_sys(dst + 1, tag(L, epoch));
             }
-            dst[2 + d] = O;
+            st_relaxed_sys(dst + 2 + d, tag(O, epoch));
         }
     }
-    __syncthreads();  // the CTA's record stores precede the flag threads' fences
-    if (d < W) {
-        uint32_t *fl = reinterpret_cast<uint32_t *>(peers.base[d] + rec_floats) + (half * W + rank) * grid + b;
-        __threadfence_system();
-        st_release_sys(fl, epoch);
-    }
-    // 2. the same CTA of every rank (bounded wait)
-    if (d == 0) s_ok = 1;
-    __syncthreads();
-    if (d < W) {
-        const uint32_t *fl =
-            reinterpret_cast<const uint32_t *>(peers.base[rank] + rec_floats) + (half * W + d) * grid + b;
-        const long long t0 = clock64();
-        while (ld_acquire_sys(fl) != epoch) {
-            if (clock64() - t0 > wait_cycles) {
-                atomicExch(&g_exchange_error, 4);
-                s_ok = 0;
-                break;
-            }
+    // 2. every rank's record of each row: the words of all ranks are loaded
+    // together, then those not yet carrying this epoch are polled
+    const unsigned long long *mine = peers.base[rank] + half * W * rows * kRec;
+    const long long t0 = clock64();
+    bool ok = true;
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        unsigned long long w[kExchMaxRanks];
+        float ov[kExchMaxRanks];
+#pragma unroll
+        for (int q = 0; q < kExchMaxRanks; ++q)
+            if (q < W) w[q] = ld_relaxed_sys(mine + ((int64_t)q * rows + r) * kRec + 2 + d);
+        if (d < 2 * W) {  // threads 0..W-1 fetch m of rank d, W..2W-1 l of rank d - W
+            const int q = d < W ? d : d - W;
+            const unsigned long long *p = mine + ((int64_t)q * rows + r) * kRec + (d < W ? 0 : 1);
+            const float v = await_word(p, ld_relaxed_sys(p), epoch, t0, wait_cycles, &ok);
+            (d < W ? s_m : s_l)[q] = v;
         }
-        __threadfence_system();
-    }
-    __syncthreads();  // the acquires precede every thread's record loads
-    if (!s_ok) return;  // block-uniform
-    // 3. merge the W records of each row
-    const float *mine = peers.base[rank] + half * W * rows * kRec;
-    for (int64_t r = b; r < rows; r += grid) {
-        float M, L, O;
-        lse_combine(W, d, PeerRecordSrc{mine, r, rows * kRec}, M, L, O);
+#pragma unroll
+        for (int q = 0; q < kExchMaxRanks; ++q)
+            if (q < W) ov[q] = await_word(mine + ((int64_t)q * rows + r) * kRec + 2 + d, w[q], epoch, t0,
+                                          wait_cycles, &ok);
+        __syncthreads();
+        // the single-batch arithmetic of lse_combine over the W records
+        float M = -INFINITY, L = 0.0f, O = 0.0f, bm = -INFINITY;
+        for (int j = 0; j < W; ++j)
+            if (s_l[j] > 0.0f) bm = fmaxf(bm, s_m[j]);
+        if (bm != M) {
+            L *= 0.0f;
+            O *= 0.0f;
+            M = bm;
+        }
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int j = 0; j < kExchMaxRanks; ++j)
+                if (j < W && s_l[j] > 0.0f) {
+                    const float e = __expf(s_m[j] - M);
+                    L = fmaf(s_l[j], e, L);
+                    O = fmaf(ov[j], e, O);
+                }
+        }
+        __syncthreads();  // s_m, s_l are refilled for the next row
         write_out(L, O, out, r, d, flags, sh);
     }
 }
@@ -725,7 +744,7 @@ extern "C" int ecc_exchange_grid(int64_t rows) {
 
 extern "C" size_t ecc_exchange_buffer_bytes(int64_t rows, int world) {
     if (rows <= 0 || world < 1 || world > kExchMaxRanks) return 0;
-    return (size_t)2 * world * rows * kRec * sizeof(float) + (size_t)2 * world * kExchMaxGrid * sizeof(uint32_t);
+    return (size_t)2 * world * rows * kRec * sizeof(unsigned long long);
 }
 
 // The exchange buffer: a whole cudaMalloc allocation (so that its IPC handle
@@ -779,7 +798,7 @@ extern "C" int ecc_lse_exchange_merge(const float *part_m, const float *part_l, 
     for (int q = 0; q < world; ++q) {
         if (!peer_buffers[q]) return ECC_ERR_NULL;
         if ((uintptr_t)peer_buffers[q] % 16) return ECC_ERR_ALIGN;
-        pb.base[q] = reinterpret_cast<float *>(peer_buffers[q]);
+        pb.base[q] = reinterpret_cast<unsigned long long *>(peer_buffers[q]);
     }
     const int grid = ecc_exchange_grid(rows);
     // a programmatic dependent of the previous kernel; it never triggers its
