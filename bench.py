@@ -792,7 +792,7 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=CTX)
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-compress", action="store_true")
-    ap.add_argument("--exchange", default="nccl", choices=["nccl", "p2p"],
+    ap.add_argument("--exchange", default="p2p", choices=["nccl", "p2p"],
                     help="N > 1: how the ranks' records are combined (NCCL all-gather, or one kernel over "
                          "peer memory)")
     ap.add_argument("--block-bytes", type=int, default=BLOCK, choices=[BLOCK, 96],
