@@ -13,9 +13,12 @@ no L2 flush is needed between steps.
 Also measured in the same run: compress throughput on the compress benchmark
 (8 KV heads x 131072 tokens, K and V, heavy-tailed fp16).
 
-N > 1 GPUs (torchrun): sequence-chunk sharding, weak scaling -- every rank
-holds its own 65536-token chunk of a context N x 65536 tokens long, computes
-split partials, all-gathers them over NCCL and merges them (LSE combine).
+N > 1 GPUs (torchrun): the same job split over the ranks (strong scaling):
+by kv head by default (rank r holds kv heads [8r/N, 8(r+1)/N) of every
+sequence; one NCCL all-gather of the fp16 outputs per step), or by sequence
+chunk with ``--shard seq`` (LSE combine of the ranks' partial records over
+peer memory or NCCL).  Rank 0 checks the final step's sharded output against
+a one-GPU decode of the same pools.
 
 ``--impl reference`` times the reference algorithm's CPU implementation (the
 oracle port in oracle/, all host threads) on a bounded sample of the same
@@ -168,6 +171,9 @@ def compress_bench(ops, workloads, dev, stream, K, peak, peak_kind):
                         "channels -> 128-B blocks",
             "tok_s": HKV * COMPRESS_TOKENS / (c_avg / 1e3), "vectors_per_s": n_vec / (c_avg / 1e3),
             "ms_per_pass": c_avg, "gbs": c_gbs,
+            # input vectors and the blocks the kernel wrote for them, for the
+            # oracle parity check of the CPU leg (removed before printing)
+            "_sample": (ck[0, 0, :32768].cpu().numpy(), cpool_k[0, 0, :32768].cpu().numpy()),
             "roofline": {"bound": "hbm", "achieved": c_gbs, "peak": peak, "unit": "GB/s",
                          "frac": c_gbs / peak,
                          "traffic": COMPRESS_DRAM_BYTES_PER_VECTOR * HKV * COMPRESS_TOKENS,
@@ -183,6 +189,7 @@ def run_compress_only(args):
     torch.cuda.set_device(dev)
     peak, peak_kind = peaks()
     comp = compress_bench(ops, workloads, dev, torch.cuda.current_stream(dev), args.steps, peak, peak_kind)
+    comp.pop("_sample")
     print(json.dumps({"compress": comp}), flush=True)
 
 
@@ -284,10 +291,49 @@ def run_model_e2e(args):
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
+def _fill_decode_pools(ops, kpool, vpool, heads, tok_range, dev):
+    """Blocks of the decode workload for kv heads ``heads`` (global indices)
+    and tokens [t0, t1) of every sequence, written to kpool / vpool at local
+    head index and token t - t0.  Kv head h's tokens come from a generator
+    seeded by h alone, so every rank of a kv-head or sequence-chunk split holds
+    exactly its part of the one-GPU pools (rank 0 rebuilds those for the
+    sharded parity check)."""
+    import torch
+    t0, t1 = tok_range
+    chunk = 8192
+    for li, h in enumerate(heads):
+        gen = torch.Generator(device=dev).manual_seed(5000 + h)
+        for c0 in range(0, CTX, chunk):
+            xk = torch.randn((B, 1, chunk, D), generator=gen, device=dev).half()
+            xv = torch.randn((B, 1, chunk, D), generator=gen, device=dev).half()
+            a, b = max(c0, t0), min(c0 + chunk, t1)
+            if a < b:
+                ops.compress_into(xk[:, :, a - c0:b - c0], kpool[:, li:li + 1], pos=a - t0, rotate=True)
+                ops.compress_into(xv[:, :, a - c0:b - c0], vpool[:, li:li + 1], pos=a - t0, rotate=True)
+
+
+def _step_inputs(n_steps, dev):
+    """New K / V token per step for every (b, kv head), and the step's queries."""
+    import torch
+    import workloads
+    gen = torch.Generator(device=dev).manual_seed(777)
+    new_k = torch.randn((n_steps, B, HKV, 1, D), generator=gen, device=dev).half()
+    new_v = torch.randn((n_steps, B, HKV, 1, D), generator=gen, device=dev).half()
+    qs = torch.stack([workloads.make_queries(i, B, HQ, device=dev) for i in range(n_steps)])
+    return new_k, new_v, qs
+
+
 def run_ours(args):
+    """The decode benchmark (B8, Hq32/Hkv8, 65536-token context growing by one
+    token per step; append + fused decode per step).  One GPU: the whole job.
+    N GPUs (torchrun): the same job split over the ranks (strong scaling) --
+    by kv head (default: rank r holds kv heads [8r/N, 8(r+1)/N) of every
+    sequence, and the ranks' fp16 outputs are all-gathered) or by sequence
+    chunk (``--shard seq``: rank r holds tokens [rL/N, (r+1)L/N) of every row,
+    the last rank also the appended ones; LSE combine of the ranks'
+    records)."""
     import torch
     import custom_ecc_cuda as ops
-    import workloads
 
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
@@ -298,55 +344,64 @@ def run_ours(args):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
         pg = dist.group.WORLD
+    mode = "single" if world == 1 else args.shard
+    if mode == "kv" and HKV % world:
+        raise SystemExit(f"{world} ranks do not divide {HKV} kv heads")
     K, W = args.steps, args.warmup
-    cap = CTX + W + K + 2 * (K + W) + 8
-    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
-
-    # --- block pools filled by the compress kernel from seeded N(0,1) ---
     rb = args.block_bytes  # 128-byte blocks, or the 96-byte records of the option
-    kpool = torch.empty((B, HKV, cap, rb), dtype=torch.uint8, device=dev)
-    vpool = torch.empty_like(kpool)
-    chunk = 8192
-    for t0 in range(0, CTX, chunk):
-        for pool in (kpool, vpool):
-            x = torch.randn((B, HKV, chunk, D), generator=gen, device=dev).half()
-            ops.compress_into(x, pool, pos=t0, rotate=True)
-    torch.cuda.synchronize()
-
     n_steps = W + K
-    new_k = torch.randn((n_steps, B, HKV, 1, D), generator=gen, device=dev).half()
-    new_v = torch.randn((n_steps, B, HKV, 1, D), generator=gen, device=dev).half()
-    qs = torch.stack([workloads.make_queries(i, B, HQ, device=dev) for i in range(n_steps)])
+    growth = n_steps + K + 8  # timed steps, then the e2e steps
+    last = rank == world - 1
+    if mode == "kv":
+        heads = list(range(rank * HKV // world, (rank + 1) * HKV // world))
+        toks = (0, CTX)
+    elif mode == "seq":
+        heads = list(range(HKV))
+        toks = (rank * CTX // world, (rank + 1) * CTX // world)
+    else:
+        heads, toks = list(range(HKV)), (0, CTX)
+    hkv_l, hq_l = len(heads), len(heads) * (HQ // HKV)
+    grows = mode != "seq" or last  # this rank appends the new tokens
+    cap = toks[1] - toks[0] + (growth if grows else 0)
+    kpool = torch.empty((B, hkv_l, cap, rb), dtype=torch.uint8, device=dev)
+    vpool = torch.empty_like(kpool)
+    _fill_decode_pools(ops, kpool, vpool, heads, toks, dev)
+    new_k, new_v, qs = _step_inputs(n_steps + K, dev)
+    h0, q0 = heads[0], heads[0] * (HQ // HKV)
+    if mode == "kv":
+        new_k, new_v = new_k[:, :, h0:h0 + hkv_l].contiguous(), new_v[:, :, h0:h0 + hkv_l].contiguous()
+        qs = qs[:, :, q0:q0 + hq_l].contiguous()
     out = torch.empty((B, HQ, 1, D), dtype=torch.float16, device=dev)
-    # one rank: the library's default split count (the TMA kernel's balanced
-    # partition for each step's length); sharded: a fixed count that covers
-    # the partition of every length the run reaches
-    splits = 0
-    nspl = max(ops.default_splits(B, HKV, s) for s in (CTX, CTX + (cap - CTX) // 2, cap)) + 1
     stream = torch.cuda.current_stream(dev)
-
+    torch.cuda.synchronize()
+    shard, nspl = None, 0
     if world > 1:
-        import torch.distributed as dist
         from custom_kv.sharding import ShardedDecode
-        # two-level combine: each rank merges its splits into one record
-        # {m, l, o[128]} per (b, q head); one all-gather of the records
-        shard = ShardedDecode("seq", pg, exchange=args.exchange)
+        shard = ShardedDecode(mode, pg, exchange=args.exchange)
+        if mode == "seq":
+            lens = [toks[1] - toks[0] + (g if grows else 0) for g in (0, growth)]
+            nspl = max(ops.default_splits(B, HKV, s) for s in lens) + 1
 
-    def step(i, seq_len, events=None):
-        # append the new token (sharded run: the last rank owns the newest chunk)
-        if world == 1 or rank == world - 1:
-            ops.compress_pair_into(new_k[i], new_v[i], kpool, vpool, pos=seq_len - 1, rotate=True)
+    def local_len(seq_len):
+        return seq_len - toks[0] if grows else toks[1] - toks[0]
+
+    def step(i, seq_len, q=None, nk=None, nv=None, dst=None, events=None):
+        """Append step i's token (at global position seq_len - 1), then
+        decode at context length seq_len; the output lands in dst."""
+        q = qs[i] if q is None else q
+        nk = new_k[i] if nk is None else nk
+        nv = new_v[i] if nv is None else nv
+        dst = out if dst is None else dst
+        if grows:
+            ops.compress_pair_into(nk, nv, kpool, vpool, pos=local_len(seq_len) - 1, rotate=True)
         if events is not None:
             events[0].record(stream)
         if world == 1:
-            ops.decode_attention(qs[i], kpool, vpool, seq_len=seq_len, rotate_q=True, unrotate_out=True,
-                                 num_splits=splits, out=out)
+            ops.decode_attention(q, kpool, vpool, seq_len=seq_len, rotate_q=True, unrotate_out=True, out=dst)
             if events is not None:
                 events[1].record(stream)
         else:
-            # ranks before the last hold a full, fixed chunk; the last rank's grows
-            local_len = seq_len if rank == world - 1 else CTX
-            shard.step(qs[i], kpool, vpool, local_len, num_splits=nspl, out=out,
+            shard.step(q, kpool, vpool, local_len(seq_len), num_splits=nspl, out=dst,
                        mark=events[1] if events is not None else None)
 
     def barrier():
@@ -354,6 +409,14 @@ def run_ours(args):
             import torch.distributed as dist
             dist.barrier()
         torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        import torch.distributed as dist
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
 
     try:
         gpu_id = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
@@ -368,7 +431,7 @@ def run_ours(args):
     barrier()
 
     # ---- timed region: K device-resident steps ----
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    ev = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(K)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     seq0 = seq
     barrier()
@@ -376,148 +439,217 @@ def run_ours(args):
     start.record(stream)
     for i in range(K):
         seq += 1
-        step(W + i, seq, ev[i])
+        step(W + i, seq, events=ev[i])
+        ev[i][2].record(stream)
     stop.record(stream)
     barrier()
     clk.mark_stop()
     clk.__exit__(None, None, None)
-    total_ms = start.elapsed_time(stop)
-    dec_ms = [a.elapsed_time(b) for a, b in ev]
-    if world > 1:
-        t = torch.tensor([total_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = t.item()
+    total_ms = max_over_ranks(start.elapsed_time(stop))
+    dec_ms = sum(a.elapsed_time(b) for a, b, _ in ev) / K
+    xch_ms = sum(b.elapsed_time(c) for _, b, c in ev) / K if world > 1 else 0.0
+    final = out.clone()
+    final_seq = seq
 
     mean_ctx = seq0 + (K + 1) / 2.0
-    # K + V blocks read per step: the last rank's chunk grows, the others' are CTX
-    rank_ctx = mean_ctx if (world == 1 or rank == world - 1) else float(CTX)
-    bytes_per_step = B * HKV * rank_ctx * 2 * rb
-    job_bytes_per_step = B * HKV * ((world - 1) * CTX + mean_ctx) * 2 * rb
+    job_bytes_per_step = B * HKV * mean_ctx * 2 * rb
+    rank_units = B * hkv_l * ((mean_ctx - toks[0]) if grows else float(toks[1] - toks[0]))
     value = job_bytes_per_step * K / (total_ms / 1e3) / 1e9
     tok_s = B * K / (total_ms / 1e3)
-    dec_avg_ms = sum(dec_ms) / len(dec_ms)
-    achieved = bytes_per_step / (dec_avg_ms / 1e3) / 1e9
+    achieved = rank_units * 2 * rb / (dec_ms / 1e3) / 1e9
     peak, peak_kind = peaks()
     clocks = clk.summary()
 
+    # ---- sharded output against the one-GPU decode of the same rows ----
+    shard_parity = None
+    if world > 1:
+        if rank == 0:
+            fk = torch.empty((B, HKV, CTX + growth, rb), dtype=torch.uint8, device=dev)
+            fv = torch.empty_like(fk)
+            _fill_decode_pools(ops, fk, fv, list(range(HKV)), (0, CTX), dev)
+            fnk, fnv, fqs = _step_inputs(n_steps + K, dev)
+            for i in range(n_steps):
+                ops.compress_pair_into(fnk[i], fnv[i], fk, fv, pos=CTX + i, rotate=True)
+            one = ops.decode_attention(fqs[n_steps - 1], fk, fv, seq_len=final_seq, rotate_q=True,
+                                       unrotate_out=True)
+            d = (one.float() - final.float()).abs()
+            ulp = (torch.nextafter(one.abs(), torch.full_like(one, float("inf"))) - one.abs()).float()
+            shard_parity = {"rows": B * HQ, "max_abs_vs_one_gpu": d.max().item(),
+                            "over_1e-3_plus_ulp": int((d > 1e-3 + ulp).sum().item()),
+                            "note": "final timed step's gathered output vs the one-GPU decode of the same pools "
+                                    "(different partition: rounding-level differences)"}
+            del fk, fv, fnk, fnv, fqs, one
+        barrier()
+
     # ---- e2e: host buffers in, result out, every step (reference-facing API) ----
-    e2e = None
-    if world == 1:
-        hq = torch.empty((K, B, HQ, 1, D), dtype=torch.float16).pin_memory()
-        hk = torch.empty((K, B, HKV, 1, D), dtype=torch.float16).pin_memory()
-        hv = torch.empty_like(hk).pin_memory()
-        hq.copy_(qs[W:].cpu())
-        hk.copy_(new_k[W:].cpu())
-        hv.copy_(new_v[W:].cpu())
-        hout = torch.empty((K, B, HQ, 1, D), dtype=torch.float16).pin_memory()
-        # Pipelined like a serving loop: a copy stream brings step i+1's
-        # inputs in and step i's output out while step i computes; device
-        # inputs and outputs are double-buffered.  Every step's copies are
-        # inside the timed region, which runs from the first input copy to
-        # the last output copy (both on the copy stream).
-        cs = torch.cuda.Stream(dev)
-        dq = [torch.empty((B, HQ, 1, D), dtype=torch.float16, device=dev) for _ in range(2)]
-        dk = [torch.empty((B, HKV, 1, D), dtype=torch.float16, device=dev) for _ in range(2)]
-        dv = [torch.empty((B, HKV, 1, D), dtype=torch.float16, device=dev) for _ in range(2)]
-        dout = [torch.empty((B, HQ, 1, D), dtype=torch.float16, device=dev) for _ in range(2)]
-        ev_in = [torch.cuda.Event() for _ in range(K)]
-        ev_done = [torch.cuda.Event() for _ in range(K)]
-        ev_out = [torch.cuda.Event() for _ in range(K)]
+    hq = torch.empty((K, B, hq_l if mode == "kv" else HQ, 1, D), dtype=torch.float16).pin_memory()
+    hk = torch.empty((K, B, new_k.shape[2], 1, D), dtype=torch.float16).pin_memory()
+    hv = torch.empty_like(hk).pin_memory()
+    hq.copy_(qs[n_steps:].cpu())
+    hk.copy_(new_k[n_steps:].cpu())
+    hv.copy_(new_v[n_steps:].cpu())
+    hout = torch.empty((K, B, HQ, 1, D), dtype=torch.float16).pin_memory()
+    # Pipelined like a serving loop: a copy stream brings step i+1's inputs
+    # in and step i's output out while step i computes; device inputs and
+    # outputs are double-buffered.  Every step's copies are inside the timed
+    # region, which runs from the first input copy to the last output copy
+    # (both on the copy stream).
+    cs = torch.cuda.Stream(dev)
+    dq = [torch.empty(hq.shape[1:], dtype=torch.float16, device=dev) for _ in range(2)]
+    dk = [torch.empty(hk.shape[1:], dtype=torch.float16, device=dev) for _ in range(2)]
+    dv = [torch.empty(hk.shape[1:], dtype=torch.float16, device=dev) for _ in range(2)]
+    dout = [torch.empty((B, HQ, 1, D), dtype=torch.float16, device=dev) for _ in range(2)]
+    ev_in = [torch.cuda.Event() for _ in range(K)]
+    ev_done = [torch.cuda.Event() for _ in range(K)]
+    ev_out = [torch.cuda.Event() for _ in range(K)]
 
-        def h2d(i):
-            b = i % 2
-            with torch.cuda.stream(cs):
-                if i >= 2:
-                    cs.wait_event(ev_done[i - 2])  # step i-2 has read buffer b
-                dq[b].copy_(hq[i], non_blocking=True)
-                dk[b].copy_(hk[i], non_blocking=True)
-                dv[b].copy_(hv[i], non_blocking=True)
-                ev_in[i].record(cs)
-
-        seq_e = seq
-        barrier()
-        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s2.record(cs)
-        h2d(0)
-        for i in range(K):
-            b = i % 2
-            if i + 1 < K:
-                h2d(i + 1)
-            seq_e += 1
-            stream.wait_event(ev_in[i])
+    def h2d(i):
+        b = i % 2
+        with torch.cuda.stream(cs):
             if i >= 2:
-                stream.wait_event(ev_out[i - 2])  # step i-2's output has left buffer b
-            ops.compress_pair_into(dk[b], dv[b], kpool, vpool, pos=seq_e - 1, rotate=True)
-            ops.decode_attention(dq[b], kpool, vpool, seq_len=seq_e, rotate_q=True, unrotate_out=True,
-                                 num_splits=splits, out=dout[b])
-            ev_done[i].record(stream)
-            with torch.cuda.stream(cs):
-                cs.wait_event(ev_done[i])
-                hout[i].copy_(dout[b], non_blocking=True)
-                ev_out[i].record(cs)
-        e2.record(cs)
-        barrier()
-        e2e_ms = s2.elapsed_time(e2)
-        mean_ctx_e = seq + (K + 1) / 2.0
-        e2e = {"value": B * HKV * mean_ctx_e * 2 * rb * K / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
-               "tok_s": B * K / (e2e_ms / 1e3), "ms_per_step": e2e_ms / K,
-               "h2d_bytes_per_step": (dq[0].numel() + dk[0].numel() + dv[0].numel()) * 2,
-               "d2h_bytes_per_step": dout[0].numel() * 2,
-               "pipelining": "copy stream overlaps step i+1's input and step i's output copies with step i"}
+                cs.wait_event(ev_done[i - 2])  # step i-2 has read buffer b
+            dq[b].copy_(hq[i], non_blocking=True)
+            dk[b].copy_(hk[i], non_blocking=True)
+            dv[b].copy_(hv[i], non_blocking=True)
+            ev_in[i].record(cs)
+
+    seq_e = seq
+    barrier()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record(cs)
+    h2d(0)
+    for i in range(K):
+        b = i % 2
+        if i + 1 < K:
+            h2d(i + 1)
+        seq_e += 1
+        stream.wait_event(ev_in[i])
+        if i >= 2:
+            stream.wait_event(ev_out[i - 2])  # step i-2's output has left buffer b
+        step(None, seq_e, q=dq[b], nk=dk[b], nv=dv[b], dst=dout[b])
+        ev_done[i].record(stream)
+        with torch.cuda.stream(cs):
+            cs.wait_event(ev_done[i])
+            hout[i].copy_(dout[b], non_blocking=True)
+            ev_out[i].record(cs)
+    e2.record(cs)
+    barrier()
+    e2e_ms = max_over_ranks(s2.elapsed_time(e2))
+    mean_ctx_e = seq + (K + 1) / 2.0
+    e2e = {"value": B * HKV * mean_ctx_e * 2 * rb * K / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
+           "tok_s": B * K / (e2e_ms / 1e3), "ms_per_step": e2e_ms / K,
+           "h2d_bytes_per_step": (dq[0].numel() + dk[0].numel() + dv[0].numel()) * 2,
+           "d2h_bytes_per_step": dout[0].numel() * 2,
+           "pipelining": "copy stream overlaps step i+1's input and step i's output copies with step i"
+                         + ("; per rank: its own query heads / kv heads in, the whole output out"
+                            if world > 1 else "")}
 
     # ---- compress throughput (8 KV heads x 131072 tokens, K and V) ----
     comp = None
     if world == 1 and not args.skip_compress:
+        pools_host = None
+        if rank == 0 and not args.skip_cpu:
+            # the decode parity check of the CPU leg reads two batch rows of
+            # the final timed step's pools (blocks beyond that length unused)
+            pools_host = (kpool[[0, B - 1], :, :final_seq].cpu().numpy(),
+                          vpool[[0, B - 1], :, :final_seq].cpu().numpy(),
+                          qs[n_steps - 1][[0, B - 1]].cpu().numpy(), final[[0, B - 1]].float().cpu().numpy())
         del kpool, vpool
         torch.cuda.empty_cache()
-        comp = compress_bench(ops, workloads, dev, stream, K, peak, peak_kind)
+        comp = compress_bench(ops, __import__("workloads"), dev, stream, K, peak, peak_kind)
+    sample = comp.pop("_sample") if comp else None
 
-    cpu = None
+    # ---- CPU leg (rank 0, one GPU): timed oracle baseline and the oracle parity check ----
+    cpu, parity = None, None
     if rank == 0 and world == 1 and not args.skip_cpu:
         cpu = cpu_baseline(args.cpu_tokens)
+        if sample is not None:
+            parity = cpu_parity(pools_host, final_seq, sample)
 
+    launches_per_step = {"single": 3, "kv": 3, "seq": (1 if args.exchange == "p2p" else 2) + 1 + (1 if last else 0)}
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": K, "warmup": W,
-            "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "fp32", "data": "synthetic",
-            "config": {"workload": f"decode step: B{B} Hq{HQ}/Hkv{HKV} D{D}, {CTX}-token compressed context "
-                                   f"per rank growing 1 token/step, append + fused decode",
-                       "batch": B, "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "context_per_rank": CTX,
-                       "parallelism": "seq-chunk" if world > 1 else "single",
-                       "num_splits": nspl if world > 1 else "default (balanced tile partition)",
-                       "l2": f"inputs {B * HKV * CTX * 2 * rb / 1e9:.2f} GB/rank > L2 (no flush needed)",
-                       "block_bytes": rb},
+            "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "fp16 MMA (split operands), fp32 accumulate", "data": "synthetic",
+            "config": decode_config(world, mode, rb),
             "decode_tok_s": tok_s, "pct_peak": value / world / peak,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
-                         "traffic": DECODE_DRAM_BYTES_PER_UNIT * B * HKV * rank_ctx if rb == BLOCK else None,
-                         "note": f"decode (split partials + merge) per step: {2 * rb} B per (token, kv head), "
-                                 f"{B * HKV} (b, kv head) rows x mean {rank_ctx:.0f} tokens; traffic from ncu "
-                                 f"(per launch of the decode kernel); peak {peak_kind}"},
-            "gpu_launches": K * (3 if world == 1 else
-                                 (2 if args.exchange == "p2p" else 3) + (1 if rank == world - 1 else 0)),
-            "clocks": clocks, "e2e": e2e, "compress": comp, "cpu_baseline": cpu,
+                         "traffic": DECODE_DRAM_BYTES_PER_UNIT * rank_units if rb == BLOCK else None,
+                         "note": f"rank 0's decode (split partials + merge) per step: {2 * rb} B per (token, kv "
+                                 f"head), {rank_units:.0f} units; traffic from ncu (per launch of the decode "
+                                 f"kernel); peak {peak_kind}"},
+            "rank0_ms": {"append_to_attention_end": dec_ms, "exchange": xch_ms},
+            "gpu_launches": K * launches_per_step[mode],
+            "clocks": clocks, "e2e": e2e, "compress": comp, "cpu_baseline": cpu, "parity": parity,
         }
         if world > 1:
-            line["exchange"] = {"p2p": "one kernel: records stored into every rank's buffer over NVLink "
-                                       "(CUDA IPC), epoch flags, merge",
-                                "nccl": "merge to records, NCCL all-gather, merge"}[args.exchange]
+            line["exchange"] = ("NCCL all-gather of the ranks' fp16 outputs" if mode == "kv" else
+                                {"p2p": "one kernel: records stored into every rank's buffer over NVLink "
+                                        "(CUDA IPC), epoch-tagged words, merge",
+                                 "nccl": "merge to records, NCCL all-gather, merge"}[args.exchange])
+            line["parity"] = shard_parity
         if comp:
             line["compress_tok_s"] = comp["tok_s"]
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
         torch.cuda.synchronize()
-        if args.exchange == "p2p":
-            if ops.device_status() != 0:  # a bounded wait in the exchange gave up: the numbers are void
-                raise RuntimeError(f"rank {rank}: peer exchange reported device status {ops.device_status()}")
+        if ops.device_status() != 0:  # a bounded wait gave up: the numbers are void
+            raise RuntimeError(f"rank {rank}: device status {ops.device_status()}")
+        if shard._peer is not None:
             shard._peer.close()
         dist.barrier()
         dist.destroy_process_group()
 
 
-LONG_B, LONG_CTX = 16, 131072
+def decode_config(world: int, mode: str, rb: int = BLOCK) -> dict:
+    """The benchmark's config object (both arms print the same one)."""
+    hkv_l = HKV // world if mode == "kv" else HKV
+    toks = CTX // world if mode == "seq" else CTX
+    rank_bytes = B * hkv_l * toks * 2 * rb
+    return {"workload": f"decode step: B{B} Hq{HQ}/Hkv{HKV} D{D}, {CTX}-token compressed context growing 1 "
+                        f"token/step, append + fused decode; the whole job on every N",
+            "batch": B, "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "context": CTX,
+            "parallelism": {"single": "single", "kv": f"kv-head x{world}", "seq": f"seq-chunk x{world}"}[mode],
+            "per_rank": f"{hkv_l} kv heads x {toks} tokens",
+            "l2": f"pools {rank_bytes / 1e9:.2f} GB per rank " + (
+                "> 126 MB L2 (no flush needed)" if rank_bytes > 126e6 else
+                "(not larger than the 126 MB L2 at this N: every step re-reads the pools)"),
+            "block_bytes": rb}
+
+
+def cpu_parity(pools_host, seq_len, comp_sample):
+    """Oracle checks of the benchmarked data (part of the CPU leg; the oracle
+    is the checker here, nothing is timed): the final timed decode step's
+    output for two batch rows (all 32 query heads) against the oracle's
+    decode of the same pools, and a sample of the compress benchmark's input
+    against the oracle's blocks (bit for bit) with the count of elements
+    within 1e-6 of a quantiser decision boundary."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import ecc_oracle
+    threads = len(os.sched_getaffinity(0))
+    kb, vb, q, got = pools_host
+    ref = ecc_oracle.decode(q, kb, vb, hkv=HKV, seq_len=seq_len, rotate_q=True, unrotate_out=True,
+                            threads=threads)
+    got = got.reshape(ref.shape)
+    err = np.abs(got - ref)
+    a = np.abs(ref.astype(np.float16))
+    half_ulp = 0.5 * (np.nextafter(a, np.float16(np.inf)) - a).astype(np.float32)
+    x16, blocks = comp_sample
+    oracle_blocks = ecc_oracle.compress(x16, rotate=True, threads=threads)
+    mism = int((oracle_blocks.reshape(-1, BLOCK) != blocks.reshape(-1, BLOCK)).any(axis=1).sum())
+    return {"decode": {"rows": f"batch rows 0 and {B - 1}, {HQ} q heads, final step ({seq_len} tokens)",
+                       "max_abs_err": float(err.max()), "elements": int(err.size),
+                       "over_plain_2e-3": int((err > 2e-3).sum()),
+                       "over_2e-3_plus_half_ulp": int((err > 2e-3 + half_ulp).sum())},
+            "compress": {"vectors": int(x16.shape[0]), "blocks_differing": mism,
+                         "elements_within_1e-6_of_a_boundary": ecc_oracle.count_ties(x16, rotate=True),
+                         "note": "vectors of the compress benchmark's K input; oracle = compress_cpu restated"}}
+
+
 LONG_B, LONG_CTX = 16, 131072
 
 
@@ -772,13 +904,14 @@ def run_reference(args):
     gbs = HKV * args.cpu_tokens * 2 * BLOCK * len(times) / total / 1e9
     line = {"impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / len(times),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-            "config": {"workload": f"decode step sample: 1 batch row x Hq{HQ}/Hkv{HKV} D{D} x {args.cpu_tokens} "
-                                   f"tokens of the {CTX}-token decode workload", "parallelism": "host threads"},
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic", "config": decode_config(world, "single" if world == 1 else args.shard),
             "decode_tok_s": 1.0 / (total / len(times)) * (args.cpu_tokens / CTX),
             "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
-                             "sample": f"oracle decode (C port of cpu_reference_decode) per step: 1 row x "
-                                       f"{args.cpu_tokens} tokens"},
+                             "sample": f"each step: oracle decode (C port of cpu_reference_decode) of 1 batch row "
+                                       f"x {HQ} q heads / {HKV} kv heads x {args.cpu_tokens} tokens of this "
+                                       f"workload, on {threads} host threads; GB/s per the same 256 B per "
+                                       f"(token, kv head)"},
             "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -792,9 +925,11 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=CTX)
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-compress", action="store_true")
+    ap.add_argument("--shard", default="kv", choices=["kv", "seq"],
+                    help="N > 1: split the decode job by kv head (default) or by sequence chunk")
     ap.add_argument("--exchange", default="p2p", choices=["nccl", "p2p"],
-                    help="N > 1: how the ranks' records are combined (NCCL all-gather, or one kernel over "
-                         "peer memory)")
+                    help="--shard seq: how the ranks' records are combined (NCCL all-gather, or one kernel "
+                         "over peer memory)")
     ap.add_argument("--block-bytes", type=int, default=BLOCK, choices=[BLOCK, 96],
                     help="record size of the decode pools: the 128-byte block (default, the reference's "
                          "format) or the 96-byte record without the pad sector")

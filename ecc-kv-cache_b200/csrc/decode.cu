@@ -10,9 +10,14 @@
 // evaluated as split-sequence (flash-decoding) partials: each CTA owns one
 // (b, kv head, split) and keeps its GQA query group resident; the merge
 // combines (m, l, o) of the splits.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <mutex>
+#include <unordered_map>
 
 #include "ecc_common.cuh"
 
@@ -25,7 +30,7 @@ int launch_decode_mma(const void *q, const void *kbp, const void *vbp, int64_t b
                       float scale_log2, int flags, cudaStream_t s);
 int launch_decode_tma(const void *q, const void *kb, const void *vb, int64_t bs_b, int64_t bs_h, float *pm,
                       float *pl, float *po, int B, int Hq, int Hkv, int64_t seq_len, int64_t chunk, int ns,
-                      float scale_log2, int flags, cudaStream_t s);
+                      float scale_log2, int flags, cudaStream_t s, const int *start_dev = nullptr);
 int tma_default_splits(int B, int Hkv, int64_t seq_len);
 int launch_decode_tma_dev(const void *q, const void *kb, const void *vb, int64_t bs_b, int64_t bs_h, float *pm,
                           float *pl, float *po, int B, int Hq, int Hkv, int64_t max_len, const int *seq_len_dev,
@@ -444,6 +449,35 @@ using namespace ecc;
 
 static inline bool aligned(const void *p, size_t a) { return ((uintptr_t)p % a) == 0; }
 
+// Driver entry points looked up through the runtime (no link against
+// libcuda): the current context, and the size of the allocation that
+// contains an address.
+template <class Fn>
+static Fn driver_fn(const char *name) {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint(name, &fn, cudaEnableDefault, &qr) != cudaSuccess ||
+        qr != cudaDriverEntryPointSuccess)
+        return nullptr;
+    return reinterpret_cast<Fn>(fn);
+}
+
+static CUcontext current_context() {
+    static const auto fn = driver_fn<PFN_cuCtxGetCurrent_v4000>("cuCtxGetCurrent");
+    CUcontext c = nullptr;
+    if (!fn || fn(&c) != CUDA_SUCCESS) return nullptr;
+    return c;
+}
+
+static size_t allocation_bytes(const void *p) {
+    static const auto fn = driver_fn<PFN_cuMemGetAddressRange_v3020>("cuMemGetAddressRange");
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (!fn || fn(&base, &size, reinterpret_cast<CUdeviceptr>(p)) != CUDA_SUCCESS) return 0;
+    // bytes from p to the end of its allocation
+    return size - (size_t)(reinterpret_cast<CUdeviceptr>(p) - base);
+}
+
 static inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 extern "C" int ecc_decode_default_splits(int B, int Hkv, int64_t seq_len) {
@@ -610,6 +644,42 @@ extern "C" int ecc_decode(const void *q_f16, const void *k_blocks, const void *v
 }
 
 // ---------------------------------------------------------------------------
+// Decode of left-padded batches: sequence b attends to tokens
+// [start_dev[b], seq_len) only.  The tokens before start_dev[b] are padding
+// that a batched prompt put in front of the shorter sequences; they are in
+// the pools (the prefill compressed them) but the attention mask excludes
+// them.  TMA-fed kernel only (GQA groups up to 8, pools a tensor map can
+// describe), with its default partition; the workspace is the one ecc_decode
+// needs with num_splits = 0.
+// ---------------------------------------------------------------------------
+extern "C" int ecc_decode_masked(const void *q_f16, const void *k_blocks, const void *v_blocks, int64_t bs_b,
+                                 int64_t bs_h, const int *start_dev, void *out_f16, void *workspace,
+                                 size_t workspace_bytes, int B, int Hq, int Hkv, int64_t seq_len, float sm_scale,
+                                 int flags, ecc_stream_t stream) {
+    int rc = check_decode_args(q_f16, k_blocks, v_blocks, B, Hq, Hkv, seq_len);
+    if (rc != ECC_OK) return rc;
+    if (!out_f16 || !start_dev) return ECC_ERR_NULL;
+    if (seq_len < 1 || Hq / Hkv > 8 || (flags & (ECC_DECODE_CUDA_CORES | ECC_DECODE_REGISTER_PATH)))
+        return ECC_ERR_SHAPE;
+    const size_t need = ecc_decode_workspace_size(B, Hq, Hkv, seq_len, 0);
+    if (!workspace || workspace_bytes < need) return ECC_ERR_WORKSPACE;
+    int64_t chunk = 0;
+    const int ns = effective_splits(B, Hkv, seq_len, 0, &chunk);
+    const size_t parts = (size_t)B * Hq * ns;
+    uintptr_t base = (reinterpret_cast<uintptr_t>(workspace) + 255) & ~(uintptr_t)255;
+    float *po = reinterpret_cast<float *>(base);
+    float *pm = po + parts * kD;
+    float *pl = pm + parts;
+    if (!(sm_scale > 0.0f)) sm_scale = 1.0f / std::sqrt((float)kD);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    rc = launch_decode_tma(q_f16, k_blocks, v_blocks, bs_b, bs_h, pm, pl, po, B, Hq, Hkv, seq_len, chunk, ns,
+                           sm_scale * kLog2e, flags & (ECC_DECODE_ROTATE_Q | ECC_DECODE_BLOCK96), s, start_dev);
+    if (rc > 0) return ECC_ERR_SHAPE;  // a pool layout the tensor-map kernel does not take
+    if (rc != ECC_OK) return rc;
+    return ecc_lse_merge(pm, pl, po, (int64_t)B * Hq, ns, out_f16, flags & ECC_DECODE_UNROTATE_OUT, stream);
+}
+
+// ---------------------------------------------------------------------------
 // Decode with the context length in device memory, for launches recorded once
 // in a CUDA graph and replayed while the context grows.
 // ---------------------------------------------------------------------------
@@ -677,23 +747,28 @@ extern "C" int ecc_decode_dev(const void *q_f16, const void *k_blocks, const voi
 // latency-critical path that cannot afford cudaMalloc's implicit
 // synchronisation.
 // ---------------------------------------------------------------------------
-#include <mutex>
-
 static __device__ __align__(256) unsigned char g_decode_scratch[ECC_DECODE_STATIC_SCRATCH_BYTES];
 
 static std::mutex g_scratch_mu;
 static void *g_scratch_addr[64];
+static CUcontext g_scratch_ctx[64];
 
 // Device address of g_decode_scratch on the current device (the host-side
-// name is only a stand-in for it), looked up once per device.
+// name is only a stand-in for it), looked up once per device and context: a
+// context that was destroyed and created again (cudaDeviceReset) loads the
+// module anew, so the cached address is dropped when the current context is
+// not the one it was taken in.
 static int static_scratch(void **out) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ECC_ERR_DEVICE;
+    if (cudaFree(nullptr) != cudaSuccess) return ECC_ERR_CUDA;  // makes the device's primary context current
+    const CUcontext ctx = current_context();
     std::lock_guard<std::mutex> lk(g_scratch_mu);
-    if (!g_scratch_addr[dev]) {
+    if (!g_scratch_addr[dev] || g_scratch_ctx[dev] != ctx) {
         void *p = nullptr;
         if (cudaGetSymbolAddress(&p, g_decode_scratch) != cudaSuccess || !p) return ECC_ERR_CUDA;
         g_scratch_addr[dev] = p;
+        g_scratch_ctx[dev] = ctx;
     }
     *out = g_scratch_addr[dev];
     return ECC_OK;
@@ -730,14 +805,24 @@ extern "C" int ecc_decode_static(const void *q_f16, const void *k_blocks, const 
 // ---------------------------------------------------------------------------
 // CTAs of one exchange call: one per row up to kExchMaxGrid, and never more
 // than can be resident at once on the device.
+static std::mutex g_exch_mu;
+static int g_exch_per_sm[64];
+
 extern "C" int ecc_exchange_grid(int64_t rows) {
     if (rows <= 0) return 0;
-    static int per_sm = 0;
-    if (!per_sm) {
-        int nb = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, lse_exchange_kernel, kD, 0) != cudaSuccess || nb < 1)
-            nb = 1;
-        per_sm = nb;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
+    int per_sm;
+    {
+        std::lock_guard<std::mutex> lk(g_exch_mu);
+        if (!g_exch_per_sm[dev]) {
+            int nb = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, lse_exchange_kernel, kD, 0) != cudaSuccess ||
+                nb < 1)
+                nb = 1;
+            g_exch_per_sm[dev] = nb;
+        }
+        per_sm = g_exch_per_sm[dev];
     }
     return (int)std::min<int64_t>({rows, (int64_t)kExchMaxGrid, (int64_t)per_sm * sm_count()});
 }
@@ -751,6 +836,28 @@ extern "C" size_t ecc_exchange_buffer_bytes(int64_t rows, int world) {
 // maps exactly it), zero-filled; the handle travels to the other ranks, which
 // map it on their own device with peer access enabled lazily.
 static_assert(sizeof(cudaIpcMemHandle_t) == ECC_IPC_HANDLE_BYTES, "IPC handle size");
+
+// Bytes of every exchange buffer this process allocated or mapped, by the
+// address it uses for it: ecc_lse_exchange_merge checks each call's rows and
+// world against them, so that no call stores past the end of a buffer on
+// another GPU.  A mapped peer buffer's size is the size of the allocation
+// behind the IPC handle (cuMemGetAddressRange).
+static std::mutex g_bufreg_mu;
+static std::unordered_map<const void *, size_t> g_bufreg;
+
+static void bufreg_put(const void *p, size_t bytes) {
+    std::lock_guard<std::mutex> lk(g_bufreg_mu);
+    g_bufreg[p] = bytes;
+}
+static void bufreg_drop(const void *p) {
+    std::lock_guard<std::mutex> lk(g_bufreg_mu);
+    g_bufreg.erase(p);
+}
+static size_t bufreg_get(const void *p) {
+    std::lock_guard<std::mutex> lk(g_bufreg_mu);
+    const auto it = g_bufreg.find(p);
+    return it == g_bufreg.end() ? 0 : it->second;
+}
 
 extern "C" int ecc_exchange_alloc(int64_t rows, int world, void **buffer, void *ipc_handle) {
     const size_t bytes = ecc_exchange_buffer_bytes(rows, world);
@@ -766,6 +873,7 @@ extern "C" int ecc_exchange_alloc(int64_t rows, int world, void **buffer, void *
     }
     std::memcpy(ipc_handle, &h, sizeof(h));
     *buffer = p;
+    bufreg_put(p, bytes);
     return ECC_OK;
 }
 
@@ -773,17 +881,27 @@ extern "C" int ecc_exchange_open(const void *ipc_handle, void **peer_buffer) {
     if (!ipc_handle || !peer_buffer) return ECC_ERR_NULL;
     cudaIpcMemHandle_t h;
     std::memcpy(&h, ipc_handle, sizeof(h));
-    return cudaIpcOpenMemHandle(peer_buffer, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? ECC_OK
-                                                                                                 : ECC_ERR_CUDA;
+    void *p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return ECC_ERR_CUDA;
+    const size_t bytes = allocation_bytes(p);
+    if (!bytes) {
+        cudaIpcCloseMemHandle(p);
+        return ECC_ERR_CUDA;
+    }
+    bufreg_put(p, bytes);
+    *peer_buffer = p;
+    return ECC_OK;
 }
 
 extern "C" int ecc_exchange_close(void *peer_buffer) {
     if (!peer_buffer) return ECC_ERR_NULL;
+    bufreg_drop(peer_buffer);
     return cudaIpcCloseMemHandle(peer_buffer) == cudaSuccess ? ECC_OK : ECC_ERR_CUDA;
 }
 
 extern "C" int ecc_exchange_free(void *buffer) {
     if (!buffer) return ECC_ERR_NULL;
+    bufreg_drop(buffer);
     return cudaFree(buffer) == cudaSuccess ? ECC_OK : ECC_ERR_CUDA;
 }
 
@@ -795,9 +913,15 @@ extern "C" int ecc_lse_exchange_merge(const float *part_m, const float *part_l, 
         return ECC_ERR_SHAPE;
     if (!part_m || !part_l || !part_o || !peer_buffers || !out_f16) return ECC_ERR_NULL;
     PeerBufs pb{};
+    const size_t need = ecc_exchange_buffer_bytes(rows, world);
     for (int q = 0; q < world; ++q) {
         if (!peer_buffers[q]) return ECC_ERR_NULL;
         if ((uintptr_t)peer_buffers[q] % 16) return ECC_ERR_ALIGN;
+        // every buffer must be one this process allocated or mapped, and large
+        // enough for this call's rows and world (the stores would otherwise
+        // land past its end, in another GPU's memory)
+        const size_t have = bufreg_get(peer_buffers[q]);
+        if (have == 0 || have < need) return ECC_ERR_SHAPE;
         pb.base[q] = reinterpret_cast<unsigned long long *>(peer_buffers[q]);
     }
     const int grid = ecc_exchange_grid(rows);

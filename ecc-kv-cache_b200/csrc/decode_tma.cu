@@ -230,8 +230,8 @@ struct Lane {
 
     // log2-scaled scores of one 16-token sub-tile (K codes at kcb, syndrome +
     // metadata at ksb): s2[e] token g, s2[2+e] token g+8, head 2c+e; tokens
-    // >= nvalid are -inf.
-    __device__ __forceinline__ void qk(uint32_t kcb, uint32_t ksb, int nvalid, float (&s2)[4]) const {
+    // outside [lo, hi) (sub-tile offsets) are -inf.
+    __device__ __forceinline__ void qk(uint32_t kcb, uint32_t ksb, int lo, int hi, float (&s2)[4]) const {
         const uint4 kca = lds128(kcb + 64 * g + 16 * c);
         const uint4 kcb8 = lds128(kcb + 64 * (g + 8) + 16 * c);
         const uint32_t ksa = lds32(ksb + 32 * g + 4 * c);
@@ -240,7 +240,7 @@ struct Lane {
         const uint32_t kb5 = ksb8 << 5, kb10 = ksb8 << 10, kb1 = ksb8 >> 1;
         const uint2 kma = lds64(ksb + 32 * g + 16);
         const uint2 kmb = lds64(ksb + 32 * (g + 8) + 16);
-        const bool va = g < nvalid, vb8 = g + 8 < nvalid;
+        const bool va = g >= lo && g < hi, vb8 = g + 8 >= lo && g + 8 < hi;
 
         // Centroid products: rows g / g+8 of the A operand carry the fp16 hi /
         // lo parts of one token's centroids, so each table entry (hi, lo)
@@ -386,14 +386,16 @@ struct Lane {
     }
 
     // One 32-token stage at `st` (two sub-tiles sharing one softmax update);
-    // tokens >= nvalid are masked.
-    __device__ __forceinline__ void tile(uint32_t st, int nvalid) {
+    // tokens outside [lo, hi) (offsets within the stage) are masked.
+    __device__ __forceinline__ void tile(uint32_t st, int lo, int hi) {
         const VRaw v0 = load_v(st + kOffVC, st + kOffVS);
         float s0[4], s1[4];
-        qk(st + kOffKC, st + kOffKS, nvalid, s0);
-        qk(st + kOffKC + kSubC, st + kOffKS + kSubS, nvalid - 16, s1);
+        qk(st + kOffKC, st + kOffKS, lo, hi, s0);
+        qk(st + kOffKC + kSubC, st + kOffKS + kSubS, lo - 16, hi - 16, s1);
 
-        float corr[2];
+        // mb: the running maximum, or 0 while every token so far is masked
+        // (left padding), so that masked scores give p = 0, not NaN
+        float corr[2], mb[2];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
             float mx = fmaxf(fmaxf(s0[e], s0[2 + e]), fmaxf(s1[e], s1[2 + e]));
@@ -401,16 +403,17 @@ struct Lane {
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
             const float mnew = fmaxf(mrun[e], mx);
-            corr[e] = ex2(mrun[e] - mnew);
+            mb[e] = mnew == -INFINITY ? 0.0f : mnew;
+            corr[e] = ex2(mrun[e] - mb[e]);
             mrun[e] = mnew;
         }
         float p0[4], p1[4];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-            p0[e] = ex2(s0[e] - mrun[e]);
-            p0[2 + e] = ex2(s0[2 + e] - mrun[e]);
-            p1[e] = ex2(s1[e] - mrun[e]);
-            p1[2 + e] = ex2(s1[2 + e] - mrun[e]);
+            p0[e] = ex2(s0[e] - mb[e]);
+            p0[2 + e] = ex2(s0[2 + e] - mb[e]);
+            p1[e] = ex2(s1[e] - mb[e]);
+            p1[2 + e] = ex2(s1[2 + e] - mb[e]);
         }
         if (corr[0] != 1.0f || corr[1] != 1.0f) {
 #pragma unroll
@@ -455,7 +458,8 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap mkc, const __grid_constant
                   const __grid_constant__ CUtensorMap mvc, const __grid_constant__ CUtensorMap mvs,
                   const __half *__restrict__ q, float *__restrict__ pm, float *__restrict__ pl,
                   float *__restrict__ po, int Hq, int Hkv, int64_t seq_len, int tpr, int64_t T, int nslots,
-                  float scale_log2, int flags, const int *__restrict__ seq_len_dev) {
+                  float scale_log2, int flags, const int *__restrict__ seq_len_dev,
+                  const int *__restrict__ start_dev) {
     extern __shared__ __align__(1024) uint8_t sm[];
     // broadcast from lane 0 so that the compiler treats the warp index, and
     // the tile cursors derived from it, as warp-uniform values
@@ -560,6 +564,8 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap mkc, const __grid_constant
         const bool row_ends = (tok0 + seg_tiles * kTile == row_tok);
         const int kvh = (int)(r % Hkv), b = (int)(r / Hkv);
         const int h0 = kvh * G;
+        // first attended token of the sequence (left padding before it)
+        const int t_start = start_dev ? __ldg(start_dev + b) : 0;
         {
             // lane (g, c) holds dims 32c..32c+31 of query head g of the group;
             // with the split columns (G <= 4) lanes g >= 4 repeat head g - 4,
@@ -667,7 +673,7 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap mkc, const __grid_constant
             __syncwarp();  // orders the warp's reads of the stage after the wait
             if (ok && !ready) jfail = j;
             ok = ok && ready;
-            if (ok) L.tile(ring + stage * kStageBytes, (int)min((int64_t)kTile, seq_len - tok0));
+            if (ok) L.tile(ring + stage * kStageBytes, t_start - tok0, (int)min((int64_t)kTile, seq_len - tok0));
             __syncwarp();
             if (ok && j + kStages < ntiles) issue_next(stage);
             ++j;
@@ -785,7 +791,7 @@ template <int G>
 static int launch_g(const CUtensorMap &kc, const CUtensorMap &ks, const CUtensorMap &vc, const CUtensorMap &vs,
                     const void *q, float *pm, float *pl, float *po, int Hq, int Hkv, int64_t seq_len, int tpr,
                     int64_t T, int grid, int ns, float scale_log2, int flags, cudaStream_t s,
-                    const int *seq_len_dev = nullptr) {
+                    const int *seq_len_dev = nullptr, const int *start_dev = nullptr) {
     static bool configured[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -797,7 +803,7 @@ static int launch_g(const CUtensorMap &kc, const CUtensorMap &ks, const CUtensor
     }
     if (launch_pdl(decode_tma_kernel<G>, dim3(grid), dim3(kThreads), kSmBytes, s, kc, ks, vc, vs,
                    reinterpret_cast<const __half *>(q), pm, pl, po, Hq, Hkv, seq_len, tpr, T, ns, scale_log2,
-                   flags, seq_len_dev) != cudaSuccess)
+                   flags, seq_len_dev, start_dev) != cudaSuccess)
         return ECC_ERR_LAUNCH;
     return launch_status();
 }
@@ -848,7 +854,7 @@ int tma_default_splits(int B, int Hkv, int64_t seq_len) { return tmak::make_plan
 // TMA kernel handles (the caller then uses another kernel), or an error.
 int launch_decode_tma(const void *q, const void *kb, const void *vb, int64_t bs_b, int64_t bs_h, float *pm,
                       float *pl, float *po, int B, int Hq, int Hkv, int64_t seq_len, int64_t chunk, int ns,
-                      float scale_log2, int flags, cudaStream_t s) {
+                      float scale_log2, int flags, cudaStream_t s, const int *start_dev) {
     using namespace tmak;
     (void)chunk;
     const int G = Hq / Hkv;
@@ -868,11 +874,11 @@ int launch_decode_tma(const void *q, const void *kb, const void *vb, int64_t bs_
         return 1;
     switch (G) {
 #define ECC_TMA_CASE(N) \
-    case N: return launch_g<N>(kc, ks, vc, vs, q, pm, pl, po, Hq, Hkv, seq_len, (int)plan.tpr, plan.T, plan.grid, ns, scale_log2, flags, s);
+    case N: return launch_g<N>(kc, ks, vc, vs, q, pm, pl, po, Hq, Hkv, seq_len, (int)plan.tpr, plan.T, plan.grid, ns, scale_log2, flags, s, nullptr, start_dev);
         ECC_TMA_CASE(1) ECC_TMA_CASE(2) ECC_TMA_CASE(3) ECC_TMA_CASE(4)
         ECC_TMA_CASE(5) ECC_TMA_CASE(6) ECC_TMA_CASE(7)
         default: return launch_g<8>(kc, ks, vc, vs, q, pm, pl, po, Hq, Hkv, seq_len, (int)plan.tpr, plan.T, plan.grid, ns,
-                                    scale_log2, flags, s);
+                                    scale_log2, flags, s, nullptr, start_dev);
 #undef ECC_TMA_CASE
     }
 }

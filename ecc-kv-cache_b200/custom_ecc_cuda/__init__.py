@@ -82,6 +82,7 @@ def _load():
         "ecc_dequantize": ([p, p, i64, p], i32),
         "ecc_pack_soa": ([p, i64, p, i64, p, i64, p, i64, p], i32),
         "ecc_decode": ([p, p, p, i64, i64, p, p, sz, i32, i32, i32, i64, f32, i32, i32, p], i32),
+        "ecc_decode_masked": ([p, p, p, i64, i64, p, p, p, sz, i32, i32, i32, i64, f32, i32, p], i32),
         "ecc_decode_workspace_size": ([i32, i32, i32, i64, i32], sz),
         "ecc_decode_default_splits": ([i32, i32, i64], i32),
         "ecc_decode_partials": ([p, p, p, i64, i64, p, p, p, i32, i32, i32, i64, f32, i32, i32, p], i32),
@@ -448,6 +449,46 @@ def decode_attention(query: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Te
     return out
 
 
+def decode_attention_masked(query: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, seq_len: int,
+                            start: torch.Tensor, sm_scale: float | None = None, rotate_q: bool = False,
+                            unrotate_out: bool = False, out: torch.Tensor | None = None,
+                            workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """decode_attention of a left-padded batch: sequence b attends to tokens
+    [start[b], seq_len) of its pools only (``start`` int32 [B] on the GPU, read
+    when the kernel runs); the tokens before start[b] are padding.  GQA groups
+    of up to 8 (the TMA-fed kernel); an output row whose whole context is
+    masked is zero."""
+    q3 = _query(query)
+    kbs = _pool_strides(k_pool, "k_pool")
+    vbs = _pool_strides(v_pool, "v_pool")
+    if kbs != vbs or k_pool.shape != v_pool.shape:
+        raise RuntimeError("k_pool and v_pool must have the same shape and strides")
+    B, hq, _ = q3.shape
+    hkv = k_pool.shape[-3]
+    if k_pool.shape[-4] != B or hq % hkv:
+        raise RuntimeError("pool batch or GQA shape does not match the query")
+    if seq_len < 1 or seq_len > k_pool.shape[-2]:
+        raise RuntimeError(f"seq_len {seq_len} must be in [1, {k_pool.shape[-2]}]")
+    _dev_int(start, "start", q3.device)
+    if start.numel() != B or not start.is_contiguous():
+        raise RuntimeError("start must be a contiguous int32 tensor of B elements")
+    if out is None:
+        out = torch.empty((B, hq, 1, D), dtype=torch.float16, device=q3.device)
+    elif not out.is_contiguous() or out.dtype != torch.float16 or out.numel() != B * hq * D:
+        raise RuntimeError("out must be a contiguous float16 tensor of B*Hq*128 elements")
+    flags = (ROTATE_Q if rotate_q else 0) | (UNROTATE_OUT if unrotate_out else 0) | _rec_flag(k_pool)
+    need = decode_workspace_size(B, hq, hkv, seq_len, 0)
+    with torch.cuda.device(q3.device):
+        ws = workspace if workspace is not None else _workspace(q3.device, need)
+        if ws.numel() < need:
+            raise RuntimeError(f"workspace too small: {ws.numel()} < {need} bytes")
+        rc = _lib.ecc_decode_masked(_ptr(q3), _ptr(k_pool), _ptr(v_pool), kbs[0], kbs[1], _ptr(start), _ptr(out),
+                                    _ptr(ws), ws.numel(), B, hq, hkv, int(seq_len),
+                                    float(sm_scale) if sm_scale else 0.0, flags, _stream(q3))
+    _check(rc, "decode_attention_masked")
+    return out
+
+
 def decode_partials(query: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, seq_len: int,
                     num_splits: int, sm_scale: float | None = None, rotate_q: bool = False,
                     cuda_cores: bool = False, kernel: str = "auto"):
@@ -621,10 +662,11 @@ def lse_exchange_merge(pm: torch.Tensor, pl: torch.Tensor, po: torch.Tensor, pee
 
 def device_status(reset: bool = False) -> int:
     """Device-side error flag of the current device since the last reset:
-    1 (or 2) if a decode kernel gave up a bounded wait (it returned early
-    instead of hanging), 3 if an append at a device-side position was out of
-    range (it wrote nothing), 4 if lse_exchange_merge gave up waiting for
-    another rank's records (those rows were not written), else 0."""
+    1 if a decode kernel gave up a bounded wait (it returned early instead of
+    hanging), 2 if the decode kernel found its shared memory at an unexpected
+    address (it computed nothing), 3 if an append at a device-side position
+    was out of range (it wrote nothing), 4 if lse_exchange_merge gave up
+    waiting for another rank's records (those rows were not written), else 0."""
     rc = int(_lib.ecc_device_status(1 if reset else 0))
     if rc < 0:
         _check(rc, "device_status")

@@ -134,6 +134,9 @@ class ErrorCorrectedCache(_HFCache):
         self._pos_dev: Optional[torch.Tensor] = None
         self._len_dev: Optional[torch.Tensor] = None
         self._dev_ws: Optional[torch.Tensor] = None
+        # attention-mask bookkeeping of decode steps (see _mask_window)
+        self._mask_memo = None
+        self._last_window = None
 
         shape = (self._num_layers, self.batch_size, self.num_heads, self._max_cache_len, self.block_bytes)
         self._k_pool = torch.zeros(shape, dtype=torch.uint8, device=dev)
@@ -300,18 +303,82 @@ class ErrorCorrectedCache(_HFCache):
         kp, vp = self.layer_pools(layer_idx)
         return ops.dequantize(kp[:, :, :L].contiguous()), ops.dequantize(vp[:, :, :L].contiguous())
 
-    def decode_attention(self, query: torch.Tensor, layer_idx: int, sm_scale: Optional[float] = None) -> torch.Tensor:
+    def decode_attention(self, query: torch.Tensor, layer_idx: int, sm_scale: Optional[float] = None,
+                         attn_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
         """One decode step of attention of ``query`` [B, Hq, 1, 128] over the
-        compressed context of ``layer_idx`` (the new token already appended)."""
+        compressed context of ``layer_idx`` (the new token already appended).
+
+        ``attn_mask``: the SDPA mask of the step ([B, 1, 1, kv_len] or [B,
+        kv_len], bool with True = attend, or additive float), or None.  Left
+        padding (each sequence attends to a suffix of the context, as batched
+        ``generate()`` with a left-padded prompt produces) runs the fused
+        kernel with a per-sequence start; a mask of any other shape of
+        attended positions takes the reconstructed context and the masked
+        SDPA.  The mask is read once per forward pass (every layer gets the
+        same tensor)."""
         kp, vp = self.layer_pools(layer_idx)
         q16 = query if query.dtype == torch.float16 else query.to(torch.float16)
         if self._dev_mode:
+            # device-side lengths (CUDA-graph replay): the mask is not read
+            # while recording; GraphDecoder refuses padded batches
             out = ops.decode_attention_dev(q16, kp, vp, self._len_dev, sm_scale=sm_scale, rotate_q=True,
                                            unrotate_out=self.rotate_values, workspace=self._dev_ws)
+            return out if query.dtype == torch.float16 else out.to(query.dtype)
+        fill = self._layer_fill[layer_idx]
+        window = self._mask_window(attn_mask, fill) if attn_mask is not None else None
+        if window is None:
+            out = ops.decode_attention(q16, kp, vp, seq_len=fill, sm_scale=sm_scale, rotate_q=True,
+                                       unrotate_out=self.rotate_values, num_splits=self.num_splits)
+        elif isinstance(window, torch.Tensor) and self.num_attention_heads // self.num_heads <= 8:
+            out = ops.decode_attention_masked(q16, kp, vp, seq_len=fill, start=window, sm_scale=sm_scale,
+                                              rotate_q=True, unrotate_out=self.rotate_values)
         else:
-            out = ops.decode_attention(q16, kp, vp, seq_len=self._layer_fill[layer_idx], sm_scale=sm_scale,
-                                       rotate_q=True, unrotate_out=self.rotate_values, num_splits=self.num_splits)
+            out = self._masked_sdpa(q16, layer_idx, fill, attn_mask, sm_scale)
         return out if query.dtype == torch.float16 else out.to(query.dtype)
+
+    def _mask_window(self, attn_mask: torch.Tensor, fill: int):
+        """None when the mask attends to every cached token; an int32 [B]
+        device tensor of first attended positions when every sequence attends
+        to a suffix of the context (left padding); False otherwise.  Cached per
+        mask tensor and length, so one forward pass reads the mask once."""
+        key = (attn_mask.data_ptr(), tuple(attn_mask.shape), attn_mask.dtype, fill)
+        hit = self._mask_memo
+        if hit is not None and hit[0] == key:
+            return hit[1]
+        m = attn_mask
+        if m.dim() == 4:
+            m = m[:, 0, -1, :]
+        elif m.dim() != 2:
+            raise RuntimeError(f"decode attention mask must be [B, 1, 1, L] or [B, L], got {tuple(attn_mask.shape)}")
+        if m.shape[0] not in (1, self.batch_size) or m.shape[-1] < fill:
+            raise RuntimeError(f"decode attention mask {tuple(attn_mask.shape)} does not cover the batch of "
+                               f"{self.batch_size} and the {fill} cached tokens")
+        attend = m[:, :fill] if m.dtype == torch.bool else m[:, :fill] > torch.finfo(m.dtype).min / 2
+        attend = attend.expand(self.batch_size, fill)
+        any_ = attend.any(-1)
+        first = torch.where(any_, attend.int().argmax(-1), torch.full_like(any_, fill, dtype=torch.int64))
+        suffix = attend.sum(-1) == fill - first
+        padded, is_suffix = torch.stack([(first > 0).any(), suffix.all()]).tolist()
+        if not is_suffix:
+            window = False
+        elif not padded:
+            window = None
+        else:
+            window = first.to(torch.int32).contiguous()
+        self._mask_memo = (key, window)
+        self._last_window = window
+        return window
+
+    def _masked_sdpa(self, q16: torch.Tensor, layer_idx: int, fill: int, attn_mask: torch.Tensor,
+                     sm_scale: Optional[float]) -> torch.Tensor:
+        """Decode under an arbitrary mask: the layer's context reconstructed
+        on the GPU (dequantise kernel + inverse WHT) and torch's masked SDPA."""
+        k, v = self._context_fp16(layer_idx, fill)
+        mask = attn_mask[..., :fill]
+        if mask.dim() == 2:
+            mask = mask[:, None, None, :]
+        return torch.nn.functional.scaled_dot_product_attention(q16, k, v, attn_mask=mask, scale=sm_scale,
+                                                                enable_gqa=self.num_attention_heads != self.num_heads)
 
     # ------------------------------------------------------------------ #
     # HuggingFace Cache protocol                                          #
@@ -356,6 +423,8 @@ class ErrorCorrectedCache(_HFCache):
     def reset(self) -> None:
         self._layer_fill = [0] * self._num_layers
         self._seen_tokens = 0
+        self._mask_memo = None
+        self._last_window = None
 
     def crop(self, max_length: int) -> None:
         if max_length < 0:

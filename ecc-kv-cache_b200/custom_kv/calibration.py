@@ -1,20 +1,42 @@
-"""calibration.py -- per-layer calibration statistics in the reference's JSON
-format (custom_kv/calibration.py:11-20, :243-249):
+"""calibration.py -- per-layer key statistics for calibrated quantisation, in
+the reference's JSON format (custom_kv/calibration.py:11-20, :243-249):
 
     {"model_id": ..., "n_samples": N, "max_length": M,
      "layers": {"0": {"scale": s, "zero": z, "alpha": a, "sigma": s}, ...}}
 
-Activations are collected with forward hooks on each layer's k_proj/v_proj
-(the reference's approach, :100-164); the rotation and quantisation
-statistics run on the GPU through custom_ecc_cuda.
+Three steps:
+
+1. ``ProjectionSampler`` -- a context manager that taps the k_proj / v_proj
+   output of every attention module (modules are found by their ``layer_idx``
+   attribute) and keeps a random sample of up to ``rows_per_pass`` rows of each
+   output per forward pass, on the host in fp32.  The reference samples 1000
+   rows per pass the same way (custom_kv/calibration.py:117-130).
+2. ``layer_statistics`` -- one layer's statistics from its sampled key rows
+   k [N, Hkv*head_dim].  Default (``per_head=False``) is what the reference's
+   calibrate_from_model computes (custom_kv/calibration.py:214-237): the
+   normalised WHT of each whole row (length Hkv*head_dim), sigma = unbiased
+   std and mean of all rotated values, scale = sigma, zero = mean, and alpha =
+   mean |x - k~| with k~ the 16-level reconstruction (ops_cpu.py:78-109) under
+   that scale and zero.  ``per_head=True`` rotates every head_dim vector on
+   its own instead -- the rotation the cache applies to the keys it stores, so
+   those statistics describe the values the calibrated quantiser actually
+   sees; it is an option because its numbers differ from the reference's.
+   The WHT runs on the GPU (custom_ecc_cuda.hadamard_rotate, bit-exact with
+   hadamard_rotate_cpu); the reductions are torch's GPU reductions, so the
+   statistics agree with the reference's CPU ones to float32 rounding.
+3. ``calibrate_from_model`` -- runs 1 and 2 over texts and writes the JSON.
 """
 from __future__ import annotations
 
 import json
 from pathlib import Path
-from typing import Any, Dict, List, Optional
+from typing import Any, Dict, Iterable, List, Optional, Sequence, Union
 
 import torch
+
+# the 16-level table of custom_kv/ops_cpu.py:19-24 (float32)
+_LEVELS = (-2.4008, -1.8435, -1.4371, -1.0993, -0.7996, -0.5224, -0.2582, 0.0,
+           0.2582, 0.5224, 0.7996, 1.0993, 1.4371, 1.8435, 2.4008, 3.1584)
 
 
 def lloyd_max_gaussian(n_levels: int = 16, sigma: float = 1.0, n_iter: int = 100) -> List[float]:
@@ -40,95 +62,184 @@ def lloyd_max_gaussian(n_levels: int = 16, sigma: float = 1.0, n_iter: int = 100
     return levels.tolist()
 
 
-def _collect_kv_activations(model, tokenizer, texts, max_length: int = 2048, device: str = "cuda") -> Dict[int, dict]:
-    """Run ``model`` over ``texts`` and keep up to 1000 random rows of every
-    layer's k_proj and v_proj outputs per forward pass (CPU fp32)."""
-    num_layers = model.config.num_hidden_layers
-    rows: Dict[int, dict] = {i: {"k": [], "v": []} for i in range(num_layers)}
-    hooks = []
+# --------------------------------------------------------------------------
+# 1. sampling of the projection outputs
+# --------------------------------------------------------------------------
+class ProjectionSampler:
+    """Samples rows of every attention layer's k_proj and v_proj output.
 
-    def grab(layer_idx: int, which: str):
-        def hook(module, inputs, output):
-            x = output.detach().float().reshape(-1, output.shape[-1])
-            n = min(1000, x.shape[0])
-            rows[layer_idx][which].append(x[torch.randperm(x.shape[0], device=x.device)[:n]].cpu())
-        return hook
+    Usage::
 
-    for i, layer in enumerate(model.model.layers):
-        hooks.append(layer.self_attn.k_proj.register_forward_hook(grab(i, "k")))
-        hooks.append(layer.self_attn.v_proj.register_forward_hook(grab(i, "v")))
-    model.eval()
-    try:
-        with torch.no_grad():
-            for text in texts:
-                inputs = tokenizer(text, return_tensors="pt", max_length=max_length, truncation=True)
-                if hasattr(inputs, "to"):
-                    inputs = inputs.to(device)
-                else:
-                    inputs = {k: v.to(device) if hasattr(v, "to") else v for k, v in inputs.items()}
-                model(**inputs)
-    finally:
-        for h in hooks:
-            h.remove()
-    return {i: {"k": torch.cat(r["k"]), "v": torch.cat(r["v"])} for i, r in rows.items() if r["k"]}
+        with ProjectionSampler(model) as tap:
+            for batch in batches:
+                model(**batch)
+        keys = tap.rows("k")    # {layer: [N, Hkv*head_dim] fp32 CPU tensor}
+
+    Every forward pass contributes min(rows_per_pass, rows of the output)
+    rows per layer, drawn without replacement with the sampler's seeded
+    generator.
+    """
+
+    def __init__(self, model, rows_per_pass: int = 1000, seed: int = 0):
+        self.model = model
+        self.rows_per_pass = int(rows_per_pass)
+        self.seed = int(seed)
+        self._gen: Dict[torch.device, torch.Generator] = {}
+        self._store: Dict[str, Dict[int, List[torch.Tensor]]] = {"k": {}, "v": {}}
+        self._handles: List = []
+
+    def _generator(self, device: torch.device) -> torch.Generator:
+        g = self._gen.get(device)
+        if g is None:
+            g = torch.Generator(device=device)
+            g.manual_seed(self.seed)
+            self._gen[device] = g
+        return g
+
+    def _tap(self, which: str, layer: int):
+        def on_output(module, inputs, output):
+            flat = output.detach().reshape(-1, output.shape[-1])
+            n = flat.shape[0]
+            take = min(self.rows_per_pass, n)
+            pick = torch.randperm(n, generator=self._generator(flat.device), device=flat.device)[:take]
+            self._store[which].setdefault(layer, []).append(flat.index_select(0, pick).float().cpu())
+        return on_output
+
+    def __enter__(self) -> "ProjectionSampler":
+        found = 0
+        for module in self.model.modules():
+            layer = getattr(module, "layer_idx", None)
+            if not isinstance(layer, int):
+                continue
+            kp, vp = getattr(module, "k_proj", None), getattr(module, "v_proj", None)
+            if kp is None or vp is None:
+                continue
+            self._handles.append(kp.register_forward_hook(self._tap("k", layer)))
+            self._handles.append(vp.register_forward_hook(self._tap("v", layer)))
+            found += 1
+        if not found:
+            raise RuntimeError("ProjectionSampler: no attention module with layer_idx, k_proj and v_proj found")
+        return self
+
+    def __exit__(self, *exc) -> None:
+        while self._handles:
+            self._handles.pop().remove()
+
+    def rows(self, which: str = "k") -> Dict[int, torch.Tensor]:
+        """{layer index: sampled rows [N, features]} for "k" or "v"."""
+        return {layer: torch.cat(parts) for layer, parts in sorted(self._store[which].items())}
 
 
-def layer_statistics(k: torch.Tensor, head_dim: int = 128, device: Optional[torch.device] = None) -> Dict[str, float]:
-    """Calibration statistics of one layer's keys k [N, Hkv*head_dim]: rotate
-    every head vector with the WHT (GPU), then sigma/mean of all rotated
-    values and alpha = mean |x - Q(x)| under the 16-level table with
-    scale = sigma, zero = mean (custom_kv/calibration.py:216-237)."""
+def _encode(tokenizer, text: str, max_length: int, device: torch.device) -> Dict[str, torch.Tensor]:
+    enc = tokenizer(text, return_tensors="pt", max_length=max_length, truncation=True)
+    items = enc.items() if hasattr(enc, "items") else dict(enc).items()
+    return {name: (val.to(device) if isinstance(val, torch.Tensor) else val) for name, val in items}
+
+
+# --------------------------------------------------------------------------
+# 2. statistics of one layer
+# --------------------------------------------------------------------------
+def _wht_rows(x: torch.Tensor, width: int) -> torch.Tensor:
+    """Normalised WHT of every run of ``width`` values of x [N, F] (fp32, GPU)."""
     import custom_ecc_cuda as ops
 
+    if width & (width - 1) or not 1 <= width <= 1024:
+        raise RuntimeError(f"the WHT width must be a power of two up to 1024, got {width}")
+    y = x.reshape(-1, width).contiguous()
+    ops.hadamard_rotate(y)
+    return y.reshape(x.shape)
+
+
+def layer_statistics(k: torch.Tensor, head_dim: int = 128, per_head: bool = False,
+                     device: Optional[torch.device] = None) -> Dict[str, float]:
+    """Calibration statistics {scale, zero, alpha, sigma} of one layer's key
+    rows k [N, Hkv*head_dim].  ``per_head=False`` (the reference's
+    statistics): WHT over each whole row; ``per_head=True``: WHT over each
+    head_dim vector."""
     dev = device or torch.device("cuda", torch.cuda.current_device())
-    x = k.to(dev, torch.float32).reshape(-1, head_dim).contiguous()
-    ops.hadamard_rotate(x)
-    sigma = x.std().item()
-    mean = x.mean().item()
-    lm = torch.tensor([-2.4008, -1.8435, -1.4371, -1.0993, -0.7996, -0.5224, -0.2582, 0.0,
-                       0.2582, 0.5224, 0.7996, 1.0993, 1.4371, 1.8435, 2.4008, 3.1584], device=dev)
-    alpha_sum = 0.0
-    for chunk in x.split(1 << 16):
-        xn = (chunk - mean) / sigma
-        q = (xn.unsqueeze(-1) - lm).abs().argmin(-1)
-        alpha_sum += (chunk - (lm[q] * sigma + mean)).abs().sum().item()
-    return {"scale": sigma, "zero": mean, "alpha": alpha_sum / x.numel(), "sigma": sigma}
+    x = k.to(dev, torch.float32)
+    if x.dim() != 2:
+        raise RuntimeError(f"k must be [N, features], got {tuple(k.shape)}")
+    width = head_dim if per_head else x.shape[1]
+    if x.shape[1] % width:
+        raise RuntimeError(f"rows of {x.shape[1]} values do not split into heads of {head_dim}")
+    xr = _wht_rows(x, width)
+    sigma = xr.std().item()
+    mean = xr.mean().item()
+    # the reconstruction of ops_cpu.lloyd_max_quantize_cpu with the scalars
+    # rounded to float32 (torch's cast of a Python scalar operand)
+    levels = torch.tensor(_LEVELS, dtype=torch.float32, device=dev)
+    sc = torch.tensor(sigma, dtype=torch.float32, device=dev)
+    zr = torch.tensor(mean, dtype=torch.float32, device=dev)
+    abs_sum = torch.zeros((), dtype=torch.float64, device=dev)
+    for part in xr.reshape(-1).split(1 << 20):
+        u = (part - zr) / sc
+        code = (u[:, None] - levels).abs().argmin(-1)
+        recon = levels[code] * sc + zr
+        abs_sum += (part - recon).abs().double().sum()
+    alpha = abs_sum.item() / xr.numel()
+    return {"scale": sigma, "zero": mean, "alpha": alpha, "sigma": sigma}
+
+
+# --------------------------------------------------------------------------
+# 3. the whole calibration
+# --------------------------------------------------------------------------
+def read_texts(source: Union[str, Path, None], limit: int, max_chars: int = 4000) -> List[str]:
+    """Texts for calibration from a directory of .txt files (sorted by name,
+    one text per file) or a single .txt file (one text per blank-line
+    separated paragraph); each cut to ``max_chars`` characters.  There is no
+    download fallback: pass ``texts=`` to calibrate_from_model instead."""
+    if source is None:
+        return []
+    path = Path(source)
+    if path.is_dir():
+        chunks: Iterable[str] = (f.read_text(encoding="utf-8") for f in sorted(path.glob("*.txt")))
+    elif path.is_file():
+        chunks = (p for p in path.read_text(encoding="utf-8").split("\n\n") if p.strip())
+    else:
+        return []
+    out: List[str] = []
+    for text in chunks:
+        if len(out) >= limit:
+            break
+        out.append(text[:max_chars])
+    return out
 
 
 def calibrate_from_model(model, tokenizer, calibration_data_path: Optional[str] = None,
-                         texts: Optional[List[str]] = None, n_samples: int = 512, max_length: int = 2048,
-                         output_path: Optional[str] = None) -> Dict[str, Any]:
-    """Per-layer calibration config from a model and texts (a directory of
-    .txt files or a list); saved as JSON when ``output_path`` is given."""
+                         texts: Optional[Sequence[str]] = None, n_samples: int = 512, max_length: int = 2048,
+                         output_path: Optional[str] = None, per_head: bool = False, rows_per_pass: int = 1000,
+                         seed: int = 0) -> Dict[str, Any]:
+    """Per-layer calibration config from ``model`` run over texts (a list, or
+    a directory / file read by ``read_texts``); written as JSON to
+    ``output_path`` when given.  Values are rounded to 6 decimals as the
+    reference's are.  ``per_head`` selects the per-head statistics (see the
+    module docstring)."""
     if texts is None:
-        texts = _load_calibration_texts(calibration_data_path, n_samples)
-    texts = texts[:n_samples]
+        texts = read_texts(calibration_data_path, n_samples)
+    texts = list(texts)[:n_samples]
+    if not texts:
+        raise RuntimeError("calibrate_from_model: no calibration texts")
     device = next(model.parameters()).device
-    acts = _collect_kv_activations(model, tokenizer, texts, max_length, str(device))
-    head_dim = getattr(model.config, "head_dim", None) or model.config.hidden_size // model.config.num_attention_heads
+    model.eval()
+    with torch.no_grad(), ProjectionSampler(model, rows_per_pass=rows_per_pass, seed=seed) as tap:
+        for text in texts:
+            model(**_encode(tokenizer, text, max_length, device))
+    cfg = model.config
+    head_dim = getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads
     layers = {}
-    for layer_idx, kv in acts.items():
-        st = layer_statistics(kv["k"], head_dim)
-        layers[str(layer_idx)] = {k: round(v, 6) for k, v in st.items()}
-    config = {"model_id": getattr(model.config, "_name_or_path", ""), "n_samples": n_samples,
-              "max_length": max_length, "layers": layers}
+    for layer, k in tap.rows("k").items():
+        stats = layer_statistics(k, head_dim=head_dim, per_head=per_head)
+        layers[str(layer)] = {name: round(val, 6) for name, val in stats.items()}
+    config = {"model_id": getattr(cfg, "_name_or_path", ""), "n_samples": n_samples, "max_length": max_length,
+              "layers": layers}
+    if per_head:
+        config["rotation"] = "per_head"
     if output_path:
-        Path(output_path).parent.mkdir(parents=True, exist_ok=True)
-        with open(output_path, "w") as f:
-            json.dump(config, f, indent=2)
+        out = Path(output_path)
+        out.parent.mkdir(parents=True, exist_ok=True)
+        out.write_text(json.dumps(config, indent=2))
     return config
-
-
-def _load_calibration_texts(data_path: Optional[str], n_samples: int) -> List[str]:
-    """Up to n_samples texts from the *.txt files of a directory (no network
-    fallback)."""
-    texts: List[str] = []
-    if data_path:
-        path = Path(data_path)
-        if path.exists():
-            for f in sorted(path.glob("*.txt"))[:n_samples]:
-                texts.append(f.read_text(encoding="utf-8")[:4000])
-    return texts
 
 
 def load_calibration_config(path: str) -> Dict[str, Any]:

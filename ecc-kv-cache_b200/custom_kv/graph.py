@@ -20,7 +20,8 @@ class GraphDecoder:
     ``first_token`` [B, 1] (int64, on the GPU) is the token that follows the
     ``cache``'s current content (typically the argmax of the prefill logits).
     The SDPA patch of ``cache`` must be active (``ecc_cache`` or
-    ``patch_model``) while the decoder is made.  Each ``step()`` feeds the
+    ``patch_model``) while the decoder is made, and the batch must be unpadded
+    (replays do not read an attention mask).  Each ``step()`` feeds the
     current token, appends its K/V to every layer, and returns the next token
     (a device tensor the next replay overwrites).  The cache's host-side
     lengths are not advanced by replays; ``sync_host_lengths()`` reads them back.
@@ -29,6 +30,10 @@ class GraphDecoder:
     def __init__(self, model, cache: ErrorCorrectedCache, first_token: torch.Tensor):
         if not isinstance(cache, ErrorCorrectedCache):
             raise TypeError("GraphDecoder needs an ErrorCorrectedCache")
+        if cache._last_window is not None:
+            # replays do not read the attention mask (it is not a graph input)
+            raise RuntimeError("GraphDecoder serves unpadded batches: the last forward pass had an attention mask "
+                               "that excludes cached tokens")
         self.model = model
         self.cache = cache
         dev = cache._device

@@ -1,17 +1,32 @@
-"""patch.py -- monkey-patches ``F.scaled_dot_product_attention`` so that
-single-token (decode) attention runs the fused ECC-INT4 decode kernel over the
-active cache's block pools (custom_kv/patch.py:23-117 of the reference).
+"""patch.py -- sends the single-token (decode) attention of a Hugging Face model
+to the fused ECC-INT4 decode kernel; ``patch_model`` / ``unpatch_model`` keep
+the names and meaning of the reference's custom_kv/patch.py:23-61.
 
-Prefill (query length > 1): the original SDPA on the fp16 K/V that
-``ErrorCorrectedCache.update`` returned.
-Decode (query length 1): ``decode_attention`` over the layer's pools -- query
-WHT, GQA, online softmax and the output un-rotation happen inside the kernel;
-no fp16 copy of the cache is made (the reference dequantised the whole layer
-and called SDPA without GQA, custom_kv/patch.py:100-117).
+Design.  One ``_DecodeRouter`` instance owns all patch state.  While it is
+installed, ``torch.nn.functional.scaled_dot_product_attention`` is the router's
+``sdpa`` method:
+
+* a query of length 1 (a decode step) is answered from the cache's block
+  pools by ``ErrorCorrectedCache.decode_attention`` -- query WHT, GQA, online
+  softmax, output un-rotation and the attention mask (left padding of a
+  batch) are handled there; no fp16 copy of the cache is made;
+* everything else (prefill) goes to the saved SDPA with its arguments
+  untouched.
+
+Which layer a decode call belongs to: Hugging Face attention writes the new
+token into the cache (``update``) immediately before it calls SDPA, so the
+cache's last updated layer is the layer of the call.  For callers that reach
+SDPA without an ``update``, attention modules that carry a ``layer_idx``
+attribute (all transformers attention classes do) report their index through a
+forward pre-hook; the router uses that hint when the cache has no context for
+its last layer.
+
+The patch is process-global (torch's SDPA symbol) and not thread-safe, as in
+the reference.
 """
 from __future__ import annotations
 
-from typing import TYPE_CHECKING, Optional
+from typing import TYPE_CHECKING, List, Optional
 
 import torch
 import torch.nn.functional as F
@@ -19,69 +34,72 @@ import torch.nn.functional as F
 if TYPE_CHECKING:
     from .cache import ErrorCorrectedCache
 
-_original_sdpa = F.scaled_dot_product_attention
-_active_cache: Optional["ErrorCorrectedCache"] = None
-_current_layer_idx: int = 0
-_is_patched: bool = False
-_hook_handles = []
+
+class _DecodeRouter:
+    def __init__(self) -> None:
+        self.cache: Optional["ErrorCorrectedCache"] = None
+        self.saved_sdpa = None
+        self.hooks: List = []
+        self.layer_hint = 0
+
+    @property
+    def active(self) -> bool:
+        return self.saved_sdpa is not None
+
+    def install(self, model, cache: "ErrorCorrectedCache") -> None:
+        if self.active:  # already installed: keep the first cache, like the reference
+            return
+        self.cache = cache
+        self.layer_hint = 0
+        self.saved_sdpa = F.scaled_dot_product_attention
+        F.scaled_dot_product_attention = self.sdpa
+        for module in _attention_modules(model):
+            self.hooks.append(module.register_forward_pre_hook(self._note_layer))
+
+    def remove(self) -> None:
+        if self.saved_sdpa is not None:
+            F.scaled_dot_product_attention = self.saved_sdpa
+        self.saved_sdpa = None
+        self.cache = None
+        self.layer_hint = 0
+        while self.hooks:
+            self.hooks.pop().remove()
+
+    def _note_layer(self, module, args) -> None:
+        self.layer_hint = int(module.layer_idx)
+
+    def _layer_of_call(self) -> int:
+        cache = self.cache
+        last = cache._last_layer
+        return last if cache._layer_fill[last] > 0 else self.layer_hint
+
+    def sdpa(self, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, attn_mask=None,
+             dropout_p: float = 0.0, is_causal: bool = False, scale=None, **kwargs) -> torch.Tensor:
+        if self.cache is not None and query.dim() == 4 and query.shape[2] == 1:
+            return self.cache.decode_attention(query, self._layer_of_call(), sm_scale=scale, attn_mask=attn_mask)
+        return self.saved_sdpa(query, key, value, attn_mask=attn_mask, dropout_p=dropout_p, is_causal=is_causal,
+                               scale=scale, **kwargs)
+
+
+def _attention_modules(model) -> List[torch.nn.Module]:
+    """Attention modules of ``model`` that know their layer index."""
+    return [m for m in model.modules() if isinstance(getattr(m, "layer_idx", None), int)
+            and any(hasattr(m, name) for name in ("q_proj", "qkv_proj", "query_key_value"))]
+
+
+_router = _DecodeRouter()
 
 
 def patch_model(model, cache: "ErrorCorrectedCache") -> None:
-    """Route decode attention of ``model`` through ``cache`` (global patch, not
-    thread-safe, idempotent)."""
-    global _active_cache, _is_patched, _current_layer_idx
-    if _is_patched:
-        return
-    _active_cache = cache
-    _current_layer_idx = 0
-    F.scaled_dot_product_attention = _ecc_sdpa
-    _install_layer_hooks(model)
-    _is_patched = True
+    """Route decode attention of ``model`` through ``cache`` (global; a second
+    call while patched does nothing)."""
+    _router.install(model, cache)
 
 
 def unpatch_model() -> None:
-    """Restore the original SDPA and remove the layer hooks."""
-    global _active_cache, _is_patched, _current_layer_idx
-    F.scaled_dot_product_attention = _original_sdpa
-    _active_cache = None
-    _is_patched = False
-    _current_layer_idx = 0
-    for handle in _hook_handles:
-        handle.remove()
-    _hook_handles.clear()
+    """Restore torch's SDPA and remove the layer hooks."""
+    _router.remove()
 
 
-def _install_layer_hooks(model) -> None:
-    try:
-        layers = model.model.layers
-    except AttributeError:
-        layers = [m for n, m in model.named_modules() if "self_attn" in n and hasattr(m, "q_proj")]
-
-    def make_hook(layer_idx):
-        def pre_hook(module, args):
-            global _current_layer_idx
-            _current_layer_idx = layer_idx
-        return pre_hook
-
-    for i, layer in enumerate(layers):
-        attn = layer.self_attn if hasattr(layer, "self_attn") else layer
-        _hook_handles.append(attn.register_forward_pre_hook(make_hook(i)))
-
-
-def _ecc_sdpa(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, attn_mask=None, dropout_p: float = 0.0,
-              is_causal: bool = False, scale=None, **kwargs) -> torch.Tensor:
-    """Patched SDPA: decode queries go to the ECC kernel, the rest to SDPA."""
-    if _active_cache is not None and query.dim() == 4 and query.shape[2] == 1:
-        return _ecc_decode_step(query, _current_layer_idx, scale)
-    return _original_sdpa(query, key, value, attn_mask=attn_mask, dropout_p=dropout_p, is_causal=is_causal,
-                          scale=scale, **kwargs)
-
-
-def _ecc_decode_step(query: torch.Tensor, layer_idx: int, scale: Optional[float] = None) -> torch.Tensor:
-    """query [B, Hq, 1, 128] in the model basis -> attention output
-    [B, Hq, 1, 128].  The layer is the one whose ``update`` ran last (the HF
-    attention calls ``update`` right before SDPA); the pre-hook index is the
-    fallback for callers that bypass ``update``."""
-    cache = _active_cache
-    layer = cache._last_layer if cache._layer_fill[cache._last_layer] > 0 else layer_idx
-    return cache.decode_attention(query, layer, sm_scale=scale)
+def is_patched() -> bool:
+    return _router.active

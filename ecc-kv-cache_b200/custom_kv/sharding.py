@@ -78,9 +78,14 @@ class PeerExchange:
     custom_ecc_cuda.lse_exchange_merge can store into all of them.  Made
     collectively (every rank at the same point); calls of ``merge`` must then
     be made in step on every rank, and ``close`` collectively at the end.
-    Not for CUDA-graph capture: each call's epoch is a kernel argument."""
+    Not for CUDA-graph capture: each call's epoch is a kernel argument.
 
-    def __init__(self, rows: int, group, device: torch.device, ops=None):
+    A merge whose bounded wait for another rank ran out raises the device
+    status flag (4) and leaves its rows unwritten instead of hanging; the flag
+    is read (one synchronisation) every ``check_every`` merges when that is
+    > 0, and always at ``close``, and turns into a ``RuntimeError``."""
+
+    def __init__(self, rows: int, group, device: torch.device, ops=None, check_every: int = 0):
         if ops is None:
             import custom_ecc_cuda as ops  # noqa: F811
         self.ops = ops
@@ -94,6 +99,8 @@ class PeerExchange:
         dist.all_gather_object(handles, handle, group=group)
         self.ptrs = [self.own if q == self.rank else ops.exchange_open(h, device) for q, h in enumerate(handles)]
         self.epoch = 0
+        self.calls = 0
+        self.check_every = int(check_every)
         dist.barrier(group=group)  # every buffer zeroed and mapped before the first call
 
     def merge(self, pm: torch.Tensor, pl: torch.Tensor, po: torch.Tensor, unrotate_out: bool = True,
@@ -102,9 +109,22 @@ class PeerExchange:
             raise RuntimeError("the exchange is closed")
         if torch.cuda.is_current_stream_capturing():
             raise RuntimeError("the peer exchange cannot be recorded in a CUDA graph (use exchange='nccl')")
-        self.epoch += 1
-        return self.ops.lse_exchange_merge(pm, pl, po, self.ptrs, self.rank, self.epoch, unrotate_out=unrotate_out,
-                                           out=out)
+        if pm.dim() != 3 or pm.shape[0] * pm.shape[1] != self.rows:
+            raise RuntimeError(f"the exchange was made for {self.rows} rows, got partials of shape {tuple(pm.shape)}")
+        # epochs run 1 .. 2^32 - 2 and round again (0 is never a valid tag);
+        # the wrap keeps consecutive calls on alternating buffer halves
+        self.epoch = self.epoch % 0xFFFFFFFE + 1
+        res = self.ops.lse_exchange_merge(pm, pl, po, self.ptrs, self.rank, self.epoch, unrotate_out=unrotate_out,
+                                          out=out)
+        self.calls += 1
+        if self.check_every > 0 and self.calls % self.check_every == 0:
+            self._raise_on_status(self.ops.device_status())
+        return res
+
+    def _raise_on_status(self, status: int) -> None:
+        if status != 0:
+            raise RuntimeError(f"rank {self.rank}: the peer exchange reported device status {status} (a wait for "
+                               f"another rank's records ran out; those outputs are not valid)")
 
     def close(self) -> None:
         """Unmap the other ranks' buffers and free this rank's (collective;
@@ -112,6 +132,7 @@ class PeerExchange:
         if not self.ptrs:
             return
         torch.cuda.synchronize(self.device)
+        status = self.ops.device_status()
         dist.barrier(group=self.group)
         for q, p in enumerate(self.ptrs):
             if q != self.rank:
@@ -119,6 +140,7 @@ class PeerExchange:
         dist.barrier(group=self.group)  # nobody maps this rank's buffer any more
         self.ops.exchange_free(self.own, self.device)
         self.ptrs = []
+        self._raise_on_status(status)
 
 
 class ShardedDecode:
@@ -218,6 +240,10 @@ class ShardedDecode:
             if mark is not None:
                 mark.record()
             if self._peer is None or self._peer.rows != B * hq_l:
+                if self._peer is not None:
+                    # every rank switches at the same step: release the old
+                    # buffers collectively before making the new ones
+                    self._peer.close()
                 self._peer = PeerExchange(B * hq_l, self.group, query.device, ops=ops)
             return self._peer.merge(pm, pl, po, unrotate_out=unrotate_out, out=out)
         rec = self._buf("rec", (B, hq_l, ops.RECORD_FLOATS), torch.float32, query.device)

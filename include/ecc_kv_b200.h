@@ -69,9 +69,18 @@ const char *ecc_strerror(int code);
 /* Library version, e.g. 100 for 0.1.0. */
 int ecc_version(void);
 
-/* 1 if a kernel of this library on the current device ran out of a bounded
- * wait (and returned early instead of hanging) since the last reset, else 0;
- * reset != 0 clears the flag.  Synchronous. */
+/* Device-side error flag of the current device since the last reset
+ * (reset != 0 clears it); synchronous:
+ *   0  no error;
+ *   1  a decode kernel ran out of a bounded wait on its copies and returned
+ *      early instead of hanging (its output is not valid);
+ *   2  the decode kernel found its shared memory at an unexpected address and
+ *      returned without computing;
+ *   3  an append at a device-side position (ecc_compress_strided_pair_at,
+ *      ..._calibrated_at) was out of range and wrote nothing;
+ *   4  ecc_lse_exchange_merge ran out of its wait for another rank's records
+ *      (the rows it waited for were not written).
+ * When several were raised, the lowest of 1/2 (decode), 3, 4 is returned. */
 int ecc_device_status(int reset);
 
 /* Self-test of the bounded device waits (no counterpart in the reference):
@@ -210,6 +219,22 @@ int ecc_decode(const void *q_f16, const void *k_blocks, const void *v_blocks, in
                int Hkv, int64_t seq_len, float sm_scale, int flags, int num_splits,
                ecc_stream_t stream);
 
+/* ecc_decode of a left-padded batch (its attention mask): sequence b attends
+ * to tokens [start_dev[b], seq_len) only; the tokens before start_dev[b] are
+ * the padding a batched prompt put in front of the shorter sequences.
+ *   start_dev: DEVICE int32 [B], read when the kernel runs; a value <= 0
+ *              masks nothing, a value >= seq_len masks the whole sequence
+ *              (its output is then zero).
+ * The other arguments are those of ecc_decode with num_splits = 0 (workspace
+ * of ecc_decode_workspace_size(B, Hq, Hkv, seq_len, 0) bytes).  GQA groups up
+ * to 8 and pool layouts a TMA tensor map can describe; ECC_ERR_SHAPE
+ * otherwise.  Replaces the attention-mask handling the reference's decode
+ * step drops (custom_kv/patch.py:87-117 calls SDPA with attn_mask=None). */
+int ecc_decode_masked(const void *q_f16, const void *k_blocks, const void *v_blocks, int64_t bs_b,
+                      int64_t bs_h, const int *start_dev, void *out_f16, void *workspace,
+                      size_t workspace_bytes, int B, int Hq, int Hkv, int64_t seq_len, float sm_scale,
+                      int flags, ecc_stream_t stream);
+
 /* Workspace bytes ecc_decode needs for these sizes (0 if it needs none);
  * num_splits as passed to ecc_decode. */
 size_t ecc_decode_workspace_size(int B, int Hq, int Hkv, int64_t seq_len, int num_splits);
@@ -259,7 +284,10 @@ int ecc_lse_merge_records(const float *records, int64_t rows, int n, int64_t rec
  *   ecc_exchange_buffer_bytes(rows, world): bytes of one rank's exchange
  *     buffer (zero-filled once before the first call).
  *   ecc_exchange_grid(rows): CTAs per call (the same on every rank).
- *   ecc_lse_exchange_merge: part_m/l/o as for ecc_lse_merge (this rank's n
+ *   ecc_lse_exchange_merge: ECC_ERR_SHAPE unless every entry of peer_buffers
+ *     is a buffer this process allocated (ecc_exchange_alloc) or mapped
+ *     (ecc_exchange_open) and holds ecc_exchange_buffer_bytes(rows, world)
+ *     bytes; part_m/l/o as for ecc_lse_merge (this rank's n
  *     split partials of every row); peer_buffers: HOST array of `world`
  *     device pointers, entry q = rank q's exchange buffer as mapped in this
  *     process (entry `rank` = this rank's own); epoch: 1, 2, 3, ... -- the

@@ -36,8 +36,11 @@ PARAMS = [(0.998123, 0.004127, 0.197531), (0.052341, -0.031, 0.0123), (7.25, 0.5
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("ECC_KV_REFERENCE"),
+                    help="checkout of the reference project (or set ECC_KV_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("--reference (or ECC_KV_REFERENCE) is required")
     sys.path.insert(0, os.path.abspath(args.reference))
     from custom_kv import ops_cpu
 

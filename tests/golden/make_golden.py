@@ -132,10 +132,13 @@ def ref_decode(ref, q16: torch.Tensor, kblk: np.ndarray, vblk: np.ndarray, procs
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("ECC_KV_REFERENCE"),
+                    help="checkout of the reference project (or set ECC_KV_REFERENCE)")
     ap.add_argument("--procs", type=int, default=os.cpu_count() or 4)
     ap.add_argument("--skip-c1-decode", action="store_true")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("--reference (or ECC_KV_REFERENCE) is required")
     ref = os.path.abspath(args.reference)
     sys.path.insert(0, ref)
     from custom_kv import ops_cpu

@@ -1,5 +1,5 @@
 """Host-side logic of the Python API that needs no GPU: construction errors
-(no CPU path), the SDPA patch lifecycle, calibration hooks and format."""
+(no CPU path), the SDPA patch lifecycle, calibration sampling and format."""
 import json
 import types
 
@@ -49,79 +49,100 @@ def test_ops_reject_cpu_tensors():
         ops.get_block_metadata(torch.zeros(4, 128, dtype=torch.uint8), 0)
 
 
+class _Attn(torch.nn.Module):
+    """Stand-in for a transformers attention module: layer_idx and projections."""
+
+    def __init__(self, layer_idx, d_model=4, d_kv=4):
+        super().__init__()
+        self.layer_idx = layer_idx
+        self.q_proj = torch.nn.Linear(d_model, d_kv, bias=False)
+        self.k_proj = torch.nn.Linear(d_model, d_kv, bias=False)
+        self.v_proj = torch.nn.Linear(d_model, d_kv, bias=False)
+
+    def forward(self, x):
+        self.k_proj(x)
+        self.v_proj(x)
+        return x
+
+
+class _Model(torch.nn.Module):
+    def __init__(self, n_layers=2, d_model=4, d_kv=4):
+        super().__init__()
+        self.d_model = d_model
+        self.config = types.SimpleNamespace(num_hidden_layers=n_layers, hidden_size=d_model,
+                                            num_attention_heads=1, head_dim=d_kv)
+        self.layers = torch.nn.ModuleList([_Attn(i, d_model, d_kv) for i in range(n_layers)])
+
+    def forward(self, input_ids=None, **kw):
+        x = torch.randn(1, input_ids.shape[1], self.d_model)
+        for layer in self.layers:
+            x = layer(x)
+        return x
+
+
 def test_patch_and_unpatch_restore_sdpa():
     from custom_kv import patch_model, unpatch_model
     from custom_kv import patch as P
-
-    class Attn(torch.nn.Module):
-        def __init__(self):
-            super().__init__()
-            self.q_proj = torch.nn.Linear(4, 4)
-
-    class Layer(torch.nn.Module):
-        def __init__(self):
-            super().__init__()
-            self.self_attn = Attn()
-
-    model = types.SimpleNamespace(model=types.SimpleNamespace(layers=[Layer(), Layer()]))
+    model = _Model()
     original = F.scaled_dot_product_attention
     for _ in range(3):
         patch_model(model, cache=object())
-        assert F.scaled_dot_product_attention is not original
-        patch_model(model, cache=object())  # idempotent
+        assert F.scaled_dot_product_attention is not original and P.is_patched()
+        assert len(P._router.hooks) == 2  # one pre-hook per attention module
+        patch_model(model, cache=object())  # a second call while patched does nothing
+        assert len(P._router.hooks) == 2
         unpatch_model()
-        assert F.scaled_dot_product_attention is original
-        assert not P._hook_handles
+        assert F.scaled_dot_product_attention is original and not P.is_patched()
+        assert not P._router.hooks
 
 
-def test_patched_sdpa_passes_prefill_through():
+def test_patched_sdpa_passes_prefill_through_and_notes_layers():
+    from custom_kv import patch_model, unpatch_model
     from custom_kv import patch as P
-    P._active_cache = None
-    q = torch.randn(1, 2, 3, 8)
-    assert torch.allclose(P._ecc_sdpa(q, q, q, is_causal=True), P._original_sdpa(q, q, q, is_causal=True))
+    model = _Model(n_layers=3)
+    original = F.scaled_dot_product_attention
+    patch_model(model, cache=object())
+    try:
+        q = torch.randn(1, 2, 3, 8)
+        got = F.scaled_dot_product_attention(q, q, q, is_causal=True)
+        assert torch.equal(got, original(q, q, q, is_causal=True))
+        model.layers[2](torch.zeros(1, 1, 4))
+        assert P._router.layer_hint == 2
+    finally:
+        unpatch_model()
 
 
-def test_calibration_hooks_capture_all_layers():
-    """Mirrors the reference's hook test (tests/integration/test_colab_compat.py:256)."""
-    from custom_kv.calibration import _collect_kv_activations
+def test_projection_sampler_taps_every_layer():
+    """Every attention module's k_proj / v_proj output is sampled, up to
+    rows_per_pass rows per forward pass (the reference's hook test is
+    tests/integration/test_colab_compat.py:256)."""
+    from custom_kv.calibration import ProjectionSampler, _encode
     n_layers, d_model, d_kv = 4, 64, 32
-
-    class SA(torch.nn.Module):
-        def __init__(self):
-            super().__init__()
-            self.k_proj = torch.nn.Linear(d_model, d_kv, bias=False)
-            self.v_proj = torch.nn.Linear(d_model, d_kv, bias=False)
-
-    class L(torch.nn.Module):
-        def __init__(self):
-            super().__init__()
-            self.self_attn = SA()
-
-        def forward(self, x):
-            self.self_attn.k_proj(x)
-            self.self_attn.v_proj(x)
-            return x
-
-    class Top(torch.nn.Module):
-        def __init__(self):
-            super().__init__()
-            self.config = types.SimpleNamespace(num_hidden_layers=n_layers)
-            self.model = torch.nn.Module()
-            self.model.layers = torch.nn.ModuleList([L() for _ in range(n_layers)])
-
-        def forward(self, input_ids=None, **kw):
-            x = torch.randn(1, input_ids.shape[1], d_model)
-            for layer in self.model.layers:
-                x = layer(x)
-            return x
+    model = _Model(n_layers, d_model, d_kv)
 
     def tok(text, return_tensors=None, max_length=None, truncation=None):
         return {"input_ids": torch.randint(0, 100, (1, min(len(text.split()), max_length or 32)))}
 
-    res = _collect_kv_activations(Top(), tok, ["hello world " * 20] * 3, max_length=32, device="cpu")
-    assert len(res) == n_layers
+    with ProjectionSampler(model, rows_per_pass=20, seed=3) as tap:
+        for text in ["hello world " * 20] * 3:
+            model(**_encode(tok, text, 32, torch.device("cpu")))
+    k, v = tap.rows("k"), tap.rows("v")
+    assert sorted(k) == list(range(n_layers)) and sorted(v) == list(range(n_layers))
     for i in range(n_layers):
-        assert res[i]["k"].shape[-1] == d_kv and res[i]["v"].shape[-1] == d_kv
+        assert k[i].shape == (60, d_kv) and v[i].shape == (60, d_kv)  # 3 passes x 20 of 32 rows
+    assert not any(m._forward_hooks for m in model.modules())  # hooks removed on exit
+
+
+def test_read_texts(tmp_path):
+    from custom_kv.calibration import read_texts
+    (tmp_path / "b.txt").write_text("second " * 1000)
+    (tmp_path / "a.txt").write_text("first")
+    assert read_texts(tmp_path, 5) == ["first", ("second " * 1000)[:4000]]
+    assert read_texts(tmp_path, 1) == ["first"]
+    f = tmp_path / "one.txt"
+    f.write_text("p1\n\np2\n\n\np3")
+    assert read_texts(f, 2) == ["p1", "p2"]
+    assert read_texts(tmp_path / "missing", 3) == [] and read_texts(None, 3) == []
 
 
 def test_lloyd_max_gaussian_is_symmetric_and_sorted():

@@ -46,7 +46,7 @@ def _err(got: torch.Tensor, ref: np.ndarray) -> float:
 
 @pytest.mark.parametrize("ci", range(4))
 @pytest.mark.parametrize("kern", ["tma", "register", "cuda_cores"])
-def test_decode_matches_reference_golden(ops, decode_golden, cuda_device, ci, kern):
+def test_decode_matches_reference_golden(ops, oracle, decode_golden, cuda_device, ci, kern):
     B, hq, hkv, L = [int(v) for v in decode_golden[f"case{ci}_meta"]]
     kb = _dev(decode_golden[f"case{ci}_kblocks"], cuda_device)
     vb = _dev(decode_golden[f"case{ci}_vblocks"], cuda_device)
@@ -54,7 +54,14 @@ def test_decode_matches_reference_golden(ops, decode_golden, cuda_device, ci, ke
     out = ops.decode_attention(q, kb, vb, seq_len=L, kernel=kern)
     ref = decode_golden[f"case{ci}_out16"].view(np.float16).astype(np.float32).reshape(B, hq, 128)
     g = out.float().cpu().numpy().reshape(ref.shape)
+    # against the reference's own fp16 output: both sides are rounded to
+    # fp16, so the sound bound is TOL plus one ulp (half an ulp each)
     assert float((np.abs(g - ref) - _ulp16(ref)).max()) <= TOL
+    # against the oracle's fp32 value (pinned to the same fixture in
+    # tests/test_oracle_golden.py): TOL plus half an ulp
+    ref32 = oracle.decode(decode_golden[f"case{ci}_q16"], decode_golden[f"case{ci}_kblocks"],
+                          decode_golden[f"case{ci}_vblocks"], hkv=hkv, seq_len=L)
+    assert _err(out, ref32) <= TOL
 
 
 def test_fused_ecc_decode_attention_soa_api(decode_golden, cuda_device):
@@ -76,7 +83,7 @@ def test_fused_ecc_decode_attention_soa_api(decode_golden, cuda_device):
 
 
 @pytest.mark.parametrize("kern", ["tma", "register", "cuda_cores"])
-def test_full_c1_decode_against_reference(ops, cuda_device, kern):
+def test_full_c1_decode_against_reference(ops, oracle, cuda_device, kern):
     """Single-layer op test: GPU compress then decode vs the reference's
     cpu_reference_decode output (GQA via repeat_kv)."""
     path = os.path.join(os.path.dirname(__file__), "golden", "c1_decode_out16.npy")
@@ -89,9 +96,12 @@ def test_full_c1_decode_against_reference(ops, cuda_device, kern):
     ops.compress_into(v16.to(cuda_device), vp, pos=0, rotate=True)
     out = ops.decode_attention(q16.to(cuda_device), kp, vp, seq_len=2048, kernel=kern)
     ref = np.load(path).view(np.float16).astype(np.float32).reshape(1, 32, 128)
-    # the reference's output is already fp16: allow one fp16 ulp on top of TOL
+    # the reference's output is already fp16: one fp16 ulp (half on each side) on top of TOL
     g = out.float().cpu().numpy().reshape(ref.shape)
     assert float((np.abs(g - ref) - _ulp16(ref)).max()) <= TOL
+    # and TOL plus half an ulp against the oracle's fp32 output on the same blocks
+    ref32 = oracle.decode(q16.numpy(), kp.cpu().numpy(), vp.cpu().numpy(), hkv=8, seq_len=2048)
+    assert _err(out, ref32) <= TOL
 
 
 def _random_pools(oracle, B, hkv, L, cap, seed):
