@@ -128,6 +128,13 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+// 8x8 transpose of 16-bit elements across the warp: lane (g, c) passes row g,
+// columns 2c, 2c+1 and receives row g, columns 2c, 2c+1 of the transpose.
+__device__ __forceinline__ uint32_t movtrans(uint32_t a) {
+    uint32_t d;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+    return d;
+}
 __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
     __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t *>(&h);
@@ -202,14 +209,28 @@ struct Lane {
     uint32_t qs[8][2];  // q of the sign products, k slot of bit p scaled by 2^-(ssh + kexp(p))
     float sgn2;         // 2^(ssh + 1): q.s = sgn2 * (sign product) - sum(q)
     float qsum[2];
-    float o[16][4];  // PV accumulators, one per dim of the lane's 16 (rows g: hi + sign, g+8: lo)
+    // PV accumulators: o[i] rows g / g+8 = dims 16g + 2i / 16g + 2i + 1 (code
+    // byte i of the lane's 8 V code bytes), columns = the n8 operand columns
+    float o[8][4];
     float mrun[2], lrun[2], zrun[2];
     uint32_t lane8, sel_half;
+    uint32_t voff;  // this lane's byte offset in the swizzled V code box (see load_v)
+    uint32_t soff;  // this lane's byte offset in the swizzled syndrome boxes (see qk, load_v)
     int g, c;
     float scale_log2;
 
     // Raw V data of one 16-token sub-tile: tokens 2c, 2c+1, 2c+8, 2c+9 (code
     // bytes 8g..8g+7, syndrome word g/2) and the metadata of tokens g, g+8.
+    //
+    // The V code box (64-byte rows) is written with the 64-byte swizzle:
+    // 16-byte chunk j of row r lands at chunk j ^ ((r >> 1) & 3).  Lane (g,
+    // c) reads chunk g/2 of rows 2c + {0, 1, 8, 9}, whose (r >> 1) & 3 is c,
+    // so its offset within a row is the lane constant 16 ((g/2) ^ c) + 8 (g &
+    // 1) (voff): a half-warp's reads then fall on 16 banks instead of 8.  The
+    // syndrome/metadata boxes (32-byte rows) use the 32-byte swizzle: chunk
+    // j of row r at chunk j ^ ((r >> 2) & 1) (soff: 16 ((r >> 2) & 1) for the
+    // rows a lane reads), which makes the syndrome-word and metadata reads
+    // conflict-free.
     struct VRaw {
         uint2 vc[4];
         uint32_t vs[4];
@@ -220,11 +241,13 @@ struct Lane {
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const int tok = 2 * c + (u & 1) + 8 * (u >> 1);
-            v.vc[u] = lds64(vcb + 64 * tok + 8 * g);
-            v.vs[u] = lds32(vsb + 32 * tok + 4 * (g >> 1));
+            v.vc[u] = lds64(vcb + 64 * tok + voff);
+            // row tok: (tok >> 2) & 1 = c >> 1
+            v.vs[u] = lds32(vsb + 32 * tok + 16 * (c >> 1) + 4 * (g >> 1));
         }
-        v.vma = lds64(vsb + 32 * g + 16);
-        v.vmb = lds64(vsb + 32 * (g + 8) + 16);
+        // metadata: chunk 1 of rows g and g + 8, (row >> 2) & 1 = g >> 2
+        v.vma = lds64(vsb + 32 * g + (16 ^ soff));
+        v.vmb = lds64(vsb + 32 * (g + 8) + (16 ^ soff));
         return v;
     }
 
@@ -234,12 +257,13 @@ struct Lane {
     __device__ __forceinline__ void qk(uint32_t kcb, uint32_t ksb, int lo, int hi, float (&s2)[4]) const {
         const uint4 kca = lds128(kcb + 64 * g + 16 * c);
         const uint4 kcb8 = lds128(kcb + 64 * (g + 8) + 16 * c);
-        const uint32_t ksa = lds32(ksb + 32 * g + 4 * c);
-        const uint32_t ksb8 = lds32(ksb + 32 * (g + 8) + 4 * c);
+        // syndrome box with the 32-byte swizzle (see load_v): rows g, g + 8
+        const uint32_t ksa = lds32(ksb + 32 * g + soff + 4 * c);
+        const uint32_t ksb8 = lds32(ksb + 32 * (g + 8) + soff + 4 * c);
         const uint32_t ka5 = ksa << 5, ka10 = ksa << 10, ka1 = ksa >> 1;
         const uint32_t kb5 = ksb8 << 5, kb10 = ksb8 << 10, kb1 = ksb8 >> 1;
-        const uint2 kma = lds64(ksb + 32 * g + 16);
-        const uint2 kmb = lds64(ksb + 32 * (g + 8) + 16);
+        const uint2 kma = lds64(ksb + 32 * g + (16 ^ soff));
+        const uint2 kmb = lds64(ksb + 32 * (g + 8) + (16 ^ soff));
         const bool va = g >= lo && g < hi, vb8 = g + 8 >= lo && g + 8 < hi;
 
         // Centroid products: rows g / g+8 of the A operand carry the fp16 hi /
@@ -277,76 +301,57 @@ struct Lane {
     }
 
     // PV products of one 16-token sub-tile with probabilities p (same layout
-    // as the scores).
+    // as the scores: p[e] token g, p[2+e] token g+8, head 2c+e).
+    //
+    // The B operand (k = token, n = column) comes from the score layout (row =
+    // token, columns 2c, 2c+1 in lane (g, c)) by one 8x8 transpose per token
+    // half (movmatrix).  Its words: ws = p*scale_v with its fp16 residual
+    // ws - fp16(ws) (a single fp16 rounding of ws is 2^-11 relative, close to
+    // the 2e-3 output tolerance when a few large values dominate), and the
+    // sign weights wa = p*alpha_v.  Groups of up to 4 heads use the idle
+    // columns 4..7 for the sign products: the score columns 4..7 repeat heads
+    // 0..3 (see the query set-up), lanes c >= 2 put 2*wa there, and the
+    // sign bits are masked in place (each fp16 half is 0 or the power of two
+    // whose only set bit is p), so every accumulator row has one known weight
+    // that the epilogue divides out; s = 2b - 1 moves -alpha_v into the
+    // zero-point sum.  Groups of 5..8 use +-1 sign operands against wa.
+    //
+    // Per code byte i of the lane (dims 16g + 2i, 16g + 2i + 1 in rows g,
+    // g + 8 of accumulator i), four products: centroids hi x ws, centroids
+    // lo x ws, centroids hi x residual, signs x sign weights.
     __device__ __forceinline__ void pv(const VRaw &v, const float (&p)[4]) {
         const float v_sa = h_lo(v.vma.x), v_aa = h_lo(v.vma.y);
         const float v_sb = h_lo(v.vmb.x), v_ab = h_lo(v.vmb.y);
         constexpr bool kSplitCols = G <= 4;
-        // P operand words per (token, head): pk = fp16 (p*scale_v, p*alpha_v
-        // (x2 with the split columns)), pr = fp16 residual of p*scale_v, so
-        // that the centroid products carry p*scale_v to ~2^-22 (a single
-        // fp16 rounding of it is 2^-11 relative, close to the 2e-3 output
-        // tolerance when a few large values dominate)
-        // pr[j/2] packs the residuals of the lane's two heads (slots j, j+1)
-        uint32_t pk[4], pr[2];
-        float res[4];
+        // rows of the pre-transpose matrices: t = 0 token g, t = 1 token g+8
+        uint32_t mw[2], mr[2], ma[2];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float pj = p[j];
-            const float ws = pj * (j < 2 ? v_sa : v_sb);
-            const float wa = (kSplitCols ? 2.0f : 1.0f) * (pj * (j < 2 ? v_aa : v_ab));
-            pk[j] = pack_h2(ws, wa);
-            res[j] = ws - h_lo(pk[j]);
+        for (int t = 0; t < 2; ++t) {
+            const float sc = t ? v_sb : v_sa, al = (kSplitCols ? 2.0f : 1.0f) * (t ? v_ab : v_aa);
+            const float w0 = p[2 * t] * sc, w1 = p[2 * t + 1] * sc;
+            mw[t] = pack_h2(w0, w1);
+            mr[t] = pack_h2(w0 - h_lo(mw[t]), w1 - h_hi(mw[t]));
+            ma[t] = pack_h2(p[2 * t] * al, p[2 * t + 1] * al);
         }
-        pr[0] = pack_h2(res[0], res[1]);
-        pr[1] = pack_h2(res[2], res[3]);
-        uint32_t bt[4], rp0, rp1;
-        {
-            const int srcA = 8 * c + ((kSplitCols ? (g & 3) : g) >> 1), srcB = srcA + 4;
-            const bool odd = g & 1;
-            // lane srcA holds the P words of tokens 2c (slots 0, 1) and 2c+8
-            // (slots 2, 3), lane srcB those of tokens 2c+1 and 2c+9
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                const int src = (t & 1) ? srcB : srcA;
-                const int j = (t >> 1) * 2;  // slot pair: tokens g (j = 0) or g+8 (j = 2)
-                const uint32_t xe = __shfl_sync(0xffffffffu, pk[j], src), xo = __shfl_sync(0xffffffffu, pk[j + 1], src);
-                bt[t] = odd ? xo : xe;
-            }
-            // residual pairs (token 2c, 2c+1) and (2c+8, 2c+9) of the lane's head
-            const uint32_t sel = odd ? 0x7632u : 0x5410u;
-            rp0 = __byte_perm(__shfl_sync(0xffffffffu, pr[0], srcA), __shfl_sync(0xffffffffu, pr[0], srcB), sel);
-            rp1 = __byte_perm(__shfl_sync(0xffffffffu, pr[1], srcA), __shfl_sync(0xffffffffu, pr[1], srcB), sel);
-        }
-        // b1: p*scale_v, b2: sign weights, b3: p*scale_v residual, bo: the
-        // operand of the odd dims' centroid products
-        uint32_t b1_0, b1_1, b2_0, b2_1, b3_0, b3_1, bo_0, bo_1;
+        // B words: [0] tokens 2c, 2c+1, [1] tokens 2c+8, 2c+9 of column g
+        uint32_t bw[2], br[2], bs[2];
         if constexpr (kSplitCols) {
-            // columns 0..3 (lanes g < 4): p*scale_v of head g, and its
-            // residual for an extra product into the even dims' accumulators;
-            // columns 4..7 (lanes g >= 4) of head g-4: the sign weights in the
-            // even dims' accumulators, the residual in the odd dims' (their
-            // columns 4..7 are otherwise unused)
-            const bool cent = g < 4;
-            const uint32_t sel = cent ? 0x5410u : 0x7632u;
-            const uint32_t y0 = __byte_perm(bt[0], bt[1], sel), y1 = __byte_perm(bt[2], bt[3], sel);
-            b1_0 = cent ? y0 : 0u;
-            b1_1 = cent ? y1 : 0u;
-            b2_0 = cent ? 0u : y0;
-            b2_1 = cent ? 0u : y1;
-            b3_0 = cent ? rp0 : 0u;
-            b3_1 = cent ? rp1 : 0u;
-            bo_0 = cent ? y0 : rp0;
-            bo_1 = cent ? y1 : rp1;
+            const bool cent = g < 4, lo_cols = c < 2;
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+                const uint32_t x = movtrans(lo_cols ? mw[t] : ma[t]);
+                const uint32_t r = movtrans(mr[t]);
+                bw[t] = cent ? x : 0u;
+                bs[t] = cent ? 0u : x;
+                br[t] = cent ? r : 0u;
+            }
         } else {
-            b1_0 = __byte_perm(bt[0], bt[1], 0x5410);
-            b1_1 = __byte_perm(bt[2], bt[3], 0x5410);
-            b2_0 = __byte_perm(bt[0], bt[1], 0x7632);
-            b2_1 = __byte_perm(bt[2], bt[3], 0x7632);
-            b3_0 = rp0;
-            b3_1 = rp1;
-            bo_0 = b1_0;
-            bo_1 = b1_1;
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+                bw[t] = movtrans(mw[t]);
+                br[t] = movtrans(mr[t]);
+                bs[t] = movtrans(ma[t]);
+            }
         }
 
         const uint32_t sA = __byte_perm(v.vs[0], v.vs[1], sel_half), sB = __byte_perm(v.vs[2], v.vs[3], sel_half);
@@ -359,28 +364,20 @@ struct Lane {
             const uint32_t ib_e = (xb0 & kLo) | ((xb1 << 4) & kHi), ib_o = ((xb0 >> 4) & kLo) | (xb1 & kHi);
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                // dims 16g + 2i (even) and 16g + 2i + 1 (odd); accumulator 2i
-                // (2i+1) holds the even (odd) dim: rows g the fp16 hi part and
-                // the sign term, rows g+8 the lo part
                 const int i = 4 * w + k;
-                const uint2 r0 = lut(ia_e, k, lane8);  // even dim, tokens 2c, 2c+1
+                const uint2 r0 = lut(ia_e, k, lane8);  // even dim, tokens 2c, 2c+1 (hi, lo)
+                const uint2 r1 = lut(ia_o, k, lane8);  // odd dim, tokens 2c, 2c+1
                 const uint2 r2 = lut(ib_e, k, lane8);  // even dim, tokens 2c+8, 2c+9
-                const uint2 r1 = lut(ia_o, k, lane8);  // odd dim
-                const uint2 r3 = lut(ib_o, k, lane8);
-                mma16816(o[2 * i], r0.x, r0.y, r2.x, r2.y, b1_0, b1_1);
-                mma16816(o[2 * i], r0.x, r0.y, r2.x, r2.y, b3_0, b3_1);
-                mma16816(o[2 * i + 1], r1.x, r1.y, r3.x, r3.y, bo_0, bo_1);
-                if constexpr (!kSplitCols) mma16816(o[2 * i + 1], r1.x, r1.y, r3.x, r3.y, b3_0, b3_1);
-                if constexpr (kSplitCols) {
-                    // columns 4..7 of accumulator 2i: rows g the even dim's
-                    // sign term, rows g+8 the odd dim's
-                    mma16816(o[2 * i], sign_bits(sA, 2 * i), sign_bits(sA, 2 * i + 1), sign_bits(sB, 2 * i),
-                             sign_bits(sB, 2 * i + 1), b2_0, b2_1);
-                } else {
-                    mma16816(o[2 * i], sign_pair(sA, 2 * i), 0u, sign_pair(sB, 2 * i), 0u, b2_0, b2_1);
-                    mma16816(o[2 * i + 1], sign_pair(sA, 2 * i + 1), 0u, sign_pair(sB, 2 * i + 1), 0u, b2_0,
-                             b2_1);
-                }
+                const uint2 r3 = lut(ib_o, k, lane8);  // odd dim, tokens 2c+8, 2c+9
+                mma16816(o[i], r0.x, r1.x, r2.x, r3.x, bw[0], bw[1]);
+                mma16816(o[i], r0.y, r1.y, r2.y, r3.y, bw[0], bw[1]);
+                mma16816(o[i], r0.x, r1.x, r2.x, r3.x, br[0], br[1]);
+                if constexpr (kSplitCols)
+                    mma16816(o[i], sign_bits(sA, 2 * i), sign_bits(sA, 2 * i + 1), sign_bits(sB, 2 * i),
+                             sign_bits(sB, 2 * i + 1), bs[0], bs[1]);
+                else
+                    mma16816(o[i], sign_pair(sA, 2 * i), sign_pair(sA, 2 * i + 1), sign_pair(sB, 2 * i),
+                             sign_pair(sB, 2 * i + 1), bs[0], bs[1]);
             }
         }
     }
@@ -417,7 +414,7 @@ struct Lane {
         }
         if (corr[0] != 1.0f || corr[1] != 1.0f) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
+            for (int i = 0; i < 8; ++i) {
                 o[i][0] *= corr[0];
                 o[i][1] *= corr[1];
                 o[i][2] *= corr[0];
@@ -550,6 +547,8 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap mkc, const __grid_constant
     L.c = lane & 3;
     L.lane8 = (uint32_t)lane * 8u;
     L.sel_half = (L.g & 1) ? 0x7632u : 0x5410u;
+    L.voff = 16u * (uint32_t)((L.g >> 1) ^ L.c) + 8u * (uint32_t)(L.g & 1);
+    L.soff = 16u * (uint32_t)((L.g >> 2) & 1);
     L.scale_log2 = scale_log2;
     bool ok = true;
     int jfail = -1;        // first tile whose wait ran out
@@ -650,7 +649,7 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap mkc, const __grid_constant
             L.qsum[1] = __shfl_sync(0xffffffffu, sum, 4 * (2 * L.c + 1));   // head 2c+1
         }
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
+        for (int i = 0; i < 8; ++i)
 #pragma unroll
             for (int k = 0; k < 4; ++k) L.o[i][k] = 0.0f;
 #pragma unroll
@@ -696,27 +695,22 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap mkc, const __grid_constant
         const int64_t prow = ((int64_t)b * Hq + h0) * nslots + slot;  // partial of head h0 of the group
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            // sign terms of dims 16g + 2i, +1: from lane c + 2 (columns
-            // 4..7) when the group uses the split columns, else already in
-            // the accumulators
+            // accumulator i: rows g / g+8 = dims 16g + 2i / 16g + 2i + 1;
+            // with the split columns the sign terms of heads 2c, 2c+1 are in
+            // columns 4..7 of lane c + 2, each row with its power-of-two weight
             float sg[4] = {0.f, 0.f, 0.f, 0.f};
             if constexpr (G <= 4) {
 #pragma unroll
                 for (int k = 0; k < 4; ++k)
-                    sg[k] = __shfl_down_sync(0xffffffffu, L.o[2 * i][k], 2) * sign_unweight(k < 2 ? 2 * i : 2 * i + 1);
-                // the odd dim's residual products (columns 4..7, rows g and g+8)
-#pragma unroll
-                for (int e = 0; e < 2; ++e)
-                    sg[2 + e] += __shfl_down_sync(0xffffffffu, L.o[2 * i + 1][e] + L.o[2 * i + 1][2 + e], 2);
+                    sg[k] = __shfl_down_sync(0xffffffffu, L.o[i][k], 2) * sign_unweight(k < 2 ? 2 * i : 2 * i + 1);
             }
             const int d0 = 16 * L.g + 2 * i;
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
                 const int h = 2 * L.c + e;
                 if (h >= G) continue;
-                float *pod = po + (prow + (int64_t)h * nslots) * kD;
-                pod[d0] = (L.o[2 * i][e] + L.o[2 * i][2 + e]) + (sg[e] + L.zrun[e]);
-                pod[d0 + 1] = (L.o[2 * i + 1][e] + L.o[2 * i + 1][2 + e]) + (sg[2 + e] + L.zrun[e]);
+                float2 *pod = reinterpret_cast<float2 *>(po + (prow + (int64_t)h * nslots) * kD + d0);
+                *pod = make_float2(L.o[i][e] + (sg[e] + L.zrun[e]), L.o[i][2 + e] + (sg[2 + e] + L.zrun[e]));
             }
         }
 #pragma unroll
@@ -773,7 +767,7 @@ static int get_encode() {
 // bytes per record (128, or 96 without the pad sector).  The boxes read bytes
 // 0..63 and 64..95 of a record, so both sizes take the same kernel.
 static int make_map(CUtensorMap *m, const void *base, int64_t seq_len, int Hkv, int B, int64_t bs_h, int64_t bs_b,
-                    uint32_t box_x, int rb) {
+                    uint32_t box_x, int rb, CUtensorMapSwizzle swz) {
     cuuint64_t dims[4] = {(cuuint64_t)rb, (cuuint64_t)seq_len, (cuuint64_t)Hkv, (cuuint64_t)B};
     cuuint64_t sh = (cuuint64_t)bs_h * rb, sb = (cuuint64_t)bs_b * rb;
     if (Hkv == 1) sh = (cuuint64_t)seq_len * rb;  // stride of an extent-1 dim is unused
@@ -782,9 +776,23 @@ static int make_map(CUtensorMap *m, const void *base, int64_t seq_len, int Hkv, 
     cuuint32_t box[4] = {box_x, (cuuint32_t)kTile, 1, 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};
     const CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void *>(base), dims, strides, box,
-                                estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? ECC_OK : ECC_ERR_CUDA;
+}
+
+// The four maps of a launch: K codes (64-byte rows, no swizzle: the K code
+// reads are conflict-free as laid out), K syndrome + metadata (32-byte rows,
+// 32-byte swizzle), V codes (64-byte swizzle), V syndrome + metadata (32-byte
+// swizzle); the kernel's stage reads undo the swizzles.
+static int make_maps(CUtensorMap *kc, CUtensorMap *ks, CUtensorMap *vc, CUtensorMap *vs, const void *kb,
+                     const void *vb, int64_t len, int Hkv, int B, int64_t bs_h, int64_t bs_b, int rb) {
+    if (make_map(kc, kb, len, Hkv, B, bs_h, bs_b, 64, rb, CU_TENSOR_MAP_SWIZZLE_NONE) != ECC_OK ||
+        make_map(ks, kb, len, Hkv, B, bs_h, bs_b, 32, rb, CU_TENSOR_MAP_SWIZZLE_32B) != ECC_OK ||
+        make_map(vc, vb, len, Hkv, B, bs_h, bs_b, 64, rb, CU_TENSOR_MAP_SWIZZLE_64B) != ECC_OK ||
+        make_map(vs, vb, len, Hkv, B, bs_h, bs_b, 32, rb, CU_TENSOR_MAP_SWIZZLE_32B) != ECC_OK)
+        return ECC_ERR_CUDA;
+    return ECC_OK;
 }
 
 template <int G>
@@ -867,11 +875,7 @@ int launch_decode_tma(const void *q, const void *kb, const void *vb, int64_t bs_
     const int rb = (flags & ECC_DECODE_BLOCK96) ? 96 : kBlockBytes;
     flags &= ECC_DECODE_ROTATE_Q;
     CUtensorMap kc, ks, vc, vs;
-    if (make_map(&kc, kb, seq_len, Hkv, B, bs_h, bs_b, 64, rb) != ECC_OK ||
-        make_map(&ks, kb, seq_len, Hkv, B, bs_h, bs_b, 32, rb) != ECC_OK ||
-        make_map(&vc, vb, seq_len, Hkv, B, bs_h, bs_b, 64, rb) != ECC_OK ||
-        make_map(&vs, vb, seq_len, Hkv, B, bs_h, bs_b, 32, rb) != ECC_OK)
-        return 1;
+    if (make_maps(&kc, &ks, &vc, &vs, kb, vb, seq_len, Hkv, B, bs_h, bs_b, rb) != ECC_OK) return 1;
     switch (G) {
 #define ECC_TMA_CASE(N) \
     case N: return launch_g<N>(kc, ks, vc, vs, q, pm, pl, po, Hq, Hkv, seq_len, (int)plan.tpr, plan.T, plan.grid, ns, scale_log2, flags, s, nullptr, start_dev);
@@ -914,11 +918,7 @@ int launch_decode_tma_dev(const void *q, const void *kb, const void *vb, int64_t
     const int rb = (flags & ECC_DECODE_BLOCK96) ? 96 : kBlockBytes;
     flags &= ECC_DECODE_ROTATE_Q;
     CUtensorMap kc, ks, vc, vs;
-    if (make_map(&kc, kb, max_len, Hkv, B, bs_h, bs_b, 64, rb) != ECC_OK ||
-        make_map(&ks, kb, max_len, Hkv, B, bs_h, bs_b, 32, rb) != ECC_OK ||
-        make_map(&vc, vb, max_len, Hkv, B, bs_h, bs_b, 64, rb) != ECC_OK ||
-        make_map(&vs, vb, max_len, Hkv, B, bs_h, bs_b, 32, rb) != ECC_OK)
-        return 1;
+    if (make_maps(&kc, &ks, &vc, &vs, kb, vb, max_len, Hkv, B, bs_h, bs_b, rb) != ECC_OK) return 1;
     switch (G) {
 #define ECC_TMA_CASE(N) \
     case N: return launch_g<N>(kc, ks, vc, vs, q, pm, pl, po, Hq, Hkv, max_len, (int)plan.tpr, plan.T, grid, ns, scale_log2, flags, s, seq_len_dev);

@@ -21,6 +21,23 @@ def ops(cuda_device):
     return custom_ecc_cuda
 
 
+class _Buffers:
+    """Exchange buffers made by the library (ecc_exchange_alloc), as the
+    exchange requires; freed on exit."""
+
+    def __init__(self, ops, dev, rows, world, count):
+        self.ops, self.dev = ops, dev
+        self.ptrs = [ops.exchange_alloc(rows, world, dev)[0] for _ in range(count)]
+
+    def __enter__(self):
+        return self.ptrs
+
+    def __exit__(self, *exc):
+        torch.cuda.synchronize(self.dev)
+        for p in self.ptrs:
+            self.ops.exchange_free(p, self.dev)
+
+
 def _partials(B, hq, n, seed, dev):
     g = torch.Generator(device=dev).manual_seed(seed)
     pm = torch.randn(B, hq, n, device=dev, generator=g) * 3
@@ -34,25 +51,37 @@ def _partials(B, hq, n, seed, dev):
 @pytest.mark.parametrize("B,hq,n", [(8, 32, 29), (1, 4, 1), (3, 40, 70)])
 def test_single_rank_exchange_equals_two_level_merge(ops, cuda_device, B, hq, n):
     rows = B * hq
-    buf = torch.zeros(ops.exchange_buffer_bytes(rows, 1), dtype=torch.uint8, device=cuda_device)
-    for epoch in range(1, 5):
-        pm, pl, po = _partials(B, hq, n, epoch, cuda_device)
-        unrot = bool(epoch & 1)
-        ref = ops.lse_merge_records(ops.lse_merge_to_record(pm, pl, po).unsqueeze(0), unrotate_out=unrot)
-        got = ops.lse_exchange_merge(pm, pl, po, [buf.data_ptr()], 0, epoch, unrotate_out=unrot)
-        assert torch.equal(got.reshape(ref.shape), ref), epoch
+    with _Buffers(ops, cuda_device, rows, 1, 1) as bufs:
+        for epoch in range(1, 5):
+            pm, pl, po = _partials(B, hq, n, epoch, cuda_device)
+            unrot = bool(epoch & 1)
+            ref = ops.lse_merge_records(ops.lse_merge_to_record(pm, pl, po).unsqueeze(0), unrotate_out=unrot)
+            got = ops.lse_exchange_merge(pm, pl, po, bufs, 0, epoch, unrotate_out=unrot)
+            assert torch.equal(got.reshape(ref.shape), ref), epoch
     assert ops.device_status() == 0
 
 
 def test_exchange_argument_errors(ops, cuda_device):
     pm, pl, po = _partials(1, 4, 3, 0, cuda_device)
-    buf = torch.zeros(ops.exchange_buffer_bytes(4, 1), dtype=torch.uint8, device=cuda_device)
-    with pytest.raises(RuntimeError):  # epochs start at 1
-        ops.lse_exchange_merge(pm, pl, po, [buf.data_ptr()], 0, 0)
-    with pytest.raises(RuntimeError):  # rank outside the peer list
-        ops.lse_exchange_merge(pm, pl, po, [buf.data_ptr()], 1, 1)
-    with pytest.raises(RuntimeError):  # more ranks than one node's limit
-        ops.lse_exchange_merge(pm, pl, po, [buf.data_ptr()] * 9, 0, 1)
+    with _Buffers(ops, cuda_device, 4, 1, 1) as bufs:
+        with pytest.raises(RuntimeError):  # epochs start at 1
+            ops.lse_exchange_merge(pm, pl, po, bufs, 0, 0)
+        with pytest.raises(RuntimeError):  # rank outside the peer list
+            ops.lse_exchange_merge(pm, pl, po, bufs, 1, 1)
+        with pytest.raises(RuntimeError):  # more ranks than one node's limit
+            ops.lse_exchange_merge(pm, pl, po, bufs * 9, 0, 1)
+        # a buffer the library did not make or map: refused, nothing is stored
+        plain = torch.zeros(ops.exchange_buffer_bytes(4, 1), dtype=torch.uint8, device=cuda_device)
+        with pytest.raises(RuntimeError):
+            ops.lse_exchange_merge(pm, pl, po, [plain.data_ptr()], 0, 1)
+        # more rows than the buffer was made for: refused
+        pm8, pl8, po8 = _partials(2, 4, 3, 0, cuda_device)
+        with pytest.raises(RuntimeError):
+            ops.lse_exchange_merge(pm8, pl8, po8, bufs, 0, 1)
+    with _Buffers(ops, cuda_device, 4, 2, 1) as bufs:
+        # a buffer made for 2 ranks x 4 rows serves 1 rank x 8 rows (same bytes)
+        pm8, pl8, po8 = _partials(2, 4, 3, 0, cuda_device)
+        ops.lse_exchange_merge(pm8, pl8, po8, bufs, 0, 1)
     assert ops.exchange_buffer_bytes(4, 9) == 0
 
 
@@ -62,17 +91,16 @@ def test_wait_for_missing_rank_gives_up(ops, cuda_device):
     reads 4 and clears, and the next call on the device works."""
     pm, pl, po = _partials(2, 8, 5, 1, cuda_device)
     rows = 16
-    mine = torch.zeros(ops.exchange_buffer_bytes(rows, 2), dtype=torch.uint8, device=cuda_device)
-    other = torch.zeros_like(mine)
     ops.device_status(reset=True)
-    ops.lse_exchange_merge(pm, pl, po, [mine.data_ptr(), other.data_ptr()], 0, 1, wait_cycles=1_000_000)
-    torch.cuda.synchronize()
+    with _Buffers(ops, cuda_device, rows, 2, 2) as bufs:
+        ops.lse_exchange_merge(pm, pl, po, bufs, 0, 1, wait_cycles=1_000_000)
+        torch.cuda.synchronize()
     assert ops.device_status(reset=True) == 4
     assert ops.device_status() == 0
-    one = torch.zeros(ops.exchange_buffer_bytes(rows, 1), dtype=torch.uint8, device=cuda_device)
-    ref = ops.lse_merge_records(ops.lse_merge_to_record(pm, pl, po).unsqueeze(0))
-    got = ops.lse_exchange_merge(pm, pl, po, [one.data_ptr()], 0, 1)
-    assert torch.equal(got.reshape(ref.shape), ref)
+    with _Buffers(ops, cuda_device, rows, 1, 1) as bufs:
+        ref = ops.lse_merge_records(ops.lse_merge_to_record(pm, pl, po).unsqueeze(0))
+        got = ops.lse_exchange_merge(pm, pl, po, bufs, 0, 1)
+        assert torch.equal(got.reshape(ref.shape), ref)
 
 
 def _free_port():
