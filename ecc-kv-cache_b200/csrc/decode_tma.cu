@@ -16,9 +16,12 @@
 // 16x64 B, K syndrome+meta 16x32 B, V codes, V syndrome+meta) on an mbarrier
 // and later waits on it, then __syncwarp hands the data to the warp.  The
 // tensor maps cover [0, seq_len) tokens, so rows past the sequence end come
-// back as zeros; such tokens are masked to -inf.  The consumer math is the one
-// of decode_mma.cu (three m16n8k16 products per 16-dim step for QK and per
-// 16-dim m-tile for PV: centroids hi, centroids lo, signs).
+// back as zeros; such tokens are masked to -inf.  QK: per 16-dim step, one
+// m16n8k16 product for the centroids of 8 tokens (rows g / g+8 = fp16 hi /
+// lo parts) per token half and one for the signs.  PV: per code byte of the
+// lane (two dims in rows g / g+8), four products: centroids hi and lo
+// against p*scale_v, centroids hi against its fp16 residual, signs against
+// the sign weights.
 //
 // Every mbarrier wait is bounded (~2 s of clock64); on timeout the warp
 // raises a device flag for ecc_device_status(), stops computing and drains
@@ -139,18 +142,24 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
     __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t *>(&h);
 }
-// code-byte table entry: offset v*256 + lane*8 assembled by one prmt.  The
-// table sits at the start of the dynamic shared memory, whose shared-window
-// address is the per-block reserve kSmemReserve (checked on the host against
-// cudaDevAttrReservedSharedMemoryPerBlock and again by the kernel), so the
-// base folds into the load's immediate offset.  The table is constant after
-// the kernel's set-up barrier, so the load is not volatile and may be
-// scheduled freely (it depends on `word` anyway).
-__device__ __forceinline__ uint2 lut(uint32_t word, int byte_idx, uint32_t lane8) {
+// Code-byte table lookup: for code byte v (codes v & 15, v >> 4) the fp16x2
+// word of their hi parts and the fp16x2 word of their lo parts.  Row v of the
+// table is 256 bytes: the hi words of the 32 lanes' private copies at v*256 +
+// 4*lane, the lo words 128 bytes further.  Every 32-bit load of a warp then
+// hits 32 distinct banks, and the two halves arrive in separate registers, so
+// the centroid MMA operands (hi words of four lookups in one register quad,
+// lo words in another) need no moves.  The offset v*256 + 4*lane is one prmt.
+// The table sits at the start of the dynamic shared memory, whose
+// shared-window address is the per-block reserve kSmemReserve (checked on the
+// host against cudaDevAttrReservedSharedMemoryPerBlock and again by the
+// kernel), so the base folds into the loads' immediate offsets.  The table is
+// constant after the kernel's set-up barrier, so the loads are not volatile
+// and may be scheduled freely.
+__device__ __forceinline__ uint2 lut(uint32_t word, int byte_idx, uint32_t lane4) {
     uint2 r;
-    asm("ld.shared.v2.u32 {%0,%1}, [%2+%3];"
-        : "=r"(r.x), "=r"(r.y)
-        : "r"(__byte_perm(word, lane8, 0x5504u | ((uint32_t)byte_idx << 4))), "n"(kSmemReserve + kSmLut));
+    const uint32_t a = __byte_perm(word, lane4, 0x5504u | ((uint32_t)byte_idx << 4));
+    asm("ld.shared.u32 %0, [%1+%2];" : "=r"(r.x) : "r"(a), "n"(kSmemReserve + kSmLut));
+    asm("ld.shared.u32 %0, [%1+%2];" : "=r"(r.y) : "r"(a), "n"(kSmemReserve + kSmLut + 128));
     return r;
 }
 // +-1 pair from bits p and p+16 of w (bit 1 -> +1.0)
@@ -213,7 +222,7 @@ struct Lane {
     // byte i of the lane's 8 V code bytes), columns = the n8 operand columns
     float o[8][4];
     float mrun[2], lrun[2], zrun[2];
-    uint32_t lane8, sel_half;
+    uint32_t lane4, sel_half;
     uint32_t voff;  // this lane's byte offset in the swizzled V code box (see load_v)
     uint32_t soff;  // this lane's byte offset in the swizzled syndrome boxes (see qk, load_v)
     int g, c;
@@ -275,10 +284,10 @@ struct Lane {
 #pragma unroll
         for (int m = 0; m < 8; ++m) {
             const int w = m >> 1, by = 2 * (m & 1);
-            const uint2 xa = lut(kwa[w], by, lane8);      // token g, k slots 2c, 2c+1
-            const uint2 ya = lut(kwa[w], by + 1, lane8);  // token g, k slots 2c+8, 2c+9
-            const uint2 xb = lut(kwb[w], by, lane8);      // token g+8
-            const uint2 yb = lut(kwb[w], by + 1, lane8);
+            const uint2 xa = lut(kwa[w], by, lane4);      // token g, k slots 2c, 2c+1
+            const uint2 ya = lut(kwa[w], by + 1, lane4);  // token g, k slots 2c+8, 2c+9
+            const uint2 xb = lut(kwb[w], by, lane4);      // token g+8
+            const uint2 yb = lut(kwb[w], by + 1, lane4);
             mma16816(sa, xa.x, xa.y, ya.x, ya.y, qc[m][0], qc[m][1]);
             mma16816(sb, xb.x, xb.y, yb.x, yb.y, qc[m][0], qc[m][1]);
             mma16816(ss, kbits(ksa, ka5, ka10, ka1, 2 * m), kbits(ksb8, kb5, kb10, kb1, 2 * m),
@@ -362,16 +371,23 @@ struct Lane {
             constexpr uint32_t kLo = 0x0F0F0F0Fu, kHi = 0xF0F0F0F0u;
             const uint32_t ia_e = (xa0 & kLo) | ((xa1 << 4) & kHi), ia_o = ((xa0 >> 4) & kLo) | (xa1 & kHi);
             const uint32_t ib_e = (xb0 & kLo) | ((xb1 << 4) & kHi), ib_o = ((xb0 >> 4) & kLo) | (xb1 & kHi);
+            uint2 r0[4], r1[4], r2[4], r3[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                r0[k] = lut(ia_e, k, lane4);
+                r1[k] = lut(ia_o, k, lane4);
+                r2[k] = lut(ib_e, k, lane4);
+                r3[k] = lut(ib_o, k, lane4);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) mma16816(o[4 * w + k], r0[k].x, r1[k].x, r2[k].x, r3[k].x, bw[0], bw[1]);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) mma16816(o[4 * w + k], r0[k].y, r1[k].y, r2[k].y, r3[k].y, bw[0], bw[1]);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) mma16816(o[4 * w + k], r0[k].x, r1[k].x, r2[k].x, r3[k].x, br[0], br[1]);
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 const int i = 4 * w + k;
-                const uint2 r0 = lut(ia_e, k, lane8);  // even dim, tokens 2c, 2c+1 (hi, lo)
-                const uint2 r1 = lut(ia_o, k, lane8);  // odd dim, tokens 2c, 2c+1
-                const uint2 r2 = lut(ib_e, k, lane8);  // even dim, tokens 2c+8, 2c+9
-                const uint2 r3 = lut(ib_o, k, lane8);  // odd dim, tokens 2c+8, 2c+9
-                mma16816(o[i], r0.x, r1.x, r2.x, r3.x, bw[0], bw[1]);
-                mma16816(o[i], r0.y, r1.y, r2.y, r3.y, bw[0], bw[1]);
-                mma16816(o[i], r0.x, r1.x, r2.x, r3.x, br[0], br[1]);
                 if constexpr (kSplitCols)
                     mma16816(o[i], sign_bits(sA, 2 * i), sign_bits(sA, 2 * i + 1), sign_bits(sB, 2 * i),
                              sign_bits(sB, 2 * i + 1), bs[0], bs[1]);
@@ -486,7 +502,8 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap mkc, const __grid_constant
         uint2 e;
         e.x = __byte_perm(e0, e1, 0x5410);
         e.y = __byte_perm(e0, e1, 0x7632);
-        reinterpret_cast<uint2 *>(sm + kSmLut + v * 256)[lane] = e;
+        reinterpret_cast<uint32_t *>(sm + kSmLut + v * 256)[lane] = e.x;
+        reinterpret_cast<uint32_t *>(sm + kSmLut + v * 256 + 128)[lane] = e.y;
     }
     __syncthreads();
     pdl_trigger();
@@ -545,7 +562,7 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap mkc, const __grid_constant
     Lane<G> L;
     L.g = lane >> 2;
     L.c = lane & 3;
-    L.lane8 = (uint32_t)lane * 8u;
+    L.lane4 = (uint32_t)lane * 4u;
     L.sel_half = (L.g & 1) ? 0x7632u : 0x5410u;
     L.voff = 16u * (uint32_t)((L.g >> 1) ^ L.c) + 8u * (uint32_t)(L.g & 1);
     L.soff = 16u * (uint32_t)((L.g >> 2) & 1);
