@@ -288,6 +288,43 @@ def run_model_e2e(args):
                       "data": "synthetic", **res, "first_token_equal": same_first}), flush=True)
 
 
+def run_prefill(args):
+    """One 32768-token prefill of the Llama-3.1-8B-shaped model (seeded
+    random fp16 weights, seeded random prompt) through the ECC cache, after
+    one warm-up prefill: every layer's K and V are compressed into the block
+    pools by the fused WHT + compress kernel while attention runs on the fp16
+    K/V.  Under ncu's launch list (gpu__time_duration only) this gives the
+    compress kernels' share of the prefill's GPU time.  Prints the wall time."""
+    import torch
+    from transformers import LlamaConfig, LlamaForCausalLM
+    from custom_kv import ecc_cache
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    prompt_len = 32768
+    cfg = LlamaConfig(hidden_size=4096, intermediate_size=14336, num_hidden_layers=32, num_attention_heads=32,
+                      num_key_value_heads=8, head_dim=128, vocab_size=128256, rope_theta=500000.0,
+                      max_position_embeddings=131072)
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = LlamaForCausalLM(cfg).half().eval()
+    prompt = torch.randint(0, cfg.vocab_size, (1, prompt_len), generator=torch.Generator().manual_seed(0)).to(dev)
+    times = []
+    with torch.no_grad():
+        for rep in range(2):
+            with ecc_cache(model, batch_size=1, max_cache_len=prompt_len + 8, device=str(dev)) as cache:
+                torch.cuda.synchronize()
+                if rep == 1:
+                    torch.cuda.profiler.start()  # ncu --profile-from-start off records this prefill only
+                t0 = time.perf_counter()
+                model(prompt, past_key_values=cache, use_cache=True, logits_to_keep=1)
+                torch.cuda.synchronize()
+                times.append(time.perf_counter() - t0)
+                if rep == 1:
+                    torch.cuda.profiler.stop()
+    print(json.dumps({"workload": f"Llama-3.1-8B shape, random fp16 weights, {prompt_len}-token prefill through "
+                                  f"the ECC cache", "prefill_s": times[-1], "warmup_s": times[0]}), flush=True)
+
+
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
@@ -566,7 +603,8 @@ def run_ours(args):
         if sample is not None:
             parity = cpu_parity(pools_host, final_seq, sample)
 
-    launches_per_step = {"single": 3, "kv": 3, "seq": (1 if args.exchange == "p2p" else 2) + 1 + (1 if last else 0)}
+    launches_per_step = {"single": 3, "kv": 3,
+                         "seq": (1 if args.exchange == "p2p" else 2) + 1 + (1 if last else 0)}
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": K, "warmup": W,
@@ -585,10 +623,12 @@ def run_ours(args):
             "clocks": clocks, "e2e": e2e, "compress": comp, "cpu_baseline": cpu, "parity": parity,
         }
         if world > 1:
-            line["exchange"] = ("NCCL all-gather of the ranks' fp16 outputs" if mode == "kv" else
-                                {"p2p": "one kernel: records stored into every rank's buffer over NVLink "
-                                        "(CUDA IPC), epoch-tagged words, merge",
-                                 "nccl": "merge to records, NCCL all-gather, merge"}[args.exchange])
+            line["exchange"] = {("kv", "p2p"): "one kernel: merge of the split partials, fp16 output rows stored "
+                                               "into every rank's buffer over NVLink (CUDA IPC), epoch-tagged words",
+                                ("kv", "nccl"): "merge, then NCCL all-gather of the ranks' fp16 outputs",
+                                ("seq", "p2p"): "one kernel: records stored into every rank's buffer over NVLink "
+                                                "(CUDA IPC), epoch-tagged words, merge",
+                                ("seq", "nccl"): "merge to records, NCCL all-gather, merge"}[(mode, args.exchange)]
             line["parity"] = shard_parity
         if comp:
             line["compress_tok_s"] = comp["tok_s"]
@@ -928,8 +968,8 @@ def main():
     ap.add_argument("--shard", default="kv", choices=["kv", "seq"],
                     help="N > 1: split the decode job by kv head (default) or by sequence chunk")
     ap.add_argument("--exchange", default="p2p", choices=["nccl", "p2p"],
-                    help="--shard seq: how the ranks' records are combined (NCCL all-gather, or one kernel "
-                         "over peer memory)")
+                    help="N > 1: how the ranks' results are combined: one kernel over peer memory (default), "
+                         "or NCCL all-gather between merge kernels")
     ap.add_argument("--block-bytes", type=int, default=BLOCK, choices=[BLOCK, 96],
                     help="record size of the decode pools: the 128-byte block (default, the reference's "
                          "format) or the 96-byte record without the pad sector")
@@ -937,6 +977,9 @@ def main():
                     help="run only the compress benchmark and print its JSON object")
     ap.add_argument("--model-e2e", action="store_true",
                     help="run the Llama-3.1-8B-shaped 32k-prompt generate() comparison and print its JSON object")
+    ap.add_argument("--prefill", action="store_true",
+                    help="run one Llama-3.1-8B-shaped 32k-token prefill through the ECC cache (for ncu launch "
+                         "lists of the prefill)")
     ap.add_argument("--long", choices=["kv", "seq"], default=None,
                     help="long-context decode (B16, 131072 tokens) sharded by kv head or by sequence chunk")
     ap.add_argument("--graph", action="store_true",
@@ -950,6 +993,8 @@ def main():
         run_compress_only(args)
     elif args.model_e2e:
         run_model_e2e(args)
+    elif args.prefill:
+        run_prefill(args)
     elif args.long:
         run_long(args)
     else:

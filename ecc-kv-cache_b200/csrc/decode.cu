@@ -433,6 +433,74 @@ lse_exchange_kernel(const float *__restrict__ pm, const float *__restrict__ pl, 
     }
 }
 
+// ---------------------------------------------------------------------------
+// Output gather over peer memory (kv-head-sharded decode, one GPU per rank):
+// rank s holds kv heads [s*Hkv/W, (s+1)*Hkv/W) of every sequence and computes
+// the outputs of their hq_l query heads.  One kernel per rank and step does
+// the merge of the rank's split partials and the all-gather of the ranks'
+// fp16 outputs.  The CTA of local row r = (b, j) merges row r's partials
+// (lse_combine, write_out's arithmetic), writes the fp16 row at its place in
+// this rank's full output [B, W*hq_l, 128] (query head s*hq_l + j) and
+// stores it into slot [p][s][r] of every other rank's buffer as 64 words
+// (epoch << 32 | two fp16, one store each, the protocol of
+// lse_exchange_kernel); then it polls slot [p][q][r] of its own buffer for
+// every other rank q until each word carries this epoch and writes rank q's
+// row (b, q*hq_l + j).  A CTA waits only for the CTAs of the same local row
+// on the other GPUs (every rank has the same rows), the grid is capped by
+// residency, and the wait is bounded (then g_exchange_error = 4).
+// ---------------------------------------------------------------------------
+constexpr int kGatherWords = kD / 2;
+
+__global__ void __launch_bounds__(kD)
+lse_gather_kernel(const float *__restrict__ pm, const float *__restrict__ pl, const float *__restrict__ po, int n,
+                  int64_t rows, int hq_l, int W, int rank, PeerBufs peers, uint32_t epoch, long long wait_cycles,
+                  __half *__restrict__ out, int flags) {
+    __shared__ float sh[kD];
+    const int d = threadIdx.x;
+    const int64_t half = epoch & 1u;
+    pdl_wait();  // the partials of the kernel before
+    const unsigned long long *mine = peers.base[rank] + half * W * rows * kGatherWords;
+    const long long t0 = clock64();
+    bool ok = true;
+    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        float M, L, O;
+        lse_combine(n, d, SplitSrc{pm, pl, po, r, n}, M, L, O);
+        float val = (L > 0.0f) ? O / L : 0.0f;
+        if (flags & ECC_DECODE_UNROTATE_OUT) {
+            sh[d] = val;
+            smem_wht128(sh, d);
+            val = sh[d];
+        }
+        const uint32_t hb = __half_as_ushort(__float2half_rn(val));
+        const int64_t b = r / hq_l, j = r - b * hq_l;
+        const int64_t stride_q = (int64_t)hq_l * kD;  // one rank's heads of a sequence
+        __half *orow = out + (b * W * hq_l + j) * kD;   // rank q's row: orow + q * stride_q
+        orow[rank * stride_q + d] = __ushort_as_half((unsigned short)hb);
+        const uint32_t hi = __shfl_down_sync(0xffffffffu, hb, 1);
+        if ((d & 1) == 0) {
+            const unsigned long long tw = ((unsigned long long)epoch << 32) | (hb | (hi << 16));
+            for (int q = 0; q < W; ++q)
+                if (q != rank)
+                    st_relaxed_sys(peers.base[q] + ((half * W + rank) * rows + r) * kGatherWords + (d >> 1), tw);
+        }
+        // the other ranks' rows: thread d < 64 takes word d of each (its two dims)
+        if (d < kGatherWords) {
+            unsigned long long w[kExchMaxRanks];
+#pragma unroll
+            for (int q = 0; q < kExchMaxRanks; ++q)
+                if (q < W && q != rank) w[q] = ld_relaxed_sys(mine + ((int64_t)q * rows + r) * kGatherWords + d);
+#pragma unroll
+            for (int q = 0; q < kExchMaxRanks; ++q)
+                if (q < W && q != rank) {
+                    const unsigned long long *src = mine + ((int64_t)q * rows + r) * kGatherWords + d;
+                    const uint32_t v = __float_as_uint(await_word(src, w[q], epoch, t0, wait_cycles, &ok));
+                    reinterpret_cast<uint32_t *>(orow + q * stride_q)[d] = v;
+                }
+        }
+        __syncthreads();  // sh is refilled for the next row
+    }
+}
+
 int exchange_device_error(int reset) {
     int v = 0;
     if (cudaMemcpyFromSymbol(&v, g_exchange_error, sizeof(int)) != cudaSuccess) return ECC_ERR_CUDA;
@@ -903,6 +971,31 @@ extern "C" int ecc_exchange_free(void *buffer) {
     if (!buffer) return ECC_ERR_NULL;
     bufreg_drop(buffer);
     return cudaFree(buffer) == cudaSuccess ? ECC_OK : ECC_ERR_CUDA;
+}
+
+extern "C" int ecc_lse_gather_merge(const float *part_m, const float *part_l, const float *part_o, int64_t rows, int n,
+                                    int hq_local, void *const *peer_buffers, int world, int rank, uint32_t epoch,
+                                    long long wait_cycles, void *out_f16, int flags, ecc_stream_t stream) {
+    if (rows <= 0 || n <= 0 || hq_local <= 0 || rows % hq_local || world < 1 || world > kExchMaxRanks || rank < 0 ||
+        rank >= world || epoch == 0 || wait_cycles <= 0 || rows > 0x7fffffff)
+        return ECC_ERR_SHAPE;
+    if (!part_m || !part_l || !part_o || !peer_buffers || !out_f16) return ECC_ERR_NULL;
+    PeerBufs pb{};
+    // slots [2][world][rows][64 words]: within a buffer made for (rows, world)
+    const size_t need = (size_t)2 * world * rows * kGatherWords * sizeof(unsigned long long);
+    for (int q = 0; q < world; ++q) {
+        if (!peer_buffers[q]) return ECC_ERR_NULL;
+        if ((uintptr_t)peer_buffers[q] % 16) return ECC_ERR_ALIGN;
+        const size_t have = bufreg_get(peer_buffers[q]);
+        if (have == 0 || have < need) return ECC_ERR_SHAPE;
+        pb.base[q] = reinterpret_cast<unsigned long long *>(peer_buffers[q]);
+    }
+    const int grid = ecc_exchange_grid(rows);
+    if (launch_pdl(lse_gather_kernel, dim3(grid), dim3(kD), 0, reinterpret_cast<cudaStream_t>(stream), part_m,
+                   part_l, part_o, n, rows, hq_local, world, rank, pb, epoch, wait_cycles,
+                   reinterpret_cast<__half *>(out_f16), flags & ECC_DECODE_UNROTATE_OUT) != cudaSuccess)
+        return ECC_ERR_LAUNCH;
+    return launch_status();
 }
 
 extern "C" int ecc_lse_exchange_merge(const float *part_m, const float *part_l, const float *part_o, int64_t rows,

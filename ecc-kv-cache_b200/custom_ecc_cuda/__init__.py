@@ -29,7 +29,8 @@ __all__ = [
     "decode_workspace_size", "default_splits", "library_path", "EccError", "compress_calibrated_into",
     "compress_pair_at", "compress_calibrated_at", "decode_attention_dev", "decode_dev_workspace_size",
     "decode_partials_dev", "decode_dev_splits", "exchange_buffer_bytes", "lse_exchange_merge",
-    "exchange_alloc", "exchange_open", "exchange_close", "exchange_free",
+    "exchange_alloc", "exchange_open", "exchange_close", "exchange_free", "lse_gather_merge",
+    "decode_attention_masked",
 ]
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -98,6 +99,8 @@ def _load():
         "ecc_exchange_free": ([p], i32),
         "ecc_lse_exchange_merge": ([p, p, p, i64, i32, p, i32, i32, ctypes.c_uint32, ctypes.c_longlong, p, i32, p],
                                    i32),
+        "ecc_lse_gather_merge": ([p, p, p, i64, i32, i32, p, i32, i32, ctypes.c_uint32, ctypes.c_longlong, p, i32,
+                                  p], i32),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -657,6 +660,34 @@ def lse_exchange_merge(pm: torch.Tensor, pl: torch.Tensor, po: torch.Tensor, pee
                                          int(wait_cycles), _ptr(out), UNROTATE_OUT if unrotate_out else 0,
                                          _stream(pm))
     _check(rc, "lse_exchange_merge")
+    return out
+
+
+def lse_gather_merge(pm: torch.Tensor, pl: torch.Tensor, po: torch.Tensor, peer_ptrs, rank: int, epoch: int,
+                     unrotate_out: bool = False, out: torch.Tensor | None = None,
+                     wait_cycles: int = 10_000_000_000) -> torch.Tensor:
+    """Kv-head-sharded output gather over peer memory: this rank's split
+    partials pm/pl [B, hq_local, n], po [B, hq_local, n, 128] are merged into
+    its fp16 output rows, which are stored into every rank's buffer
+    (``peer_ptrs`` as for lse_exchange_merge); the result out [B, W*hq_local,
+    1, 128] holds every rank's heads (rank q's at heads q*hq_local ..) -- what
+    lse_merge and an all-gather of the outputs give, in one kernel.
+    ``epoch``: 1, 2, ... in step on every rank."""
+    rows, n = _check_partials(pm, pl, po)
+    if pm.dim() != 3:
+        raise RuntimeError("partials must be [B, hq_local, n]")
+    B, hq_l = pm.shape[0], pm.shape[1]
+    W = len(peer_ptrs)
+    if out is None:
+        out = torch.empty((B, W * hq_l, 1, D), dtype=torch.float16, device=pm.device)
+    elif not out.is_contiguous() or out.dtype != torch.float16 or out.numel() != B * W * hq_l * D:
+        raise RuntimeError("out must be a contiguous float16 tensor of B*W*hq_local*128 elements")
+    arr = (ctypes.c_void_p * W)(*[int(x) for x in peer_ptrs])
+    with torch.cuda.device(pm.device):
+        rc = _lib.ecc_lse_gather_merge(_ptr(pm), _ptr(pl), _ptr(po), rows, n, hq_l, arr, W, int(rank), int(epoch),
+                                       int(wait_cycles), _ptr(out), UNROTATE_OUT if unrotate_out else 0,
+                                       _stream(pm))
+    _check(rc, "lse_gather_merge")
     return out
 
 

@@ -4,7 +4,10 @@
 * **kv-head sharding** (``mode="kv"``): rank r holds kv heads
   [r*Hkv/N, (r+1)*Hkv/N) of every sequence and serves their query heads.
   Attention needs no exchange; one all-gather of the ranks' fp16 outputs
-  assembles the layer's attention output [B, Hq, 1, 128].
+  assembles the layer's attention output [B, Hq, 1, 128].  With
+  ``exchange="p2p"`` the merge of the split partials and that all-gather are
+  one kernel per rank that stores its output rows straight into every rank's
+  buffer over NVLink.
 * **sequence-chunk sharding** (``mode="seq"``): rank r holds tokens
   [r*L/N, (r+1)*L/N) of every (sequence, kv head) row; new tokens are
   appended on the last rank.  Each rank computes split partials (m, l, o) of
@@ -121,6 +124,25 @@ class PeerExchange:
             self._raise_on_status(self.ops.device_status())
         return res
 
+    def gather(self, pm: torch.Tensor, pl: torch.Tensor, po: torch.Tensor, unrotate_out: bool = True,
+               out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Kv-head sharding: merge this rank's partials of its query heads and
+        all-gather the fp16 outputs in one kernel (lse_gather_merge); ``out``
+        [B, W*hq_local, 1, 128].  Shares the epoch sequence of ``merge``."""
+        if not self.ptrs:
+            raise RuntimeError("the exchange is closed")
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("the peer exchange cannot be recorded in a CUDA graph (use exchange='nccl')")
+        if pm.dim() != 3 or pm.shape[0] * pm.shape[1] != self.rows:
+            raise RuntimeError(f"the exchange was made for {self.rows} rows, got partials of shape {tuple(pm.shape)}")
+        self.epoch = self.epoch % 0xFFFFFFFE + 1
+        res = self.ops.lse_gather_merge(pm, pl, po, self.ptrs, self.rank, self.epoch, unrotate_out=unrotate_out,
+                                        out=out)
+        self.calls += 1
+        if self.check_every > 0 and self.calls % self.check_every == 0:
+            self._raise_on_status(self.ops.device_status())
+        return res
+
     def _raise_on_status(self, status: int) -> None:
         if status != 0:
             raise RuntimeError(f"rank {self.rank}: the peer exchange reported device status {status} (a wait for "
@@ -150,9 +172,11 @@ class ShardedDecode:
     custom_ecc_cuda: decode_attention, decode_partials, lse_merge_to_record,
     lse_merge_records, RECORD_FLOATS).  Buffers for the exchange are made on
     first use and reused, so a steady decode loop allocates nothing.
-    ``exchange`` (seq mode): "nccl" (all-gather of the records between two
-    merge kernels) or "p2p" (one kernel over peer memory, PeerExchange; GPUs
-    of one node, not inside a CUDA graph).
+    ``exchange``: "nccl" (seq mode: all-gather of the records between two
+    merge kernels; kv mode: all-gather of the fp16 outputs) or "p2p" (one
+    kernel over peer memory, PeerExchange: seq mode merges and exchanges the
+    records, kv mode merges and gathers the outputs; GPUs of one node, not
+    inside a CUDA graph -- with device-side lengths kv mode takes NCCL).
     """
 
     def __init__(self, mode: str, group=None, ops=None, exchange: str = "nccl"):
@@ -170,6 +194,14 @@ class ShardedDecode:
         self.world = dist.get_world_size(self.group)
         self.rank = dist.get_rank(self.group)
         self._bufs: dict = {}
+
+    def _ensure_peer(self, rows: int, device: torch.device) -> None:
+        if self._peer is None or self._peer.rows != rows:
+            if self._peer is not None:
+                # every rank switches at the same step: release the old
+                # buffers collectively before making the new ones
+                self._peer.close()
+            self._peer = PeerExchange(rows, self.group, device, ops=self.ops)
 
     def _buf(self, key, shape, dtype, device):
         b = self._bufs.get(key)
@@ -198,6 +230,18 @@ class ShardedDecode:
         custom_ecc_cuda.decode_dev_splits(B, Hkv, pool capacity))."""
         ops, W = self.ops, self.world
         B, hq_l = query.shape[0], query.shape[1]
+        if self.mode == "kv" and self.exchange == "p2p" and seq_len_dev is None:
+            # partials of this rank's heads, then one kernel: merge + output
+            # all-gather over peer memory
+            splits = ops.default_splits(B, k_pool.shape[-3], local_len)
+            pm, pl, po = ops.decode_partials(query, k_pool, v_pool, seq_len=local_len, num_splits=splits,
+                                             rotate_q=rotate_q)
+            if mark is not None:
+                mark.record()
+            if out is None:
+                out = torch.empty((B, W * hq_l, 1, D), dtype=torch.float16, device=query.device)
+            self._ensure_peer(B * hq_l, query.device)
+            return self._peer.gather(pm, pl, po, unrotate_out=unrotate_out, out=out)
         if self.mode == "kv":
             loc = self._buf("loc", (B, hq_l, 1, D), torch.float16, query.device)
             if seq_len_dev is not None:
@@ -239,12 +283,7 @@ class ShardedDecode:
         if self.exchange == "p2p":
             if mark is not None:
                 mark.record()
-            if self._peer is None or self._peer.rows != B * hq_l:
-                if self._peer is not None:
-                    # every rank switches at the same step: release the old
-                    # buffers collectively before making the new ones
-                    self._peer.close()
-                self._peer = PeerExchange(B * hq_l, self.group, query.device, ops=ops)
+            self._ensure_peer(B * hq_l, query.device)
             return self._peer.merge(pm, pl, po, unrotate_out=unrotate_out, out=out)
         rec = self._buf("rec", (B, hq_l, ops.RECORD_FLOATS), torch.float32, query.device)
         ops.lse_merge_to_record(pm, pl, po, out=rec)

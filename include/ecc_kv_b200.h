@@ -317,6 +317,26 @@ int ecc_lse_exchange_merge(const float *part_m, const float *part_l, const float
                            void *const *peer_buffers, int world, int rank, uint32_t epoch, long long wait_cycles,
                            void *out_f16, int flags, ecc_stream_t stream);
 
+/* Output gather over peer memory, for decode sharded by kv head over the GPUs
+ * of one node (no counterpart in the reference, which runs on one GPU): the
+ * merge of this rank's split partials (ecc_lse_merge) and the all-gather of
+ * the ranks' fp16 outputs as one kernel per rank and step.  Rank s serves
+ * query heads [s*hq_local, (s+1)*hq_local) of every sequence.
+ *   part_m/l/o: this rank's n split partials of rows = B * hq_local rows
+ *     (layout of ecc_lse_merge);
+ *   peer_buffers, world, rank, epoch, wait_cycles: as for
+ *     ecc_lse_exchange_merge; the buffers must hold 2 * world * rows * 512
+ *     bytes (a buffer from ecc_exchange_alloc(rows, world) does), else
+ *     ECC_ERR_SHAPE;
+ *   out: [B, world * hq_local, 128] fp16, the whole attention output of the
+ *     step on every rank; flags may hold ECC_DECODE_UNROTATE_OUT.
+ * Every rank must make the same sequence of calls (with ecc_lse_exchange_merge
+ * calls they share one epoch sequence) with the same rows.  A wait that runs
+ * out raises the ecc_device_status flag (4). */
+int ecc_lse_gather_merge(const float *part_m, const float *part_l, const float *part_o, int64_t rows, int n,
+                         int hq_local, void *const *peer_buffers, int world, int rank, uint32_t epoch,
+                         long long wait_cycles, void *out_f16, int flags, ecc_stream_t stream);
+
 /* Bytes of the library-owned device array ecc_decode_static uses for its
  * split partials (4 MiB on every GPU that loads the library, kept until the
  * process exits). */

@@ -3,8 +3,8 @@ on the GPU.  One GPU: with one rank the kernel's merge equals
 lse_merge_to_record + lse_merge_records bit for bit over successive epochs
 (both buffer halves), and a wait for a rank that never stores gives up,
 raises the device flag and leaves the GPU usable.  Two GPUs (skipped with
-fewer): sequence-sharded decode steps with the p2p exchange equal those with
-the NCCL all-gather bit for bit."""
+fewer): sequence-sharded and kv-head-sharded decode steps with the p2p
+exchange equal those with the NCCL all-gather bit for bit."""
 import os
 import socket
 
@@ -103,6 +103,20 @@ def test_wait_for_missing_rank_gives_up(ops, cuda_device):
         assert torch.equal(got.reshape(ref.shape), ref)
 
 
+@pytest.mark.parametrize("B,hq_l,n", [(8, 4, 29), (2, 16, 5)])
+def test_single_rank_gather_equals_merge(ops, cuda_device, B, hq_l, n):
+    """With one rank the fused merge + output gather is lse_merge, bit for bit."""
+    rows = B * hq_l
+    with _Buffers(ops, cuda_device, rows, 1, 1) as bufs:
+        for epoch in range(1, 4):
+            pm, pl, po = _partials(B, hq_l, n, epoch, cuda_device)
+            unrot = bool(epoch & 1)
+            ref = ops.lse_merge(pm, pl, po, unrotate_out=unrot)
+            got = ops.lse_gather_merge(pm, pl, po, bufs, 0, epoch, unrotate_out=unrot)
+            assert torch.equal(got.reshape(ref.shape), ref), epoch
+    assert ops.device_status() == 0
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -135,9 +149,23 @@ def _two_gpu_worker(rank, world, port):
             assert torch.equal(a, b), (rank, step)
             if rank == world - 1:  # the last rank's chunk grows
                 ops.compress_into(torch.randn(B, hkv, 1, D, device=dev, generator=g).half(), kp, pos=n0 + step)
+        # kv-head sharding: each rank serves its hq/world query heads over its
+        # own pools; the fused merge + output gather equals lse_merge + the
+        # NCCL all-gather bit for bit, and every rank ends with the whole output
+        kref, kp2p = ShardedDecode("kv"), ShardedDecode("kv", exchange="p2p")
+        hq_l = hq // world
+        for step in range(4):
+            q = torch.randn(B, hq, 1, D, generator=torch.Generator().manual_seed(50 + step)).half()
+            q_l = q[:, rank * hq_l:(rank + 1) * hq_l].contiguous().to(dev)
+            a = kref.step(q_l, kp, vp, n0 + step)
+            b = kp2p.step(q_l, kp, vp, n0 + step)
+            assert a.shape == (B, hq, 1, D) and torch.equal(a, b), (rank, step)
+            own = ops.decode_attention(q_l, kp, vp, seq_len=n0 + step, rotate_q=True, unrotate_out=True)
+            assert torch.equal(b[:, rank * hq_l:(rank + 1) * hq_l], own)
         torch.cuda.synchronize()
         assert ops.device_status() == 0
         p2p._peer.close()
+        kp2p._peer.close()
     finally:
         dist.destroy_process_group()
 
