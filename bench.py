@@ -422,14 +422,14 @@ def run_ours(args):
     def local_len(seq_len):
         return seq_len - toks[0] if grows else toks[1] - toks[0]
 
-    def step(i, seq_len, q=None, nk=None, nv=None, dst=None, events=None):
+    def step(i, seq_len, q=None, nk=None, nv=None, dst=None, events=None, append=True):
         """Append step i's token (at global position seq_len - 1), then
         decode at context length seq_len; the output lands in dst."""
         q = qs[i] if q is None else q
         nk = new_k[i] if nk is None else nk
         nv = new_v[i] if nv is None else nv
         dst = out if dst is None else dst
-        if grows:
+        if grows and append:
             ops.compress_pair_into(nk, nv, kpool, vpool, pos=local_len(seq_len) - 1, rotate=True)
         if events is not None:
             events[0].record(stream)
@@ -467,8 +467,9 @@ def run_ours(args):
         step(i, seq)
     barrier()
 
-    # ---- timed region: K device-resident steps ----
-    ev = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(K)]
+    # ---- timed region: K device-resident steps.  No event inside: an event
+    # between two launches would keep the next kernel from starting early
+    # (programmatic dependent launch) ----
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     seq0 = seq
     barrier()
@@ -476,17 +477,27 @@ def run_ours(args):
     start.record(stream)
     for i in range(K):
         seq += 1
-        step(W + i, seq, events=ev[i])
-        ev[i][2].record(stream)
+        step(W + i, seq)
     stop.record(stream)
     barrier()
     clk.mark_stop()
     clk.__exit__(None, None, None)
     total_ms = max_over_ranks(start.elapsed_time(stop))
-    dec_ms = sum(a.elapsed_time(b) for a, b, _ in ev) / K
-    xch_ms = sum(b.elapsed_time(c) for _, b, c in ev) / K if world > 1 else 0.0
     final = out.clone()
     final_seq = seq
+
+    # ---- per-launch times for the roofline and the exchange: the same K
+    # decode steps again (same lengths and queries, the tokens already
+    # appended), one event pair around this rank's attention launches and one
+    # more after the exchange ----
+    ev = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(K)]
+    barrier()
+    for i in range(K):
+        step(W + i, seq0 + 1 + i, events=ev[i], append=False)
+        ev[i][2].record(stream)
+    barrier()
+    dec_ms = sum(a.elapsed_time(b) for a, b, _ in ev) / K
+    xch_ms = sum(b.elapsed_time(c) for _, b, c in ev) / K if world > 1 else 0.0
 
     mean_ctx = seq0 + (K + 1) / 2.0
     job_bytes_per_step = B * HKV * mean_ctx * 2 * rb
@@ -616,9 +627,11 @@ def run_ours(args):
                          "frac": achieved / peak,
                          "traffic": DECODE_DRAM_BYTES_PER_UNIT * rank_units if rb == BLOCK else None,
                          "note": f"rank 0's decode (split partials + merge) per step: {2 * rb} B per (token, kv "
-                                 f"head), {rank_units:.0f} units; traffic from ncu (per launch of the decode "
-                                 f"kernel); peak {peak_kind}"},
-            "rank0_ms": {"append_to_attention_end": dec_ms, "exchange": xch_ms},
+                                 f"head), {rank_units:.0f} units, timed per launch with CUDA events in a second "
+                                 f"pass over the timed steps; traffic from ncu (per launch of the decode kernel); "
+                                 f"peak {peak_kind}"},
+            "rank0_ms": {"attention": dec_ms, "exchange": xch_ms,
+                         "note": "per step, CUDA events around each launch in a second pass over the same steps"},
             "gpu_launches": K * launches_per_step[mode],
             "clocks": clocks, "e2e": e2e, "compress": comp, "cpu_baseline": cpu, "parity": parity,
         }
