@@ -428,14 +428,14 @@ struct Lane {
             p1[e] = ex2(s1[e] - mb[e]);
             p1[2 + e] = ex2(s1[2 + e] - mb[e]);
         }
-        if (corr[0] != 1.0f || corr[1] != 1.0f) {
+        // unconditional rescale (32 multiplies): no branch in the middle of
+        // the stage, so the compiler schedules the whole stage as one block
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                o[i][0] *= corr[0];
-                o[i][1] *= corr[1];
-                o[i][2] *= corr[0];
-                o[i][3] *= corr[1];
-            }
+        for (int i = 0; i < 8; ++i) {
+            o[i][0] *= corr[0];
+            o[i][1] *= corr[1];
+            o[i][2] *= corr[0];
+            o[i][3] *= corr[1];
         }
         const VRaw v1 = load_v(st + kOffVC + kSubC, st + kOffVS + kSubS);
         {
