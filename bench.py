@@ -47,12 +47,12 @@ COMPRESS_TOKENS = 131072
 
 # DRAM bytes per unit measured with ncu (dram__bytes_read.sum +
 # dram__bytes_write.sum of one launch of the decode kernel at B8 x 8 kv heads x
-# 65531 tokens, and of one compress launch of 8 x 131072 vectors, divided by the
+# 65541 tokens, and of one compress launch of 8 x 131072 vectors, divided by the
 # units each processed).
 # Decode: per (token, kv head), algorithmic 256 B.  Compress: per vector,
 # algorithmic 384 B; the output blocks of a launch partly stay in the 126 MB L2
 # when the launch ends, so DRAM writes are counted below 128 B per vector.
-DECODE_DRAM_BYTES_PER_UNIT = (1.073872e9 + 3.862016e6) / (B * HKV * 65531)
+DECODE_DRAM_BYTES_PER_UNIT = (1.074417e9 + 6.3168e6) / (B * HKV * 65541)
 COMPRESS_DRAM_BYTES_PER_VECTOR = (268.652032e6 + 97.288704e6) / (HKV * COMPRESS_TOKENS)
 
 
