@@ -469,15 +469,34 @@ def run_ours(args):
 
     # ---- timed region: K device-resident steps.  No event inside: an event
     # between two launches would keep the next kernel from starting early
-    # (programmatic dependent launch) ----
+    # (programmatic dependent launch).  With --graph the K steps are recorded
+    # once as a CUDA graph (the same launches, lengths baked into each) and
+    # the timed region is one replay: no host work per step ----
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     seq0 = seq
+    graph = None
+    if args.graph:
+        # workspaces for the longest step exist before the capture
+        ops._workspace(dev, ops.decode_workspace_size(B, hq_l, hkv_l, local_len(seq0 + K) + 64, 0) + (1 << 20))
+        barrier()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            s_ = seq0
+            for i in range(K):
+                s_ += 1
+                step(W + i, s_)
     barrier()
     clk.mark_start()
     start.record(stream)
-    for i in range(K):
-        seq += 1
-        step(W + i, seq)
+    h0 = time.perf_counter()
+    if graph is not None:
+        graph.replay()
+        seq += K
+    else:
+        for i in range(K):
+            seq += 1
+            step(W + i, seq)
+    host_ms = (time.perf_counter() - h0) * 1e3 / K  # host time to issue one step
     stop.record(stream)
     barrier()
     clk.mark_stop()
@@ -630,9 +649,11 @@ def run_ours(args):
                                  f"head), {rank_units:.0f} units, timed per launch with CUDA events in a second "
                                  f"pass over the timed steps; traffic from ncu (per launch of the decode kernel); "
                                  f"peak {peak_kind}"},
-            "rank0_ms": {"attention": dec_ms, "exchange": xch_ms,
-                         "note": "per step, CUDA events around each launch in a second pass over the same steps"},
-            "gpu_launches": K * launches_per_step[mode],
+            "rank0_ms": {"attention": dec_ms, "exchange": xch_ms, "host_issue": host_ms,
+                         "note": "per step: attention and exchange by CUDA events around each launch in a second "
+                                 "pass over the same steps; host_issue = host wall time to issue one step in the "
+                                 "timed loop (a step is host-bound when it is not below ms_per_step)"},
+            "gpu_launches": K * launches_per_step[mode], "cuda_graph": bool(args.graph),
             "clocks": clocks, "e2e": e2e, "compress": comp, "cpu_baseline": cpu, "parity": parity,
         }
         if world > 1:
@@ -646,6 +667,7 @@ def run_ours(args):
         if comp:
             line["compress_tok_s"] = comp["tok_s"]
         print(json.dumps(line), flush=True)
+    del graph  # a graph holding NCCL work is released before the process group
     if world > 1:
         import torch.distributed as dist
         torch.cuda.synchronize()
@@ -996,7 +1018,8 @@ def main():
     ap.add_argument("--long", choices=["kv", "seq"], default=None,
                     help="long-context decode (B16, 131072 tokens) sharded by kv head or by sequence chunk")
     ap.add_argument("--graph", action="store_true",
-                    help="with --long: every step one CUDA-graph replay (device-side lengths)")
+                    help="decode benchmark: the K timed steps recorded once as a CUDA graph and replayed; with "
+                         "--long: every step one CUDA-graph replay (device-side lengths)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

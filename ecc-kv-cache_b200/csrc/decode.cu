@@ -366,15 +366,39 @@ __device__ __forceinline__ float await_word(const unsigned long long *p, unsigne
     return __uint_as_float((uint32_t)w);
 }
 
+// Epoch of an exchange call.  Host epochs come as a kernel argument.  With a
+// device-side epoch state {counter, done} (calls recorded in a CUDA graph,
+// whose arguments are fixed) the epoch is counter % (2^32 - 2) + 1, read after
+// the previous kernel: never 0, consecutive calls alternate parity (the
+// buffer half).  The last CTA to finish advances the counter -- every CTA
+// read it before it counts itself done -- so the next call, ordered after
+// this kernel, gets the next epoch.
+__device__ __forceinline__ uint32_t call_epoch(uint32_t epoch, const unsigned long long *state) {
+    if (!state) return epoch;
+    return (uint32_t)(*reinterpret_cast<const volatile unsigned long long *>(state) % 0xFFFFFFFEull) + 1u;
+}
+__device__ __forceinline__ void advance_epoch(unsigned long long *state) {
+    if (!state) return;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(state + 1, 1ull) == (unsigned long long)gridDim.x - 1ull) {
+            state[1] = 0ull;
+            atomicAdd(state, 1ull);
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kD)
 lse_exchange_kernel(const float *__restrict__ pm, const float *__restrict__ pl, const float *__restrict__ po, int n,
-                    int64_t rows, int W, int rank, PeerBufs peers, uint32_t epoch, long long wait_cycles,
-                    __half *__restrict__ out, int flags) {
+                    int64_t rows, int W, int rank, PeerBufs peers, uint32_t epoch_arg, unsigned long long *estate,
+                    long long wait_cycles, __half *__restrict__ out, int flags) {
     __shared__ float sh[kD];
     __shared__ float s_m[kExchMaxRanks], s_l[kExchMaxRanks];
     const int d = threadIdx.x;
-    const int64_t half = epoch & 1u;
     pdl_wait();  // the partials of the kernel before
+    const uint32_t epoch = call_epoch(epoch_arg, estate);
+    const int64_t half = epoch & 1u;
     // 1. this rank's record of each row, stored into every rank's buffer
     for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
         float M, L, O;
@@ -431,6 +455,7 @@ lse_exchange_kernel(const float *__restrict__ pm, const float *__restrict__ pl, 
         __syncthreads();  // s_m, s_l are refilled for the next row
         write_out(L, O, out, r, d, flags, sh);
     }
+    advance_epoch(estate);
 }
 
 // ---------------------------------------------------------------------------
@@ -453,12 +478,13 @@ constexpr int kGatherWords = kD / 2;
 
 __global__ void __launch_bounds__(kD)
 lse_gather_kernel(const float *__restrict__ pm, const float *__restrict__ pl, const float *__restrict__ po, int n,
-                  int64_t rows, int hq_l, int W, int rank, PeerBufs peers, uint32_t epoch, long long wait_cycles,
-                  __half *__restrict__ out, int flags) {
+                  int64_t rows, int hq_l, int W, int rank, PeerBufs peers, uint32_t epoch_arg,
+                  unsigned long long *estate, long long wait_cycles, __half *__restrict__ out, int flags) {
     __shared__ float sh[kD];
     const int d = threadIdx.x;
-    const int64_t half = epoch & 1u;
     pdl_wait();  // the partials of the kernel before
+    const uint32_t epoch = call_epoch(epoch_arg, estate);
+    const int64_t half = epoch & 1u;
     const unsigned long long *mine = peers.base[rank] + half * W * rows * kGatherWords;
     const long long t0 = clock64();
     bool ok = true;
@@ -499,6 +525,7 @@ lse_gather_kernel(const float *__restrict__ pm, const float *__restrict__ pl, co
         }
         __syncthreads();  // sh is refilled for the next row
     }
+    advance_epoch(estate);
 }
 
 int exchange_device_error(int reset) {
@@ -973,56 +1000,93 @@ extern "C" int ecc_exchange_free(void *buffer) {
     return cudaFree(buffer) == cudaSuccess ? ECC_OK : ECC_ERR_CUDA;
 }
 
-extern "C" int ecc_lse_gather_merge(const float *part_m, const float *part_l, const float *part_o, int64_t rows, int n,
-                                    int hq_local, void *const *peer_buffers, int world, int rank, uint32_t epoch,
-                                    long long wait_cycles, void *out_f16, int flags, ecc_stream_t stream) {
-    if (rows <= 0 || n <= 0 || hq_local <= 0 || rows % hq_local || world < 1 || world > kExchMaxRanks || rank < 0 ||
-        rank >= world || epoch == 0 || wait_cycles <= 0 || rows > 0x7fffffff)
-        return ECC_ERR_SHAPE;
-    if (!part_m || !part_l || !part_o || !peer_buffers || !out_f16) return ECC_ERR_NULL;
-    PeerBufs pb{};
-    // slots [2][world][rows][64 words]: within a buffer made for (rows, world)
-    const size_t need = (size_t)2 * world * rows * kGatherWords * sizeof(unsigned long long);
+// Peer pointers of an exchange call, each checked against the registry: a
+// buffer this process allocated or mapped, of at least `need` bytes (the
+// stores would otherwise land past its end, in another GPU's memory).
+static int peer_table(void *const *peer_buffers, int world, size_t need, PeerBufs *pb) {
     for (int q = 0; q < world; ++q) {
         if (!peer_buffers[q]) return ECC_ERR_NULL;
         if ((uintptr_t)peer_buffers[q] % 16) return ECC_ERR_ALIGN;
         const size_t have = bufreg_get(peer_buffers[q]);
         if (have == 0 || have < need) return ECC_ERR_SHAPE;
-        pb.base[q] = reinterpret_cast<unsigned long long *>(peer_buffers[q]);
+        pb->base[q] = reinterpret_cast<unsigned long long *>(peer_buffers[q]);
     }
+    return ECC_OK;
+}
+
+// Host epoch (epoch >= 1, state null) or device-side epoch state (epoch 0).
+static int gather_merge(const float *part_m, const float *part_l, const float *part_o, int64_t rows, int n,
+                        int hq_local, void *const *peer_buffers, int world, int rank, uint32_t epoch,
+                        uint64_t *state, long long wait_cycles, void *out_f16, int flags, ecc_stream_t stream) {
+    if (rows <= 0 || n <= 0 || hq_local <= 0 || rows % hq_local || world < 1 || world > kExchMaxRanks || rank < 0 ||
+        rank >= world || (epoch == 0) == (state == nullptr) || wait_cycles <= 0 || rows > 0x7fffffff)
+        return ECC_ERR_SHAPE;
+    if (!part_m || !part_l || !part_o || !peer_buffers || !out_f16) return ECC_ERR_NULL;
+    if ((uintptr_t)state % 8) return ECC_ERR_ALIGN;
+    PeerBufs pb{};
+    // slots [2][world][rows][64 words]: within a buffer made for (rows, world)
+    const int rc = peer_table(peer_buffers, world, (size_t)2 * world * rows * kGatherWords * 8, &pb);
+    if (rc != ECC_OK) return rc;
     const int grid = ecc_exchange_grid(rows);
     if (launch_pdl(lse_gather_kernel, dim3(grid), dim3(kD), 0, reinterpret_cast<cudaStream_t>(stream), part_m,
-                   part_l, part_o, n, rows, hq_local, world, rank, pb, epoch, wait_cycles,
-                   reinterpret_cast<__half *>(out_f16), flags & ECC_DECODE_UNROTATE_OUT) != cudaSuccess)
+                   part_l, part_o, n, rows, hq_local, world, rank, pb, epoch,
+                   reinterpret_cast<unsigned long long *>(state), wait_cycles, reinterpret_cast<__half *>(out_f16),
+                   flags & ECC_DECODE_UNROTATE_OUT) != cudaSuccess)
         return ECC_ERR_LAUNCH;
     return launch_status();
+}
+
+static int exchange_merge(const float *part_m, const float *part_l, const float *part_o, int64_t rows, int n,
+                          void *const *peer_buffers, int world, int rank, uint32_t epoch, uint64_t *state,
+                          long long wait_cycles, void *out_f16, int flags, ecc_stream_t stream) {
+    if (rows <= 0 || n <= 0 || world < 1 || world > kExchMaxRanks || rank < 0 || rank >= world ||
+        (epoch == 0) == (state == nullptr) || wait_cycles <= 0 || rows > 0x7fffffff)
+        return ECC_ERR_SHAPE;
+    if (!part_m || !part_l || !part_o || !peer_buffers || !out_f16) return ECC_ERR_NULL;
+    if ((uintptr_t)state % 8) return ECC_ERR_ALIGN;
+    PeerBufs pb{};
+    const int rc = peer_table(peer_buffers, world, ecc_exchange_buffer_bytes(rows, world), &pb);
+    if (rc != ECC_OK) return rc;
+    const int grid = ecc_exchange_grid(rows);
+    // a programmatic dependent of the previous kernel; it never triggers its
+    // own dependents, so none starts before it ends
+    if (launch_pdl(lse_exchange_kernel, dim3(grid), dim3(kD), 0, reinterpret_cast<cudaStream_t>(stream), part_m,
+                   part_l, part_o, n, rows, world, rank, pb, epoch, reinterpret_cast<unsigned long long *>(state),
+                   wait_cycles, reinterpret_cast<__half *>(out_f16), flags & ECC_DECODE_UNROTATE_OUT) != cudaSuccess)
+        return ECC_ERR_LAUNCH;
+    return launch_status();
+}
+
+extern "C" int ecc_lse_gather_merge(const float *part_m, const float *part_l, const float *part_o, int64_t rows, int n,
+                                    int hq_local, void *const *peer_buffers, int world, int rank, uint32_t epoch,
+                                    long long wait_cycles, void *out_f16, int flags, ecc_stream_t stream) {
+    if (epoch == 0) return ECC_ERR_SHAPE;
+    return gather_merge(part_m, part_l, part_o, rows, n, hq_local, peer_buffers, world, rank, epoch, nullptr,
+                        wait_cycles, out_f16, flags, stream);
+}
+
+extern "C" int ecc_lse_gather_merge_dev(const float *part_m, const float *part_l, const float *part_o, int64_t rows,
+                                        int n, int hq_local, void *const *peer_buffers, int world, int rank,
+                                        uint64_t *epoch_state, long long wait_cycles, void *out_f16, int flags,
+                                        ecc_stream_t stream) {
+    if (!epoch_state) return ECC_ERR_NULL;
+    return gather_merge(part_m, part_l, part_o, rows, n, hq_local, peer_buffers, world, rank, 0, epoch_state,
+                        wait_cycles, out_f16, flags, stream);
 }
 
 extern "C" int ecc_lse_exchange_merge(const float *part_m, const float *part_l, const float *part_o, int64_t rows,
                                       int n, void *const *peer_buffers, int world, int rank, uint32_t epoch,
                                       long long wait_cycles, void *out_f16, int flags, ecc_stream_t stream) {
-    if (rows <= 0 || n <= 0 || world < 1 || world > kExchMaxRanks || rank < 0 || rank >= world || epoch == 0 ||
-        wait_cycles <= 0 || rows > 0x7fffffff)
-        return ECC_ERR_SHAPE;
-    if (!part_m || !part_l || !part_o || !peer_buffers || !out_f16) return ECC_ERR_NULL;
-    PeerBufs pb{};
-    const size_t need = ecc_exchange_buffer_bytes(rows, world);
-    for (int q = 0; q < world; ++q) {
-        if (!peer_buffers[q]) return ECC_ERR_NULL;
-        if ((uintptr_t)peer_buffers[q] % 16) return ECC_ERR_ALIGN;
-        // every buffer must be one this process allocated or mapped, and large
-        // enough for this call's rows and world (the stores would otherwise
-        // land past its end, in another GPU's memory)
-        const size_t have = bufreg_get(peer_buffers[q]);
-        if (have == 0 || have < need) return ECC_ERR_SHAPE;
-        pb.base[q] = reinterpret_cast<unsigned long long *>(peer_buffers[q]);
-    }
-    const int grid = ecc_exchange_grid(rows);
-    // a programmatic dependent of the previous kernel; it never triggers its
-    // own dependents, so none starts before it ends
-    if (launch_pdl(lse_exchange_kernel, dim3(grid), dim3(kD), 0, reinterpret_cast<cudaStream_t>(stream), part_m,
-                   part_l, part_o, n, rows, world, rank, pb, epoch, wait_cycles,
-                   reinterpret_cast<__half *>(out_f16), flags & ECC_DECODE_UNROTATE_OUT) != cudaSuccess)
-        return ECC_ERR_LAUNCH;
-    return launch_status();
+    if (epoch == 0) return ECC_ERR_SHAPE;
+    return exchange_merge(part_m, part_l, part_o, rows, n, peer_buffers, world, rank, epoch, nullptr, wait_cycles,
+                          out_f16, flags, stream);
+}
+
+extern "C" int ecc_lse_exchange_merge_dev(const float *part_m, const float *part_l, const float *part_o,
+                                          int64_t rows, int n, void *const *peer_buffers, int world, int rank,
+                                          uint64_t *epoch_state, long long wait_cycles, void *out_f16, int flags,
+                                          ecc_stream_t stream) {
+    if (!epoch_state) return ECC_ERR_NULL;
+    return exchange_merge(part_m, part_l, part_o, rows, n, peer_buffers, world, rank, 0, epoch_state, wait_cycles,
+                          out_f16, flags, stream);
 }

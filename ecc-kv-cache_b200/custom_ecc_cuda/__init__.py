@@ -101,6 +101,8 @@ def _load():
                                    i32),
         "ecc_lse_gather_merge": ([p, p, p, i64, i32, i32, p, i32, i32, ctypes.c_uint32, ctypes.c_longlong, p, i32,
                                   p], i32),
+        "ecc_lse_exchange_merge_dev": ([p, p, p, i64, i32, p, i32, i32, p, ctypes.c_longlong, p, i32, p], i32),
+        "ecc_lse_gather_merge_dev": ([p, p, p, i64, i32, i32, p, i32, i32, p, ctypes.c_longlong, p, i32, p], i32),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -647,7 +649,9 @@ def lse_exchange_merge(pm: torch.Tensor, pl: torch.Tensor, po: torch.Tensor, pee
     of all ranks' buffers as mapped in this process, ``peer_ptrs[rank]`` this
     rank's own), and the records of all ranks merged into out [..., 128]
     fp16 -- what lse_merge_to_record, an all-gather and lse_merge_records
-    give, in one kernel.  ``epoch``: 1, 2, ... in step on every rank."""
+    give, in one kernel.  ``epoch``: 1, 2, ... in step on every rank, or an
+    epoch state (int64 CUDA tensor [2], zero-filled once) that the kernel
+    reads and advances itself, for calls recorded in a CUDA graph."""
     rows, n = _check_partials(pm, pl, po)
     W = len(peer_ptrs)
     if out is None:
@@ -656,11 +660,23 @@ def lse_exchange_merge(pm: torch.Tensor, pl: torch.Tensor, po: torch.Tensor, pee
         raise RuntimeError("out must be a contiguous float16 tensor of rows*128 elements")
     arr = (ctypes.c_void_p * W)(*[int(x) for x in peer_ptrs])
     with torch.cuda.device(pm.device):
-        rc = _lib.ecc_lse_exchange_merge(_ptr(pm), _ptr(pl), _ptr(po), rows, n, arr, W, int(rank), int(epoch),
-                                         int(wait_cycles), _ptr(out), UNROTATE_OUT if unrotate_out else 0,
-                                         _stream(pm))
+        if isinstance(epoch, torch.Tensor):
+            _epoch_state(epoch, pm.device)
+            rc = _lib.ecc_lse_exchange_merge_dev(_ptr(pm), _ptr(pl), _ptr(po), rows, n, arr, W, int(rank),
+                                                 _ptr(epoch), int(wait_cycles), _ptr(out),
+                                                 UNROTATE_OUT if unrotate_out else 0, _stream(pm))
+        else:
+            rc = _lib.ecc_lse_exchange_merge(_ptr(pm), _ptr(pl), _ptr(po), rows, n, arr, W, int(rank), int(epoch),
+                                             int(wait_cycles), _ptr(out), UNROTATE_OUT if unrotate_out else 0,
+                                             _stream(pm))
     _check(rc, "lse_exchange_merge")
     return out
+
+
+def _epoch_state(t: torch.Tensor, device) -> None:
+    if not t.is_cuda or t.dtype != torch.int64 or t.numel() != 2 or not t.is_contiguous() or t.device != device:
+        raise RuntimeError("an epoch state must be a contiguous int64 CUDA tensor of 2 elements on the partials' "
+                           "device")
 
 
 def lse_gather_merge(pm: torch.Tensor, pl: torch.Tensor, po: torch.Tensor, peer_ptrs, rank: int, epoch: int,
@@ -672,7 +688,9 @@ def lse_gather_merge(pm: torch.Tensor, pl: torch.Tensor, po: torch.Tensor, peer_
     (``peer_ptrs`` as for lse_exchange_merge); the result out [B, W*hq_local,
     1, 128] holds every rank's heads (rank q's at heads q*hq_local ..) -- what
     lse_merge and an all-gather of the outputs give, in one kernel.
-    ``epoch``: 1, 2, ... in step on every rank."""
+    ``epoch``: 1, 2, ... in step on every rank, or an epoch state (int64
+    CUDA tensor [2], zero-filled once) that the kernel reads and advances
+    itself, for calls recorded in a CUDA graph."""
     rows, n = _check_partials(pm, pl, po)
     if pm.dim() != 3:
         raise RuntimeError("partials must be [B, hq_local, n]")
@@ -684,9 +702,15 @@ def lse_gather_merge(pm: torch.Tensor, pl: torch.Tensor, po: torch.Tensor, peer_
         raise RuntimeError("out must be a contiguous float16 tensor of B*W*hq_local*128 elements")
     arr = (ctypes.c_void_p * W)(*[int(x) for x in peer_ptrs])
     with torch.cuda.device(pm.device):
-        rc = _lib.ecc_lse_gather_merge(_ptr(pm), _ptr(pl), _ptr(po), rows, n, hq_l, arr, W, int(rank), int(epoch),
-                                       int(wait_cycles), _ptr(out), UNROTATE_OUT if unrotate_out else 0,
-                                       _stream(pm))
+        if isinstance(epoch, torch.Tensor):
+            _epoch_state(epoch, pm.device)
+            rc = _lib.ecc_lse_gather_merge_dev(_ptr(pm), _ptr(pl), _ptr(po), rows, n, hq_l, arr, W, int(rank),
+                                               _ptr(epoch), int(wait_cycles), _ptr(out),
+                                               UNROTATE_OUT if unrotate_out else 0, _stream(pm))
+        else:
+            rc = _lib.ecc_lse_gather_merge(_ptr(pm), _ptr(pl), _ptr(po), rows, n, hq_l, arr, W, int(rank),
+                                           int(epoch), int(wait_cycles), _ptr(out),
+                                           UNROTATE_OUT if unrotate_out else 0, _stream(pm))
     _check(rc, "lse_gather_merge")
     return out
 

@@ -81,7 +81,8 @@ class PeerExchange:
     custom_ecc_cuda.lse_exchange_merge can store into all of them.  Made
     collectively (every rank at the same point); calls of ``merge`` must then
     be made in step on every rank, and ``close`` collectively at the end.
-    Not for CUDA-graph capture: each call's epoch is a kernel argument.
+    The call epochs live in device memory (``state``, advanced by each
+    call's kernel), so calls can be recorded in a CUDA graph and replayed.
 
     A merge whose bounded wait for another rank ran out raises the device
     status flag (4) and leaves its rows unwritten instead of hanging; the flag
@@ -101,7 +102,7 @@ class PeerExchange:
         handles = [None] * self.world
         dist.all_gather_object(handles, handle, group=group)
         self.ptrs = [self.own if q == self.rank else ops.exchange_open(h, device) for q, h in enumerate(handles)]
-        self.epoch = 0
+        self.state = torch.zeros(2, dtype=torch.int64, device=device)  # epoch counter, CTAs done
         self.calls = 0
         self.check_every = int(check_every)
         dist.barrier(group=group)  # every buffer zeroed and mapped before the first call
@@ -110,37 +111,31 @@ class PeerExchange:
               out: Optional[torch.Tensor] = None) -> torch.Tensor:
         if not self.ptrs:
             raise RuntimeError("the exchange is closed")
-        if torch.cuda.is_current_stream_capturing():
-            raise RuntimeError("the peer exchange cannot be recorded in a CUDA graph (use exchange='nccl')")
         if pm.dim() != 3 or pm.shape[0] * pm.shape[1] != self.rows:
             raise RuntimeError(f"the exchange was made for {self.rows} rows, got partials of shape {tuple(pm.shape)}")
-        # epochs run 1 .. 2^32 - 2 and round again (0 is never a valid tag);
-        # the wrap keeps consecutive calls on alternating buffer halves
-        self.epoch = self.epoch % 0xFFFFFFFE + 1
-        res = self.ops.lse_exchange_merge(pm, pl, po, self.ptrs, self.rank, self.epoch, unrotate_out=unrotate_out,
+        res = self.ops.lse_exchange_merge(pm, pl, po, self.ptrs, self.rank, self.state, unrotate_out=unrotate_out,
                                           out=out)
-        self.calls += 1
-        if self.check_every > 0 and self.calls % self.check_every == 0:
-            self._raise_on_status(self.ops.device_status())
+        self._count()
         return res
+
+    def _count(self) -> None:
+        self.calls += 1
+        if (self.check_every > 0 and self.calls % self.check_every == 0
+                and not torch.cuda.is_current_stream_capturing()):
+            self._raise_on_status(self.ops.device_status())
 
     def gather(self, pm: torch.Tensor, pl: torch.Tensor, po: torch.Tensor, unrotate_out: bool = True,
                out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Kv-head sharding: merge this rank's partials of its query heads and
         all-gather the fp16 outputs in one kernel (lse_gather_merge); ``out``
-        [B, W*hq_local, 1, 128].  Shares the epoch sequence of ``merge``."""
+        [B, W*hq_local, 1, 128].  Shares the epoch state of ``merge``."""
         if not self.ptrs:
             raise RuntimeError("the exchange is closed")
-        if torch.cuda.is_current_stream_capturing():
-            raise RuntimeError("the peer exchange cannot be recorded in a CUDA graph (use exchange='nccl')")
         if pm.dim() != 3 or pm.shape[0] * pm.shape[1] != self.rows:
             raise RuntimeError(f"the exchange was made for {self.rows} rows, got partials of shape {tuple(pm.shape)}")
-        self.epoch = self.epoch % 0xFFFFFFFE + 1
-        res = self.ops.lse_gather_merge(pm, pl, po, self.ptrs, self.rank, self.epoch, unrotate_out=unrotate_out,
+        res = self.ops.lse_gather_merge(pm, pl, po, self.ptrs, self.rank, self.state, unrotate_out=unrotate_out,
                                         out=out)
-        self.calls += 1
-        if self.check_every > 0 and self.calls % self.check_every == 0:
-            self._raise_on_status(self.ops.device_status())
+        self._count()
         return res
 
     def _raise_on_status(self, status: int) -> None:
@@ -175,8 +170,8 @@ class ShardedDecode:
     ``exchange``: "nccl" (seq mode: all-gather of the records between two
     merge kernels; kv mode: all-gather of the fp16 outputs) or "p2p" (one
     kernel over peer memory, PeerExchange: seq mode merges and exchanges the
-    records, kv mode merges and gathers the outputs; GPUs of one node, not
-    inside a CUDA graph -- with device-side lengths kv mode takes NCCL).
+    records, kv mode merges and gathers the outputs; GPUs of one node; the
+    epochs live in device memory, so a step can be recorded in a CUDA graph).
     """
 
     def __init__(self, mode: str, group=None, ops=None, exchange: str = "nccl"):
@@ -230,12 +225,21 @@ class ShardedDecode:
         custom_ecc_cuda.decode_dev_splits(B, Hkv, pool capacity))."""
         ops, W = self.ops, self.world
         B, hq_l = query.shape[0], query.shape[1]
-        if self.mode == "kv" and self.exchange == "p2p" and seq_len_dev is None:
+        if self.mode == "kv" and self.exchange == "p2p":
             # partials of this rank's heads, then one kernel: merge + output
             # all-gather over peer memory
-            splits = ops.default_splits(B, k_pool.shape[-3], local_len)
-            pm, pl, po = ops.decode_partials(query, k_pool, v_pool, seq_len=local_len, num_splits=splits,
-                                             rotate_q=rotate_q)
+            hkv_l, cap = k_pool.shape[-3], k_pool.shape[-2]
+            if seq_len_dev is not None:
+                splits = max(num_splits, ops.decode_dev_splits(B, hkv_l, cap))
+                parts = (self._buf("pm", (B, hq_l, splits), torch.float32, query.device),
+                         self._buf("pl", (B, hq_l, splits), torch.float32, query.device),
+                         self._buf("po", (B, hq_l, splits, D), torch.float32, query.device))
+                pm, pl, po = ops.decode_partials_dev(query, k_pool, v_pool, seq_len_dev, splits, rotate_q=rotate_q,
+                                                     out=parts)
+            else:
+                splits = ops.default_splits(B, hkv_l, local_len)
+                pm, pl, po = ops.decode_partials(query, k_pool, v_pool, seq_len=local_len, num_splits=splits,
+                                                 rotate_q=rotate_q)
             if mark is not None:
                 mark.record()
             if out is None:

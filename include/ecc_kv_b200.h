@@ -337,6 +337,23 @@ int ecc_lse_gather_merge(const float *part_m, const float *part_l, const float *
                          int hq_local, void *const *peer_buffers, int world, int rank, uint32_t epoch,
                          long long wait_cycles, void *out_f16, int flags, ecc_stream_t stream);
 
+/* The two peer-memory merges with the epoch in device memory instead of a
+ * kernel argument, so that a step can be recorded once in a CUDA graph and
+ * replayed (no counterpart in the reference).  epoch_state: DEVICE array of
+ * two uint64 {counter, done}, zero-filled once before the first call; the
+ * call's epoch is counter % (2^32 - 2) + 1 and the kernel's last CTA
+ * advances the counter, so successive calls (eager or replayed) take
+ * successive epochs.  Every rank keeps its own state and makes the same
+ * sequence of calls; do not mix these with the host-epoch forms on one set
+ * of buffers.  Other arguments as ecc_lse_exchange_merge /
+ * ecc_lse_gather_merge. */
+int ecc_lse_exchange_merge_dev(const float *part_m, const float *part_l, const float *part_o, int64_t rows, int n,
+                               void *const *peer_buffers, int world, int rank, uint64_t *epoch_state,
+                               long long wait_cycles, void *out_f16, int flags, ecc_stream_t stream);
+int ecc_lse_gather_merge_dev(const float *part_m, const float *part_l, const float *part_o, int64_t rows, int n,
+                             int hq_local, void *const *peer_buffers, int world, int rank, uint64_t *epoch_state,
+                             long long wait_cycles, void *out_f16, int flags, ecc_stream_t stream);
+
 /* Bytes of the library-owned device array ecc_decode_static uses for its
  * split partials (4 MiB on every GPU that loads the library, kept until the
  * process exits). */

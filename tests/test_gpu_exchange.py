@@ -117,6 +117,46 @@ def test_single_rank_gather_equals_merge(ops, cuda_device, B, hq_l, n):
     assert ops.device_status() == 0
 
 
+def test_device_epoch_state_and_graph_replay(ops, cuda_device):
+    """Epochs from a device-side state: each call (eager or replayed from a
+    CUDA graph) takes the next epoch and advances the state itself; results
+    equal the host-epoch merges."""
+    B, hq, n = 2, 8, 7
+    rows = B * hq
+    state = torch.zeros(2, dtype=torch.int64, device=cuda_device)
+    with _Buffers(ops, cuda_device, rows, 1, 2) as (gbuf, xbuf):
+        pm, pl, po = _partials(B, hq, n, 3, cuda_device)
+        ref_g = ops.lse_merge(pm, pl, po, unrotate_out=True)
+        ref_x = ops.lse_merge_records(ops.lse_merge_to_record(pm, pl, po).unsqueeze(0), unrotate_out=True)
+        for _ in range(3):
+            got = ops.lse_gather_merge(pm, pl, po, [gbuf], 0, state, unrotate_out=True)
+            assert torch.equal(got.reshape(ref_g.shape), ref_g)
+        assert state.tolist() == [3, 0]  # counter advanced once per call, done counter reset
+        xstate = torch.zeros(2, dtype=torch.int64, device=cuda_device)
+        out_g = torch.empty((B, hq, 1, D), dtype=torch.float16, device=cuda_device)
+        out_x = torch.empty((B, hq, D), dtype=torch.float16, device=cuda_device)
+        side = torch.cuda.Stream(cuda_device)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):  # warm-up off the capture
+            ops.lse_gather_merge(pm, pl, po, [gbuf], 0, state, unrotate_out=True, out=out_g)
+            ops.lse_exchange_merge(pm, pl, po, [xbuf], 0, xstate, unrotate_out=True, out=out_x)
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            ops.lse_gather_merge(pm, pl, po, [gbuf], 0, state, unrotate_out=True, out=out_g)
+            ops.lse_exchange_merge(pm, pl, po, [xbuf], 0, xstate, unrotate_out=True, out=out_x)
+        for _ in range(5):
+            out_g.zero_()
+            out_x.zero_()
+            graph.replay()
+            assert torch.equal(out_g.reshape(ref_g.shape), ref_g)
+            assert torch.equal(out_x.reshape(ref_x.shape), ref_x)
+        torch.cuda.synchronize()
+        assert state.tolist()[0] == 4 + 5 and xstate.tolist()[0] == 1 + 5
+        del graph
+    assert ops.device_status() == 0
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
