@@ -193,13 +193,14 @@ decode_v1_kernel(const __half *__restrict__ q, const uint8_t *__restrict__ kb, c
 // LSE combine of n partials (m natural-log units, l, unnormalised o) of one
 // row by a 128-thread block, thread d = dim d: M = max over the non-empty
 // partials (l > 0; -inf if none), L and O relative to M.  Partial i is read
-// through src(i) = {m, l, o[d]}.  Partials go in batches of up to 32 and each
-// batch is one memory round trip: every thread issues its o loads of the
-// whole batch together with the batch's (m, l) loads (threads < 32), the
-// batch maximum comes from shared memory, and sums kept under an earlier
-// maximum are rescaled.  With n <= 32 (every split count of one device's
-// default partition up to 32 per row) M is the global maximum and the sums
-// run in partial order.
+// through src(i) = {m, l, o[d]}.  Partials go in batches of up to 32: every
+// thread loads its o of the whole batch at once and threads < 32 the batch's
+// (m, l), the batch maximum comes from shared memory, and sums kept under an
+// earlier maximum are rescaled.  The loads of batch i + 1 are issued before
+// batch i is combined (two register sets), so a row of many partials costs
+// about one memory round trip, not one per batch.  With n <= 32 (every split
+// count of one device's default partition up to 32 per row) M is the global
+// maximum and the sums run in partial order.
 template <class Src>
 __device__ __forceinline__ void lse_combine(int n, int d, const Src &src, float &M, float &L, float &O) {
     constexpr int kBatch = 32;
@@ -207,15 +208,26 @@ __device__ __forceinline__ void lse_combine(int n, int d, const Src &src, float 
     M = -INFINITY;
     L = 0.0f;
     O = 0.0f;
+    float ov[kBatch], mv = 0.0f, lv = 0.0f;
+    auto fetch = [&](int c0, float (&o)[kBatch], float &m, float &l) {
+        const int cn = min(kBatch, n - c0);
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) o[j] = (j < cn) ? src.o(c0 + j, d) : 0.0f;
+        if (d < cn) {
+            m = src.m(c0 + d);
+            l = src.l(c0 + d);
+        }
+    };
+    if (n > 0) fetch(0, ov, mv, lv);
     for (int c0 = 0; c0 < n; c0 += kBatch) {
         const int cn = min(kBatch, n - c0);
-        float ov[kBatch];
-#pragma unroll
-        for (int j = 0; j < kBatch; ++j) ov[j] = (j < cn) ? src.o(c0 + j, d) : 0.0f;
         if (d < cn) {
-            s_m[d] = src.m(c0 + d);
-            s_l[d] = src.l(c0 + d);
+            s_m[d] = mv;
+            s_l[d] = lv;
         }
+        float nv[kBatch];
+        float nm = 0.0f, nl = 0.0f;
+        if (c0 + kBatch < n) fetch(c0 + kBatch, nv, nm, nl);  // block-uniform
         __syncthreads();
         float bm = M;
         for (int j = 0; j < cn; ++j)
@@ -236,6 +248,12 @@ __device__ __forceinline__ void lse_combine(int n, int d, const Src &src, float 
                 }
         }
         __syncthreads();  // the batch's (m, l) slots are refilled next
+        if (c0 + kBatch < n) {
+#pragma unroll
+            for (int j = 0; j < kBatch; ++j) ov[j] = nv[j];
+            mv = nm;
+            lv = nl;
+        }
     }
 }
 

@@ -228,6 +228,81 @@ struct Lane {
     int g, c;
     float scale_log2;
 
+    // Query fragments of a row segment from the lane's fp16 query words qw
+    // (dims 32c..32c+31 of its head): the centroid operand qc, the sign
+    // operand qs with its exponent sgn2, and the per-head sums qsum.
+    __device__ __forceinline__ void set_query(const uint4 (&qw)[4], bool rotate) {
+        float x[32];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t wv[4] = {qw[k].x, qw[k].y, qw[k].z, qw[k].w};
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+                x[8 * k + 2 * m] = h_lo(wv[m]);
+                x[8 * k + 2 * m + 1] = h_hi(wv[m]);
+            }
+        }
+        if (rotate) {  // q_rot = fp16(WHT(q)), like patch.py:106
+#pragma unroll
+            for (int s = 1; s < 32; s <<= 1)
+#pragma unroll
+                for (int k = 0; k < 32; ++k)
+                    if ((k & s) == 0) {
+                        const float a = x[k], bb = x[k + s];
+                        x[k] = __fadd_rn(a, bb);
+                        x[k + s] = __fsub_rn(a, bb);
+                    }
+#pragma unroll
+            for (int s = 1; s <= 2; s <<= 1) {  // strides 32, 64: partner lane c ^ s
+                const float sgn = (c & s) ? -1.0f : 1.0f;
+#pragma unroll
+                for (int k = 0; k < 32; ++k) {
+                    const float p = __shfl_xor_sync(0xffffffffu, x[k], s);
+                    x[k] = __fmaf_rn(sgn, x[k], p);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+                const float v = x[k];
+                const float q0 = __fmul_rn(v, kInvSqrt128);
+                const float rem = __fmaf_rn(-q0, kSqrt128, v);
+                x[k] = __half2float(__float2half_rn(__fmaf_rn(rem, kInvSqrt128, q0)));
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+            qc[m][0] = pack_h2(x[4 * m], x[4 * m + 1]);
+            qc[m][1] = pack_h2(x[4 * m + 2], x[4 * m + 3]);
+        }
+        // sign-product operand: scale 2^-ssh keeps q * 2^(14 - ssh) < 2^15
+        // for the largest |q| of the group (q is fp16, the scalings are
+        // exact powers of two)
+        {
+            float qmax = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 32; ++k) qmax = fmaxf(qmax, fabsf(x[k]));
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, off));
+            const int e2 = (qmax > 0.0f) ? ((__float_as_int(qmax) >> 23) & 0xff) - 127 : 0;
+            const int ssh = max(0, e2);
+            sgn2 = __int_as_float((ssh + 1 + 127) << 23);
+#pragma unroll
+            for (int m = 0; m < 8; ++m) {
+                const float f0 = __int_as_float((127 - ssh - kexp(2 * m)) << 23);
+                const float f1 = __int_as_float((127 - ssh - kexp(2 * m + 1)) << 23);
+                qs[m][0] = pack_h2(x[2 * m] * f0, x[2 * m + 16] * f0);
+                qs[m][1] = pack_h2(x[2 * m + 1] * f1, x[2 * m + 17] * f1);
+            }
+        }
+        float sum = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 32; ++k) sum += x[k];
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        qsum[0] = __shfl_sync(0xffffffffu, sum, 4 * (2 * c));       // head 2c
+        qsum[1] = __shfl_sync(0xffffffffu, sum, 4 * (2 * c + 1));   // head 2c+1
+    }
+
     // Raw V data of one 16-token sub-tile: tokens 2c, 2c+1, 2c+8, 2c+9 (code
     // bytes 8g..8g+7, syndrome word g/2) and the metadata of tokens g, g+8.
     //
@@ -557,11 +632,29 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap mkc, const __grid_constant
             }
         }
     };
-    for (int s = 0; s < kStages && s < ntiles; ++s) issue_next(s);
-
     Lane<G> L;
     L.g = lane >> 2;
     L.c = lane & 3;
+    // Query words of lane (g, c): dims 32c..32c+31 of query head g of the
+    // group (with the split columns, G <= 4, lanes g >= 4 repeat head g - 4,
+    // so that the softmax state of columns 4..7, the V sign products, is that
+    // of the head they belong to); zero for heads past the group.  The first
+    // segment's words are requested before the first stages, so that they do
+    // not queue behind the whole grid's first tiles.
+    auto load_q = [&](uint4 (&qw)[4], int64_t row) {
+        const int qh = (G <= 4) ? (L.g & 3) : L.g;
+        const int b_ = (int)(row / Hkv), h0_ = (int)(row % Hkv) * G;
+        const uint4 *src = reinterpret_cast<const uint4 *>(q + ((int64_t)b_ * Hq + h0_ + qh) * kD + 32 * L.c);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) qw[k] = qh < G ? __ldg(src + k) : make_uint4(0u, 0u, 0u, 0u);
+    };
+    {
+        uint4 qw[4];
+        load_q(qw, tbeg / tpr);
+        for (int s = 0; s < kStages && s < ntiles; ++s) issue_next(s);
+        L.set_query(qw, (flags & ECC_DECODE_ROTATE_Q) != 0);
+    }
+
     L.lane4 = (uint32_t)lane * 4u;
     L.sel_half = (L.g & 1) ? 0x7632u : 0x5410u;
     L.voff = 16u * (uint32_t)((L.g >> 1) ^ L.c) + 8u * (uint32_t)(L.g & 1);
@@ -582,88 +675,10 @@ decode_tma_kernel(const __grid_constant__ CUtensorMap mkc, const __grid_constant
         const int h0 = kvh * G;
         // first attended token of the sequence (left padding before it)
         const int t_start = start_dev ? __ldg(start_dev + b) : 0;
-        {
-            // lane (g, c) holds dims 32c..32c+31 of query head g of the group;
-            // with the split columns (G <= 4) lanes g >= 4 repeat head g - 4,
-            // so that the softmax state of columns 4..7 (the V sign products)
-            // is that of the head they belong to
-            float x[32];
-            const int qh = (G <= 4) ? (L.g & 3) : L.g;
-            if (qh < G) {
-                const uint4 *src = reinterpret_cast<const uint4 *>(q + ((int64_t)b * Hq + h0 + qh) * kD + 32 * L.c);
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const uint4 u = __ldg(src + k);
-                    const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-                    for (int m = 0; m < 4; ++m) {
-                        x[8 * k + 2 * m] = h_lo(wv[m]);
-                        x[8 * k + 2 * m + 1] = h_hi(wv[m]);
-                    }
-                }
-            } else {
-#pragma unroll
-                for (int k = 0; k < 32; ++k) x[k] = 0.0f;
-            }
-            if (flags & ECC_DECODE_ROTATE_Q) {  // q_rot = fp16(WHT(q)), like patch.py:106
-#pragma unroll
-                for (int s = 1; s < 32; s <<= 1)
-#pragma unroll
-                    for (int k = 0; k < 32; ++k)
-                        if ((k & s) == 0) {
-                            const float a = x[k], bb = x[k + s];
-                            x[k] = __fadd_rn(a, bb);
-                            x[k + s] = __fsub_rn(a, bb);
-                        }
-#pragma unroll
-                for (int s = 1; s <= 2; s <<= 1) {  // strides 32, 64: partner lane c ^ s
-                    const float sgn = (L.c & s) ? -1.0f : 1.0f;
-#pragma unroll
-                    for (int k = 0; k < 32; ++k) {
-                        const float p = __shfl_xor_sync(0xffffffffu, x[k], s);
-                        x[k] = __fmaf_rn(sgn, x[k], p);
-                    }
-                }
-#pragma unroll
-                for (int k = 0; k < 32; ++k) {
-                    const float v = x[k];
-                    const float q0 = __fmul_rn(v, kInvSqrt128);
-                    const float rem = __fmaf_rn(-q0, kSqrt128, v);
-                    x[k] = __half2float(__float2half_rn(__fmaf_rn(rem, kInvSqrt128, q0)));
-                }
-            }
-#pragma unroll
-            for (int m = 0; m < 8; ++m) {
-                L.qc[m][0] = pack_h2(x[4 * m], x[4 * m + 1]);
-                L.qc[m][1] = pack_h2(x[4 * m + 2], x[4 * m + 3]);
-            }
-            // sign-product operand: scale 2^-ssh keeps q * 2^(14 - ssh) < 2^15
-            // for the largest |q| of the group (q is fp16, the scalings are
-            // exact powers of two)
-            {
-                float qmax = 0.0f;
-#pragma unroll
-                for (int k = 0; k < 32; ++k) qmax = fmaxf(qmax, fabsf(x[k]));
-#pragma unroll
-                for (int off = 1; off < 32; off <<= 1) qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, off));
-                const int e2 = (qmax > 0.0f) ? ((__float_as_int(qmax) >> 23) & 0xff) - 127 : 0;
-                const int ssh = max(0, e2);
-                L.sgn2 = __int_as_float((ssh + 1 + 127) << 23);
-#pragma unroll
-                for (int m = 0; m < 8; ++m) {
-                    const float f0 = __int_as_float((127 - ssh - kexp(2 * m)) << 23);
-                    const float f1 = __int_as_float((127 - ssh - kexp(2 * m + 1)) << 23);
-                    L.qs[m][0] = pack_h2(x[2 * m] * f0, x[2 * m + 16] * f0);
-                    L.qs[m][1] = pack_h2(x[2 * m + 1] * f1, x[2 * m + 17] * f1);
-                }
-            }
-            float sum = 0.0f;
-#pragma unroll
-            for (int k = 0; k < 32; ++k) sum += x[k];
-            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-            L.qsum[0] = __shfl_sync(0xffffffffu, sum, 4 * (2 * L.c));       // head 2c
-            L.qsum[1] = __shfl_sync(0xffffffffu, sum, 4 * (2 * L.c + 1));   // head 2c+1
+        if (j > 0) {
+            uint4 qw[4];
+            load_q(qw, r);
+            L.set_query(qw, (flags & ECC_DECODE_ROTATE_Q) != 0);
         }
 #pragma unroll
         for (int i = 0; i < 8; ++i)
