@@ -15,10 +15,13 @@ Also measured in the same run: compress throughput on the compress benchmark
 
 N > 1 GPUs (torchrun): the same job split over the ranks (strong scaling):
 by kv head by default (rank r holds kv heads [8r/N, 8(r+1)/N) of every
-sequence; one NCCL all-gather of the fp16 outputs per step), or by sequence
-chunk with ``--shard seq`` (LSE combine of the ranks' partial records over
-peer memory or NCCL).  Rank 0 checks the final step's sharded output against
-a one-GPU decode of the same pools.
+sequence; one kernel per step merges the rank's partials and gathers the
+ranks' fp16 outputs over peer memory, or NCCL with ``--exchange nccl``), or by
+sequence chunk with ``--shard seq`` (LSE combine of the ranks' partial
+records over peer memory or NCCL).  With N > 1 the K timed steps are
+recorded once as a CUDA graph and replayed (``--graph off``: issued eagerly,
+which the host's issue time bounds at 8 GPUs).  Rank 0 checks the final
+step's sharded output against a one-GPU decode of the same pools.
 
 ``--impl reference`` times the reference algorithm's CPU implementation (the
 oracle port in oracle/, all host threads) on a bounded sample of the same
@@ -1017,10 +1020,13 @@ def main():
                          "lists of the prefill)")
     ap.add_argument("--long", choices=["kv", "seq"], default=None,
                     help="long-context decode (B16, 131072 tokens) sharded by kv head or by sequence chunk")
-    ap.add_argument("--graph", action="store_true",
-                    help="decode benchmark: the K timed steps recorded once as a CUDA graph and replayed; with "
+    ap.add_argument("--graph", choices=["auto", "on", "off"], default="auto",
+                    help="decode benchmark: the K timed steps recorded once as a CUDA graph and replayed "
+                         "(auto: with more than one GPU, where an eager step is bound by host issue time); with "
                          "--long: every step one CUDA-graph replay (device-side lengths)")
     args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    args.graph = args.graph == "on" or (args.graph == "auto" and world > 1 and not args.long)
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     if args.impl == "reference":
