@@ -55,7 +55,7 @@ COMPRESS_TOKENS = 131072
 # Decode: per (token, kv head), algorithmic 256 B.  Compress: per vector,
 # algorithmic 384 B; the output blocks of a launch partly stay in the 126 MB L2
 # when the launch ends, so DRAM writes are counted below 128 B per vector.
-DECODE_DRAM_BYTES_PER_UNIT = (1.074417e9 + 6.3168e6) / (B * HKV * 65541)
+DECODE_DRAM_BYTES_PER_UNIT = (1.074460e9 + 3.663104e6) / (B * HKV * 65541)
 COMPRESS_DRAM_BYTES_PER_VECTOR = (268.652032e6 + 97.288704e6) / (HKV * COMPRESS_TOKENS)
 
 
