@@ -917,7 +917,8 @@ extern "C" int ecc_decode_static(const void *q_f16, const void *k_blocks, const 
 // Record exchange over peer memory (lse_exchange_kernel above).
 // ---------------------------------------------------------------------------
 // CTAs of one exchange call: one per row up to kExchMaxGrid, and never more
-// than can be resident at once on the device.
+// than can be resident at once on the device (the smaller occupancy of the
+// two exchange kernels, which both use this grid).
 static std::mutex g_exch_mu;
 static int g_exch_per_sm[64];
 
@@ -929,11 +930,11 @@ extern "C" int ecc_exchange_grid(int64_t rows) {
     {
         std::lock_guard<std::mutex> lk(g_exch_mu);
         if (!g_exch_per_sm[dev]) {
-            int nb = 0;
-            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, lse_exchange_kernel, kD, 0) != cudaSuccess ||
-                nb < 1)
-                nb = 1;
-            g_exch_per_sm[dev] = nb;
+            int na = 0, nb = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&na, lse_exchange_kernel, kD, 0) != cudaSuccess)
+                na = 1;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, lse_gather_kernel, kD, 0) != cudaSuccess) nb = 1;
+            g_exch_per_sm[dev] = std::max(1, std::min(na, nb));
         }
         per_sm = g_exch_per_sm[dev];
     }
