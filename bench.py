@@ -909,7 +909,7 @@ def run_long(args):
         line = {
             "metric": "long-context ECC-INT4 decode attention: job HBM GB/s; decode tok/s", "value":
                 job_bytes * K / (total_ms / 1e3) / 1e9, "unit": "GB/s", "n_gpus": world, "steps": K, "warmup": W,
-            "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "strong", "dtype": "fp32",
+            "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "strong", "dtype": "fp16 MMA (split operands), fp32 accumulate",
             "data": "synthetic",
             "config": {"workload": f"long-context decode step: B{Bl} Hq{HQ}/Hkv{HKV} D{D}, {LONG_CTX}-token "
                                    f"compressed context per sequence, one layer, append + fused decode",
