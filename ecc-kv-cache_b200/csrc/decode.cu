@@ -193,17 +193,18 @@ decode_v1_kernel(const __half *__restrict__ q, const uint8_t *__restrict__ kb, c
 // LSE combine of n partials (m natural-log units, l, unnormalised o) of one
 // row by a 128-thread block, thread d = dim d: M = max over the non-empty
 // partials (l > 0; -inf if none), L and O relative to M.  Partial i is read
-// through src(i) = {m, l, o[d]}.  Partials go in batches of up to 32: every
-// thread loads its o of the whole batch at once and threads < 32 the batch's
+// through src(i) = {m, l, o[d]}.  Partials go in batches of up to 64: every
+// thread loads its o of the whole batch at once and threads < 64 the batch's
 // (m, l), the batch maximum comes from shared memory, and sums kept under an
 // earlier maximum are rescaled.  The loads of batch i + 1 are issued before
 // batch i is combined (two register sets), so a row of many partials costs
-// about one memory round trip, not one per batch.  With n <= 32 (every split
-// count of one device's default partition up to 32 per row) M is the global
-// maximum and the sums run in partial order.
+// about one memory round trip per two batches' worth of loads in flight.
+// With n <= 64 (every split count of one device's default partition up to 64
+// per row) M is the global maximum and the sums run in partial order.
 template <class Src>
 __device__ __forceinline__ void lse_combine(int n, int d, const Src &src, float &M, float &L, float &O) {
-    constexpr int kBatch = 32;
+    constexpr int kBatch = 64;
+    static_assert(kBatch <= kD, "one thread per (m, l) pair of a batch");
     __shared__ float s_m[kBatch], s_l[kBatch];
     M = -INFINITY;
     L = 0.0f;

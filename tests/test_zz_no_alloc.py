@@ -6,8 +6,8 @@ a latency-critical path that cannot take cudaMalloc's implicit
 synchronisation.  For them libeccb200.so keeps the decode's split partials in
 a fixed library-owned device array.  This test calls that entry point
 directly through the C ABI (ctypes) and checks it against the workspace-based
-ecc_decode on two calls in a row, with different inputs, so that the second
-call cannot pass on what the first left in the shared array.
+ecc_decode and the oracle on two calls in a row, with different inputs, so
+that the second call cannot pass on what the first left in the shared array.
 
 It lives in a file of its own that pytest collects last, so a run that stops
 at the first failure has already run every other test.
@@ -55,7 +55,10 @@ def _static_decode(lib, q, kp, vp, seq_len, flags, num_splits=0):
     return rc, out
 
 
-def test_static_decode_matches_workspace_decode_twice(lib, cuda_device):
+def test_static_decode_matches_workspace_decode_and_oracle_twice(lib, oracle, cuda_device):
+    """Two calls in a row with different inputs: each equals the
+    workspace-based decode within 2e-3 and the oracle within 2e-3 beyond
+    the fp16 rounding of the oracle's value (half an fp16 ulp)."""
     import custom_ecc_cuda as ops
     cases = [  # (B, hq, hkv, L, seq_len, flags, seed)
         (2, 32, 8, 4096, 4000, 3, 1),
@@ -71,6 +74,12 @@ def test_static_decode_matches_workspace_decode_twice(lib, cuda_device):
         torch.cuda.synchronize()
         err = (got.float() - ref.float()).abs().max().item()
         assert err <= TOL, err
+        want = oracle.decode(q.cpu().numpy(), kp.cpu().numpy(), vp.cpu().numpy(), hkv=hkv, seq_len=seq_len,
+                             rotate_q=bool(flags & 1), unrotate_out=bool(flags & 2)).astype(np.float32)
+        a = np.abs(want.astype(np.float16))
+        half_ulp = (np.nextafter(a, np.float16(np.inf)) - a).astype(np.float32) / 2
+        g = got.float().cpu().numpy().reshape(want.shape)
+        assert float((np.abs(g - want) - half_ulp).max()) <= TOL
 
 
 def test_static_decode_rejects_requests_beyond_the_array(lib, cuda_device):
