@@ -192,70 +192,99 @@ decode_v1_kernel(const __half *__restrict__ q, const uint8_t *__restrict__ kb, c
 
 // LSE combine of n partials (m natural-log units, l, unnormalised o) of one
 // row by a 128-thread block, thread d = dim d: M = max over the non-empty
-// partials (l > 0; -inf if none), L and O relative to M.  Partial i is read
-// through src(i) = {m, l, o[d]}.  Partials go in batches of up to 64: every
-// thread loads its o of the whole batch at once and threads < 64 the batch's
-// (m, l), the batch maximum comes from shared memory, and sums kept under an
-// earlier maximum are rescaled.  The loads of batch i + 1 are issued before
-// batch i is combined (two register sets), so a row of many partials costs
-// about one memory round trip per two batches' worth of loads in flight.
-// With n <= 64 (every split count of one device's default partition up to 64
-// per row) M is the global maximum and the sums run in partial order.
+// partials (l > 0; -inf if none), w_j = exp(m_j - M) (0 for empty
+// partials), L = sum_j l_j w_j, O = sum_j o_j[d] w_j.  Partial j is read
+// through src(j) = {m, l, o[d]}.
+//   1. M: thread t takes partials t, t + 128, ...; block maximum.
+//   2. Batches of 64 partials, whose o loads go out one batch ahead (two
+//      register sets): threads t < 64 put w of partial c0 + t in shared
+//      memory and add l w to their own running sum; every thread adds o w
+//      of the batch into four accumulators (partial j into j mod 4).
+//   3. O = (a0 + a1) + (a2 + a3); L = the 64 running sums reduced by the
+//      fixed tree of lse_block_sum64.
+// Every step has a fixed order, so the result does not depend on timing,
+// and the record merge of the peer exchange (lse_exchange_kernel) uses the
+// same helpers so that it equals this function bit for bit.
+constexpr int kLseBatch = 64;
+static_assert(kLseBatch <= kD, "one thread per partial of a batch");
+
+__device__ __forceinline__ float lse_weight(float m, float l, float M) {
+    return (l > 0.0f && M != -INFINITY) ? __expf(m - M) : 0.0f;
+}
+// o * w with the empty partials' o (possibly never written) left out
+__device__ __forceinline__ float lse_term(float o, float w, float acc) { return w != 0.0f ? fmaf(o, w, acc) : acc; }
+
+// Maximum of v over the block's 128 threads (every thread gets it).
+__device__ __forceinline__ float lse_block_max(float v, float *red) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    const float r = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    __syncthreads();  // red is reused
+    return r;
+}
+// Sum of v over threads 0..63 (the others' v ignored), in one fixed order:
+// a shfl_down tree within each of warps 0 and 1, then warp 0 + warp 1.
+__device__ __forceinline__ float lse_block_sum64(float v, float *red) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_down_sync(0xffffffffu, v, off);
+    if (threadIdx.x == 0 || threadIdx.x == 32) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    const float r = red[0] + red[1];
+    __syncthreads();  // red is reused
+    return r;
+}
+
 template <class Src>
 __device__ __forceinline__ void lse_combine(int n, int d, const Src &src, float &M, float &L, float &O) {
-    constexpr int kBatch = 64;
-    static_assert(kBatch <= kD, "one thread per (m, l) pair of a batch");
-    __shared__ float s_m[kBatch], s_l[kBatch];
-    M = -INFINITY;
-    L = 0.0f;
-    O = 0.0f;
-    float ov[kBatch], mv = 0.0f, lv = 0.0f;
-    auto fetch = [&](int c0, float (&o)[kBatch], float &m, float &l) {
-        const int cn = min(kBatch, n - c0);
+    __shared__ float s_w[kLseBatch];
+    __shared__ float s_red[kD / 32];
+    float mx = -INFINITY;
+    for (int j = d; j < n; j += kD)
+        if (src.l(j) > 0.0f) mx = fmaxf(mx, src.m(j));
+    M = lse_block_max(mx, s_red);
+
+    float ov[kLseBatch], mv = 0.0f, lv = 0.0f;
+    auto fetch = [&](int c0, float (&o)[kLseBatch], float &m, float &l) {
+        const int cn = min(kLseBatch, n - c0);
 #pragma unroll
-        for (int j = 0; j < kBatch; ++j) o[j] = (j < cn) ? src.o(c0 + j, d) : 0.0f;
+        for (int j = 0; j < kLseBatch; ++j) o[j] = (j < cn) ? src.o(c0 + j, d) : 0.0f;
         if (d < cn) {
             m = src.m(c0 + d);
             l = src.l(c0 + d);
         }
     };
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f, lw = 0.0f;
     if (n > 0) fetch(0, ov, mv, lv);
-    for (int c0 = 0; c0 < n; c0 += kBatch) {
-        const int cn = min(kBatch, n - c0);
-        if (d < cn) {
-            s_m[d] = mv;
-            s_l[d] = lv;
+    for (int c0 = 0; c0 < n; c0 += kLseBatch) {
+        const int cn = min(kLseBatch, n - c0);
+        if (d < kLseBatch) {
+            const float w = d < cn ? lse_weight(mv, lv, M) : 0.0f;
+            s_w[d] = w;
+            if (d < cn) lw = fmaf(lv, w, lw);
         }
-        float nv[kBatch];
+        float nv[kLseBatch];
         float nm = 0.0f, nl = 0.0f;
-        if (c0 + kBatch < n) fetch(c0 + kBatch, nv, nm, nl);  // block-uniform
+        if (c0 + kLseBatch < n) fetch(c0 + kLseBatch, nv, nm, nl);  // block-uniform
         __syncthreads();
-        float bm = M;
-        for (int j = 0; j < cn; ++j)
-            if (s_l[j] > 0.0f) bm = fmaxf(bm, s_m[j]);
-        if (bm != M) {  // block-uniform
-            const float r = (M == -INFINITY) ? 0.0f : __expf(M - bm);
-            L *= r;
-            O *= r;
-            M = bm;
-        }
-        if (M != -INFINITY) {
 #pragma unroll
-            for (int j = 0; j < kBatch; ++j)
-                if (j < cn && s_l[j] > 0.0f) {
-                    const float e = __expf(s_m[j] - M);
-                    L = fmaf(s_l[j], e, L);
-                    O = fmaf(ov[j], e, O);
-                }
+        for (int j = 0; j < kLseBatch; j += 4) {
+            a0 = lse_term(ov[j], s_w[j], a0);
+            a1 = lse_term(ov[j + 1], s_w[j + 1], a1);
+            a2 = lse_term(ov[j + 2], s_w[j + 2], a2);
+            a3 = lse_term(ov[j + 3], s_w[j + 3], a3);
         }
-        __syncthreads();  // the batch's (m, l) slots are refilled next
-        if (c0 + kBatch < n) {
+        __syncthreads();  // s_w is refilled next
+        if (c0 + kLseBatch < n) {
 #pragma unroll
-            for (int j = 0; j < kBatch; ++j) ov[j] = nv[j];
+            for (int j = 0; j < kLseBatch; ++j) ov[j] = nv[j];
             mv = nm;
             lv = nl;
         }
     }
+    O = (a0 + a1) + (a2 + a3);
+    L = lse_block_sum64(lw, s_red);
 }
 
 // Split partials of one row: m, l [row][n], o [row][n][128].
@@ -414,6 +443,7 @@ lse_exchange_kernel(const float *__restrict__ pm, const float *__restrict__ pl, 
                     long long wait_cycles, __half *__restrict__ out, int flags) {
     __shared__ float sh[kD];
     __shared__ float s_m[kExchMaxRanks], s_l[kExchMaxRanks];
+    __shared__ float s_w[kLseBatch], s_red[kD / 32];
     const int d = threadIdx.x;
     pdl_wait();  // the partials of the kernel before
     const uint32_t epoch = call_epoch(epoch_arg, estate);
@@ -453,25 +483,22 @@ lse_exchange_kernel(const float *__restrict__ pm, const float *__restrict__ pl, 
             if (q < W) ov[q] = await_word(mine + ((int64_t)q * rows + r) * kRec + 2 + d, w[q], epoch, t0,
                                           wait_cycles, &ok);
         __syncthreads();
-        // the single-batch arithmetic of lse_combine over the W records
-        float M = -INFINITY, L = 0.0f, O = 0.0f, bm = -INFINITY;
-        for (int j = 0; j < W; ++j)
-            if (s_l[j] > 0.0f) bm = fmaxf(bm, s_m[j]);
-        if (bm != M) {
-            L *= 0.0f;
-            O *= 0.0f;
-            M = bm;
+        // lse_combine's arithmetic over the W records (bit for bit): the
+        // same maximum, weights, accumulator assignment and sum tree
+        const float M = lse_block_max((d < W && s_l[d] > 0.0f) ? s_m[d] : -INFINITY, s_red);
+        float lw = 0.0f;
+        if (d < kLseBatch) {
+            const float wt = d < W ? lse_weight(s_m[d], s_l[d], M) : 0.0f;
+            s_w[d] = wt;
+            if (d < W) lw = fmaf(s_l[d], wt, lw);
         }
-        if (M != -INFINITY) {
+        __syncthreads();
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-            for (int j = 0; j < kExchMaxRanks; ++j)
-                if (j < W && s_l[j] > 0.0f) {
-                    const float e = __expf(s_m[j] - M);
-                    L = fmaf(s_l[j], e, L);
-                    O = fmaf(ov[j], e, O);
-                }
-        }
-        __syncthreads();  // s_m, s_l are refilled for the next row
+        for (int j = 0; j < kExchMaxRanks; ++j)
+            if (j < W) acc[j & 3] = lse_term(ov[j], s_w[j], acc[j & 3]);
+        const float O = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+        const float L = lse_block_sum64(lw, s_red);  // its barriers also end this row's reads of s_m, s_l, s_w
         write_out(L, O, out, r, d, flags, sh);
     }
     advance_epoch(estate);
