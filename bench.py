@@ -676,8 +676,7 @@ def run_ours(args):
         torch.cuda.synchronize()
         if ops.device_status() != 0:  # a bounded wait gave up: the numbers are void
             raise RuntimeError(f"rank {rank}: device status {ops.device_status()}")
-        if shard._peer is not None:
-            shard._peer.close()
+        shard.close()
         dist.barrier()
         dist.destroy_process_group()
 

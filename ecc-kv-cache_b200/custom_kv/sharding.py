@@ -190,6 +190,15 @@ class ShardedDecode:
         self.rank = dist.get_rank(self.group)
         self._bufs: dict = {}
 
+    def close(self) -> None:
+        """Release the peer-memory exchange (its buffers and the peers'
+        mappings) and check the device status it reports.  Collective: every
+        rank calls it, before destroy_process_group.  A no-op without a peer
+        exchange; the next p2p step makes a new one."""
+        if self._peer is not None:
+            peer, self._peer = self._peer, None
+            peer.close()
+
     def _ensure_peer(self, rows: int, device: torch.device) -> None:
         if self._peer is None or self._peer.rows != rows:
             if self._peer is not None:

@@ -204,8 +204,8 @@ def _two_gpu_worker(rank, world, port):
             assert torch.equal(b[:, rank * hq_l:(rank + 1) * hq_l], own)
         torch.cuda.synchronize()
         assert ops.device_status() == 0
-        p2p._peer.close()
-        kp2p._peer.close()
+        p2p.close()
+        kp2p.close()
     finally:
         dist.destroy_process_group()
 
