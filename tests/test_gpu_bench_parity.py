@@ -3,7 +3,8 @@ heads over 8 kv heads, 65536-token context growing by one token per step),
 against the oracle -- not kernel against kernel.
 
 Tolerance: |out - ref| <= 2e-3 + ulp_fp16(ref)/2 against the oracle's fp32
-output (the 2e-3 of the north star beyond the fp16 rounding of the value).
+output (the decode's 2e-3 output tolerance beyond the fp16 rounding of the
+value).
 How many elements also pass a plain 2e-3 is printed."""
 import numpy as np
 import pytest
