@@ -698,8 +698,8 @@ def decode_config(world: int, mode: str, rb: int = BLOCK) -> dict:
 
 
 def cpu_parity(pools_host, seq_len, comp_sample):
-    """Oracle checks of the benchmarked data (part of the CPU leg; the oracle
-    is the checker here, nothing is timed): the final timed decode step's
+    """Oracle checks of the benchmarked data (part of the CPU leg; nothing
+    is timed here): the final timed decode step's
     output for two batch rows (all 32 query heads) against the oracle's
     decode of the same pools, and a sample of the compress benchmark's input
     against the oracle's blocks (bit for bit) with the count of elements

@@ -4,7 +4,8 @@
  * TEST INFRASTRUCTURE ONLY.  Nothing in the product (the CUDA library, the
  * Python packages) links, loads or calls this file.  It is used by tests/,
  * by __graft_entry__.smoke() and by bench.py's CPU-baseline leg, always as
- * the checker, never as the thing measured or shipped.
+ * the reference results the CUDA path is compared with, never as the thing
+ * measured or shipped.
  *
  * It restates, in plain C, the reference's CPU algorithm for the two hot
  * paths of j-arndt/ecc-kv-cache:

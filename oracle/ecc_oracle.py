@@ -2,7 +2,8 @@
 
 Nothing in the product imports this module.  It is used by ``tests/``,
 ``__graft_entry__.smoke()`` and the CPU-baseline leg of ``bench.py``, always
-as the checker of the CUDA path, never as the thing measured or shipped.
+as the reference results the CUDA path is compared with, never as the thing
+measured or shipped.
 
 Two independent restatements of the reference's CPU algorithm live here:
 
