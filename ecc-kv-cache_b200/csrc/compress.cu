@@ -47,8 +47,9 @@ constexpr float kBand = 4e-6f;    // exact-recompute band around each threshold 
 // reference's RN(d / scale) adds <= 1.2e-7, its flip point lies within 1e-7
 // of the exact midpoint and thr within 1.2e-7 of it: a decision with
 // |w| >= 5.2e-7 is the reference's.  A CPU stress of 4 M near-threshold
-// quotients sees wrong decisions only for |w| < 2.8e-7.
-constexpr float kBandFast = 1.5e-6f;
+// quotients sees wrong decisions only for |w| < 2.8e-7.  The band is 1.5x
+// the bound.
+constexpr float kBandFast = 8e-7f;
 constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: fma(u, 8, kMagic + 96) rounds 8u+96 to an integer
 constexpr int kCompressWarps = 8;
 constexpr int kVecPerWarp = 8;

@@ -9,7 +9,8 @@ import pytest
 import workloads
 
 CELLS, MAGIC, BAND = 192, np.float32(12582912.0), np.float32(4e-6)
-BAND_FAST = np.float32(1.5e-6)  # the packed fast pass's band (compress.cu kBandFast)
+BAND_FAST = np.float32(8e-7)  # the packed fast pass's band (compress.cu kBandFast)
+BAND_BOUND = 5.2e-7  # |w| beyond which a fast-pass decision is the reference's (error budget in compress.cu)
 
 
 def test_division_by_sqrt128_sampled(oracle):
@@ -114,8 +115,9 @@ def test_fast_pass_quantiser_equals_argmin(oracle):
 def test_fast_pass_band_near_thresholds(oracle):
     """Quotients placed within 3e-6 of every decision threshold over scales
     1e-3..1e3: no fast-pass decision outside the band differs from the
-    reference's RN(d / scale) argmin, and the closest wrong decision of an
-    unbanded rule stays far inside the band."""
+    reference's RN(d / scale) argmin, and every wrong decision of an
+    unbanded rule lies inside the error-budget bound, which the band
+    exceeds by 1.5x."""
     C = oracle.LM_CENTROIDS.astype(np.float32)
     tab, m, _ = _table(C)
     rng = np.random.default_rng(5)
@@ -128,8 +130,9 @@ def test_fast_pass_band_near_thresholds(oracle):
     rs = (np.float64(1.0) / scale.astype(np.float64)).astype(np.float32)
     w = (d.astype(np.float64) * rs.astype(np.float64) - m[j].astype(np.float64)).astype(np.float32)
     wrong = (j + (w >= 0)) != q_ref
+    assert BAND_FAST >= 1.5 * BAND_BOUND
     assert not np.any(wrong & (np.abs(w) >= BAND_FAST))
-    assert np.abs(w[wrong]).max() < BAND_FAST / 4
+    assert np.abs(w[wrong]).max() < BAND_BOUND
 
 
 def _lanes_tsum(V):
