@@ -119,6 +119,8 @@ def _worker(rank, world, port, mode, B, hkv, hq, L, seed):
         ulp = np.spacing(np.abs(ref16).astype(np.float16)).astype(np.float32)
         err = np.abs(out.float().numpy().reshape(B, hq, D) - ref16)
         assert np.all(err <= TOL + ulp / 2), f"rank {rank} {mode}: max err {err.max()}"
+        shard.close()  # collective release; without a peer-memory exchange a no-op
+        shard.close()
     finally:
         dist.destroy_process_group()
 
